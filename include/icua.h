@@ -1,0 +1,190 @@
+/*
+ * icua.h - C ABI of the B200 (sm_100a) engine for the Qwen3VLTextModel token loop.
+ *
+ * This header is the drop-in boundary: it replaces the Metal-typed surface of the reference's
+ * `public final class Engine` (Sources/Engine/Engine.swift) and is the counterpart of the
+ * reference's C target `Sources/CShim` (Package.swift:14).  Plain pointers, sizes and status
+ * codes only; no CUDA or torch types appear in any signature.
+ *
+ * Errors: every call returns an icua_status; on failure a message is available from
+ * icua_last_error() (per engine) or icua_global_error() (calls without an engine).  This
+ * replaces the reference's `throw EngineError(String)` (Sources/Engine/ModelFile.swift:158-161).
+ * Threading: one engine per thread; calls on one engine are not reentrant (the reference engine
+ * is single-queue and synchronous, Engine.swift:65, 790).
+ */
+#ifndef ICUA_H
+#define ICUA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    ICUA_OK = 0,
+    ICUA_ERR_INVALID = 1,     /* bad argument (null pointer, size, id, token out of range) */
+    ICUA_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+    ICUA_ERR_OOM = 3,         /* device or host allocation failed */
+    ICUA_ERR_IO = 4,          /* model file could not be opened, mapped or read */
+    ICUA_ERR_FORMAT = 5,      /* model file header or tensor table mismatch */
+    ICUA_ERR_STATE = 6,       /* call out of order (weights missing, engine failed) */
+    ICUA_ERR_CAPACITY = 7,    /* context, pass, steps or session capacity exceeded */
+    ICUA_ERR_UNSUPPORTED = 8, /* weight format not implemented by the kernels */
+    ICUA_ERR_TIMEOUT = 9      /* a bounded device-side wait gave up (kernel error flag set) */
+} icua_status;
+
+/* Weight formats.  0..2 are the reference WeightFormat raw values (ModelFile.swift:6-9):
+ * f16, q8 (symmetric int8, groups of 32, fp16 scale), q4 (affine int4, groups of 64, fp16
+ * scale+bias).  3 is the BASELINE format: decoder matrices symmetric int4 in groups of 32 with
+ * an fp16 scale (offset-binary nibbles, u = q + 8) and the tied embedding / lm_head in q8. */
+enum { ICUA_FMT_F16 = 0, ICUA_FMT_Q8 = 1, ICUA_FMT_Q4 = 2, ICUA_FMT_Q4S = 3 };
+
+/* KV cache element type.  The reference stores fp16 (Shaders.swift:776-783). */
+enum { ICUA_KV_F16 = 0, ICUA_KV_BF16 = 1 };
+
+/* Tensor ids: the reference TensorID numbering (ModelFile.swift:62-111). */
+enum {
+    ICUA_TID_EMBED = 315,
+    ICUA_TID_EMBED_SB = 316,
+    ICUA_TID_FINAL_NORM = 317,
+    ICUA_TID_LAYER_BASE = 318,
+    ICUA_TID_PER_LAYER = 14,
+    ICUA_SLOT_ATTN_NORM = 0, ICUA_SLOT_WQKV = 1, ICUA_SLOT_WQKV_SB = 2, ICUA_SLOT_Q_NORM = 3,
+    ICUA_SLOT_K_NORM = 4, ICUA_SLOT_WO = 5, ICUA_SLOT_WO_SB = 6, ICUA_SLOT_MLP_NORM = 7,
+    ICUA_SLOT_WGU = 8, ICUA_SLOT_WGU_SB = 9, ICUA_SLOT_WD = 10, ICUA_SLOT_WD_SB = 11,
+    ICUA_TENSOR_COUNT = 710
+};
+
+typedef struct icua_engine icua_engine;
+
+/* Engine configuration; mirrors Engine.init(modelPath:maxContext:maxPass:maxSteps:...)
+ * (Engine.swift:54-55).  n_layers and vocab are the model's (28, 151936); smaller values are
+ * accepted for tests. */
+typedef struct {
+    int32_t device;         /* CUDA device ordinal */
+    int32_t n_layers;       /* decoder layers (28) */
+    int32_t vocab;          /* vocabulary rows of the tied embedding (151936) */
+    int32_t max_context;    /* KV positions per session (reference default 2048) */
+    int32_t max_pass;       /* max prompt tokens per prefill call (reference default 512) */
+    int32_t max_steps;      /* max generated tokens per call (reference default 256) */
+    int32_t max_sessions;   /* KV caches held (1 for the reference's single session) */
+    int32_t format;         /* ICUA_FMT_* */
+    int32_t kv_dtype;       /* ICUA_KV_* */
+    int32_t steps_per_graph;/* decode steps captured per CUDA graph launch (>=1) */
+} icua_config;
+
+/* Mirrors Engine.Timing (Engine.swift:44-51); times are device times from CUDA events. */
+typedef struct {
+    double vision_ms;       /* always 0: the vision encoder is outside this engine */
+    double prefill_ms;
+    double decode_ms;
+    double total_ms;        /* host wall time of the call */
+    int32_t prefill_tokens;
+    int32_t generated_tokens;
+} icua_timing;
+
+/* Optional visual inputs for a prompt (replace the ViT outputs poolerBuf / deepstackBufs,
+ * Engine.swift:20-21).  Host fp32 arrays, row-major [n_vis, 2048]; deepstack[i] may be NULL. */
+typedef struct {
+    const float* pooler;
+    const float* deepstack[3];
+    int32_t n_vis;
+    int32_t llm_h, llm_w;   /* merged grid; n_vis == llm_h * llm_w */
+} icua_visual;
+
+/* ---- lifecycle -------------------------------------------------------------------------- */
+void icua_default_config(icua_config* cfg);
+icua_status icua_engine_create(const icua_config* cfg, icua_engine** out);
+void icua_engine_destroy(icua_engine* eng);
+const char* icua_last_error(const icua_engine* eng);
+const char* icua_global_error(void);
+
+/* Loads an .icua model file (ModelFile.swift:113-156 layout: "ICU1", version 1, format,
+ * tensor count, (offset,size) table, 256-byte aligned tensors).  Replaces the mmap + MTLBuffer
+ * wrap of Engine.init (Engine.swift:62-77). */
+icua_status icua_engine_load_file(icua_engine* eng, const char* path);
+
+/* Sets one tensor from host bytes laid out as in the .icua file for that tensor id (row-major
+ * codes / packed nibbles, and the SB tensor with the scales).  Matrices are repacked and
+ * uploaded once both the codes and the SB tensor of a matrix are present. */
+icua_status icua_engine_set_tensor(icua_engine* eng, int32_t tensor_id, const void* data, uint64_t bytes);
+
+/* Returns ICUA_OK when every tensor the kernels need is resident on the device. */
+icua_status icua_engine_ready(icua_engine* eng);
+
+/* ---- the token loop (Engine.generateVision without the ViT, Engine.swift:696-827) ---------- */
+/* eos tokens (Engine.swift:12) and whether generation stops on them (reference: yes). */
+icua_status icua_set_eos(icua_engine* eng, int32_t eos0, int32_t eos1, int32_t stop_on_eos);
+
+/* Prompt pass for `session`: appends tokens[0..n) at the session's current position (0 after a
+ * reset), runs all layers and produces the first generated token.  `visual` may be NULL; when
+ * given, IMAGE_PAD (151655) rows take pooler rows, DeepStack rows are added after layers 0..2
+ * and positions follow the 3D M-RoPE layout (Engine.swift:254-298).  write_logits copies the
+ * first-token logits to an internal buffer readable with icua_get_logits. */
+icua_status icua_prefill(icua_engine* eng, int32_t session, const int32_t* tokens, int32_t n,
+                         const icua_visual* visual, int32_t write_logits, int32_t* first_token);
+
+/* Greedy decode of up to `max_new` tokens after a prefill; out_tokens has room for max_new.
+ * Stops early on EOS when enabled.  *n_out receives the count (EOS not included, as
+ * Engine.swift:808-816). */
+icua_status icua_decode(icua_engine* eng, int32_t session, int32_t max_new, int32_t* out_tokens,
+                        int32_t* n_out);
+
+/* One decode step driven from the host: the step input token is copied from host memory and the
+ * generated token is copied back (used by callers that interleave their own logic per token).
+ * The step's logits are kept for icua_get_logits. */
+icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token, int32_t* out_token);
+
+/* Whole call: reset session, prefill, decode; returns tokens like generateVision. */
+icua_status icua_generate(icua_engine* eng, int32_t session, const int32_t* tokens, int32_t n,
+                          const icua_visual* visual, int32_t max_new, int32_t write_first_logits,
+                          int32_t* out_tokens, int32_t* n_out);
+
+/* Resets a session to position 0 (empty KV). */
+icua_status icua_reset_session(icua_engine* eng, int32_t session);
+
+/* Fills a session's KV cache with given values (BASELINE config 2 injection): k and v are host
+ * fp32 [n_layers][n_pos][8][128]; they are rounded to the cache type.  Position becomes n_pos. */
+icua_status icua_inject_kv(icua_engine* eng, int32_t session, const float* k, const float* v, int32_t n_pos);
+
+/* Same as icua_inject_kv but draws the values on the device from N(0,1) with a counter-based
+ * generator (seeded), for long contexts where a host array would be large. */
+icua_status icua_inject_kv_random(icua_engine* eng, int32_t session, int32_t n_pos, uint64_t seed);
+
+/* Logits of the last step that was asked to write them (fp32 [vocab]). */
+icua_status icua_get_logits(icua_engine* eng, float* host_out);
+/* Writes logits at every decode step into a host array [max_new][vocab] on the next
+ * icua_decode call (parity runs); pass NULL to switch off. */
+icua_status icua_capture_step_logits(icua_engine* eng, float* host_out, int32_t capacity_steps);
+
+icua_status icua_get_timing(icua_engine* eng, icua_timing* out);
+icua_status icua_session_position(icua_engine* eng, int32_t session, int32_t* pos);
+
+/* ---- kernel-level entry points (device pointers; used by the microbench and the tests) -------- */
+/* Packed device size of an [n_rows, k] matrix in format fmt (ICUA_FMT_Q4S or ICUA_FMT_Q8). */
+uint64_t icua_packed_bytes(int32_t fmt, int32_t n_rows, int32_t k);
+/* Repacks reference-layout host codes + scales into the device tile layout (host to host). */
+icua_status icua_pack_matrix(int32_t fmt, int32_t n_rows, int32_t k, const void* codes,
+                             const uint16_t* scales, void* packed_out);
+/* y[n_rows] = W x on the device; x is fp32 [k] (x_dtype 0) or bf16 [k] (x_dtype 1).
+ * scratch_dev must hold icua_gemv_scratch_bytes(); stream is a cudaStream_t or NULL. */
+uint64_t icua_gemv_scratch_bytes(int32_t fmt, int32_t n_rows, int32_t k);
+icua_status icua_gemv(int32_t fmt, int32_t n_rows, int32_t k, const void* packed_dev,
+                      const void* x_dev, int32_t x_dtype, float* y_dev, void* scratch_dev,
+                      void* stream);
+/* Bit-exact dequantization of a packed device matrix to fp32 row-major [n_rows, k]. */
+icua_status icua_dequant(int32_t fmt, int32_t n_rows, int32_t k, const void* packed_dev, float* out_dev,
+                         void* stream);
+
+/* ---- host quantizers (reference Converter, Convert.swift:208-320) --------------------------- */
+/* q8: codes int8 [rows, cols], scales fp16 bits [rows, cols/32] (Convert.swift:215-241). */
+icua_status icua_quantize_q8(const float* w, int32_t rows, int32_t cols, int8_t* codes, uint16_t* scales);
+/* q4s: packed nibbles [rows, cols/2] (u = q + 8, even index low), scales [rows, cols/32]. */
+icua_status icua_quantize_q4s(const float* w, int32_t rows, int32_t cols, uint8_t* packed, uint16_t* scales);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ICUA_H */

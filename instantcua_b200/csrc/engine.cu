@@ -1,0 +1,1081 @@
+// Engine host code and C ABI (include/icua.h): weights, KV caches, device loop state, CUDA graphs
+// of PDL-chained kernels, prefill / decode drivers.
+//
+// Counterpart of the reference's Swift Engine (Sources/Engine/Engine.swift): init (54-185),
+// prepareMRoPE (254-298), encodeLLMLayer / encodeLMHead / encodeCommit / encodePrefill /
+// encodeDecodeStep (476-681) and generateVision's token loop (696-827).  Where the reference
+// encodes 142 dispatches per token into a Metal command buffer and batches 8 steps per submit,
+// this engine captures `steps_per_graph` decode steps into one CUDA graph whose kernels are
+// chained with programmatic dependent launch, so each kernel streams its weights while the
+// previous one finishes.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/icua.h"
+#include "attn_decode.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "misc.cuh"
+
+namespace icua_host {
+uint16_t f32_to_f16_bits(float f);
+float f16_bits_to_f32(uint16_t h);
+void pack_q4s(int n_rows, int k, const uint8_t* packed, const uint16_t* scales, const int* row_map, uint8_t* out);
+void pack_q8(int n_rows, int k, const int8_t* codes, const uint16_t* scales, const int* row_map, uint8_t* out);
+}  // namespace icua_host
+
+using namespace icua;
+
+namespace {
+
+thread_local std::string g_error;
+
+struct Matrix {
+    uint8_t* dev = nullptr;
+    int fmt = 0, n_rows = 0, k = 0;
+    long long n_units = 0;
+    int slot_units = 1, n_slots = 1;
+    size_t smem = 0;
+};
+
+struct Layer {
+    Matrix qkv, o, gu, d;
+    float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *mlp_norm = nullptr;
+};
+
+struct Session {
+    DevState* st = nullptr;       // device
+    int* prompt = nullptr;        // device [max_pass]
+    int* out_tokens = nullptr;    // device [max_steps + slack]
+    float2* rope = nullptr;       // device [max_ctx][64]
+    void* kc = nullptr;           // device [L][NKV][max_ctx][HD]
+    void* vc = nullptr;
+    // host mirror
+    int pos = 0;
+    int step = 0;
+    int done = 0;
+    int rope_delta = 0;
+    cudaGraphExec_t g_prefill_tok = nullptr, g_step1 = nullptr, g_stepn = nullptr;
+};
+
+}  // namespace
+
+struct icua_engine {
+    icua_config cfg{};
+    int n_sm = 0;
+    int n_workers = 0;
+    int att_split = 1;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    bool failed = false;
+    bool uploaded = false;
+    std::map<int, std::vector<uint8_t>> staged;
+    std::vector<Layer> layers;
+    Matrix embed;
+    float* final_norm = nullptr;
+    // activations
+    float *x = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr;
+    float* pooler = nullptr;
+    float* deepstack[3] = {nullptr, nullptr, nullptr};
+    float* step_logits = nullptr;
+    float* step_logits_host = nullptr;
+    int step_logits_cap = 0;
+    // scratch
+    float* partials = nullptr;
+    unsigned* tile_cnt = nullptr;
+    float* att_part = nullptr;
+    unsigned* att_cnt = nullptr;
+    float* cta_best_v = nullptr;
+    int* cta_best_i = nullptr;
+    unsigned* cta_done = nullptr;
+    std::vector<Session> sessions;
+    std::vector<void*> allocations;
+    int eos0 = 151645, eos1 = 151643, stop_on_eos = 1;
+    icua_timing timing{};
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    float inv_freq[64];
+};
+
+namespace {
+
+icua_status fail(icua_engine* e, icua_status s, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (e) e->err = buf;
+    g_error = buf;
+    return s;
+}
+
+#define CK(call)                                                                                   \
+    do {                                                                                           \
+        cudaError_t _e = (call);                                                                   \
+        if (_e != cudaSuccess) return fail(eng, ICUA_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(_e)); \
+    } while (0)
+
+icua_status dalloc(icua_engine* eng, void** p, size_t bytes) {
+    cudaError_t e = cudaMalloc(p, bytes < 16 ? 16 : bytes);
+    if (e != cudaSuccess) return fail(eng, ICUA_ERR_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    eng->allocations.push_back(*p);
+    return ICUA_OK;
+}
+
+template <typename T>
+icua_status dalloc_t(icua_engine* eng, T** p, size_t count) {
+    return dalloc(eng, reinterpret_cast<void**>(p), count * sizeof(T));
+}
+
+int kv_elem_bytes(const icua_engine* e) { return 2; }
+
+void ring_geometry(int fmt, long long n_units, int n_workers, int& su, int& ns) {
+    const int ub = unit_bytes(fmt);
+    const long long R = (n_units + n_workers - 1) / n_workers;
+    if (R * ub <= 16384) {
+        ns = (int)std::min<long long>(4, std::max<long long>(R, 1));
+        su = (int)((R + ns - 1) / ns);
+        if (su < 1) su = 1;
+    } else {
+        su = std::max(1, 4096 / ub);
+        ns = 3;
+    }
+}
+
+void setup_matrix(Matrix& m, int fmt, int n_rows, int k, int n_workers) {
+    m.fmt = fmt;
+    m.n_rows = n_rows;
+    m.k = k;
+    m.n_units = (long long)(n_rows / 16) * (k / 64);
+    ring_geometry(fmt, m.n_units, n_workers, m.slot_units, m.n_slots);
+    GemvSmem L{k, m.n_slots, m.slot_units, unit_bytes(fmt)};
+    m.smem = (size_t)L.total();
+}
+
+template <typename Kern, typename P>
+cudaError_t launch(Kern kernel, int grid, int block, size_t smem, cudaStream_t s, const P& params, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, params);
+}
+
+template <int FMT, int EPI>
+cudaError_t launch_gemv(icua_engine* e, const Matrix& m, const GemvParams& p, cudaStream_t s) {
+    return launch(gemv_kernel<FMT, EPI>, e->n_sm, 256, m.smem, s, p, true);
+}
+
+bool g_attrs_set[16] = {false};
+
+cudaError_t set_smem_attrs() {
+    static bool done = false;
+    if (done) return cudaSuccess;
+    const int big = 220 * 1024;
+    cudaError_t e;
+#define SETA(K)                                                                     \
+    e = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, big); \
+    if (e != cudaSuccess) return e;
+    SETA((gemv_kernel<FMT_Q4S, EPI_STORE>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_RESID>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_SWIGLU>));
+    SETA((gemv_kernel<FMT_Q8, EPI_LOGITS>));
+    SETA((gemv_kernel<FMT_Q8, EPI_STORE>));
+    SETA((attn_decode_kernel<__half>));
+    SETA((attn_decode_kernel<__nv_bfloat16>));
+#undef SETA
+    done = true;
+    return cudaSuccess;
+}
+
+GemvParams base_params(icua_engine* e, const Matrix& m) {
+    GemvParams p{};
+    p.w = m.dev;
+    p.n_units = m.n_units;
+    p.n_rows = m.n_rows;
+    p.k = m.k;
+    p.upt = m.k / 64;
+    p.slot_units = m.slot_units;
+    p.n_slots = m.n_slots;
+    p.partials = e->partials;
+    p.tile_cnt = e->tile_cnt;
+    return p;
+}
+
+// ---- one decode / prefill step ------------------------------------------------------------------
+cudaError_t record_layers(icua_engine* e, Session& S) {
+    cudaError_t err;
+    const int L = e->cfg.n_layers;
+    for (int l = 0; l < L; ++l) {
+        Layer& ly = e->layers[l];
+        // 1. RMSNorm + QKV projection (layer 0 embeds the input row first)
+        GemvParams p = base_params(e, ly.qkv);
+        p.in_mode = (l == 0) ? IN_EMBED : IN_F32;
+        p.x = e->x;
+        p.norm_w = ly.attn_norm;
+        p.embed = e->embed.dev;
+        p.prompt = S.prompt;
+        p.pooler = e->pooler;
+        p.x_resid = e->x;
+        p.out = e->qkv;
+        p.st = S.st;
+        if ((err = launch_gemv<FMT_Q4S, EPI_STORE>(e, ly.qkv, p, e->stream)) != cudaSuccess) return err;
+        // 2. QK norm + RoPE + KV append + split-K attention
+        const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
+        if (e->cfg.kv_dtype == ICUA_KV_BF16) {
+            AttnParams<__nv_bfloat16> a{};
+            a.qkv = e->qkv;
+            a.q_norm = ly.q_norm;
+            a.k_norm = ly.k_norm;
+            a.rope = S.rope;
+            a.kc = reinterpret_cast<__nv_bfloat16*>(S.kc) + kv_layer * l;
+            a.vc = reinterpret_cast<__nv_bfloat16*>(S.vc) + kv_layer * l;
+            a.max_ctx = e->cfg.max_context;
+            a.n_split = e->att_split;
+            a.attn_out = e->attn;
+            a.part = e->att_part;
+            a.cnt = e->att_cnt;
+            a.st = S.st;
+            err = launch(attn_decode_kernel<__nv_bfloat16>, NKV * e->att_split, 256, AttnSmem<__nv_bfloat16>::total,
+                         e->stream, a, true);
+        } else {
+            AttnParams<__half> a{};
+            a.qkv = e->qkv;
+            a.q_norm = ly.q_norm;
+            a.k_norm = ly.k_norm;
+            a.rope = S.rope;
+            a.kc = reinterpret_cast<__half*>(S.kc) + kv_layer * l;
+            a.vc = reinterpret_cast<__half*>(S.vc) + kv_layer * l;
+            a.max_ctx = e->cfg.max_context;
+            a.n_split = e->att_split;
+            a.attn_out = e->attn;
+            a.part = e->att_part;
+            a.cnt = e->att_cnt;
+            a.st = S.st;
+            err = launch(attn_decode_kernel<__half>, NKV * e->att_split, 256, AttnSmem<__half>::total, e->stream, a,
+                         true);
+        }
+        if (err != cudaSuccess) return err;
+        // 3. o-proj + residual
+        p = base_params(e, ly.o);
+        p.in_mode = IN_F32;
+        p.x = e->attn;
+        p.x_resid = e->x;
+        p.st = S.st;
+        if ((err = launch_gemv<FMT_Q4S, EPI_RESID>(e, ly.o, p, e->stream)) != cudaSuccess) return err;
+        // 4. RMSNorm + gate/up + SwiGLU
+        p = base_params(e, ly.gu);
+        p.in_mode = IN_F32;
+        p.x = e->x;
+        p.norm_w = ly.mlp_norm;
+        p.out = e->h;
+        p.st = S.st;
+        if ((err = launch_gemv<FMT_Q4S, EPI_SWIGLU>(e, ly.gu, p, e->stream)) != cudaSuccess) return err;
+        // 5. down + residual (+ DeepStack rows after layers 0..2 while prefilling visual rows)
+        p = base_params(e, ly.d);
+        p.in_mode = IN_F32;
+        p.x = e->h;
+        p.x_resid = e->x;
+        p.deepstack = (l < 3) ? e->deepstack[l] : nullptr;
+        p.st = S.st;
+        if ((err = launch_gemv<FMT_Q4S, EPI_RESID>(e, ly.d, p, e->stream)) != cudaSuccess) return err;
+    }
+    return cudaSuccess;
+}
+
+cudaError_t record_head(icua_engine* e, Session& S) {
+    GemvParams p = base_params(e, e->embed);
+    p.in_mode = IN_F32;
+    p.x = e->x;
+    p.norm_w = e->final_norm;
+    p.logits = e->logits;
+    p.cta_best_v = e->cta_best_v;
+    p.cta_best_i = e->cta_best_i;
+    p.cta_done = e->cta_done;
+    p.out_tokens = S.out_tokens;
+    p.step_logits = e->step_logits;
+    p.st = S.st;
+    return launch_gemv<FMT_Q8, EPI_LOGITS>(e, e->embed, p, e->stream);
+}
+
+icua_status build_graph(icua_engine* eng, Session& S, int kind, cudaGraphExec_t* out) {
+    // kind 0: prefill token (layers + advance); 1: one decode step; 2: steps_per_graph steps
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(eng->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t err = cudaSuccess;
+    if (kind == 0) {
+        err = record_layers(eng, S);
+        if (err == cudaSuccess) err = launch(advance_kernel, 1, 32, 0, eng->stream, S.st, true);
+    } else {
+        const int n = kind == 1 ? 1 : eng->cfg.steps_per_graph;
+        for (int i = 0; i < n && err == cudaSuccess; ++i) {
+            err = record_layers(eng, S);
+            if (err == cudaSuccess) err = record_head(eng, S);
+        }
+    }
+    cudaError_t e2 = cudaStreamEndCapture(eng->stream, &g);
+    if (err != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        return fail(eng, ICUA_ERR_CUDA, "graph capture: %s", cudaGetErrorString(err));
+    }
+    if (e2 != cudaSuccess) return fail(eng, ICUA_ERR_CUDA, "end capture: %s", cudaGetErrorString(e2));
+    cudaError_t e3 = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e3 != cudaSuccess) return fail(eng, ICUA_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e3));
+    return ICUA_OK;
+}
+
+void drop_graphs(Session& S) {
+    if (S.g_prefill_tok) cudaGraphExecDestroy(S.g_prefill_tok);
+    if (S.g_step1) cudaGraphExecDestroy(S.g_step1);
+    if (S.g_stepn) cudaGraphExecDestroy(S.g_stepn);
+    S.g_prefill_tok = S.g_step1 = S.g_stepn = nullptr;
+}
+
+icua_status ensure_graphs(icua_engine* eng, Session& S) {
+    icua_status s;
+    if (!S.g_prefill_tok && (s = build_graph(eng, S, 0, &S.g_prefill_tok)) != ICUA_OK) return s;
+    if (!S.g_step1 && (s = build_graph(eng, S, 1, &S.g_step1)) != ICUA_OK) return s;
+    if (!S.g_stepn && (s = build_graph(eng, S, 2, &S.g_stepn)) != ICUA_OK) return s;
+    return ICUA_OK;
+}
+
+// ---- M-RoPE table (reference prepareMRoPE, Engine.swift:254-298) ---------------------------------
+// Slots >= start get angles for positions laid out as the reference: text slots before the visual
+// block use t=h=w=slot, visual slots (visOffset + v) use (visOffset, visOffset + v / llm_w,
+// visOffset + v % llm_w), later slots use slot + rope_delta.  Frequency i < 60 takes H when
+// i % 3 == 1 and W when i % 3 == 2, T otherwise.  inv_freq follows the fp32 oracle formula.
+void fill_rope(icua_engine* e, std::vector<float2>& tab, int start, int vis_abs, int llm_h, int llm_w,
+               int rope_delta) {
+    const int n_vis = llm_h * llm_w;
+    for (int slot = start; slot < e->cfg.max_context; ++slot) {
+        int pt, ph, pw;
+        if (vis_abs < 0 || slot < vis_abs) {
+            pt = ph = pw = slot + (vis_abs < 0 ? rope_delta : 0);
+        } else if (slot < vis_abs + n_vis) {
+            const int v = slot - vis_abs;
+            pt = vis_abs;
+            ph = vis_abs + v / llm_w;
+            pw = vis_abs + v % llm_w;
+        } else {
+            pt = ph = pw = slot + rope_delta;
+        }
+        for (int i = 0; i < 64; ++i) {
+            const int pv = (i < 60 && i % 3 == 1) ? ph : (i < 60 && i % 3 == 2) ? pw : pt;
+            const float ang = (float)pv * e->inv_freq[i];
+            tab[(size_t)slot * 64 + i] = make_float2((float)cos((double)ang), (float)sin((double)ang));
+        }
+    }
+}
+
+icua_status check_ready(icua_engine* eng) {
+    if (eng->failed) return fail(eng, ICUA_ERR_STATE, "engine failed earlier: %s", eng->err.c_str());
+    if (!eng->uploaded) return fail(eng, ICUA_ERR_STATE, "weights are not complete (icua_engine_ready)");
+    return ICUA_OK;
+}
+
+Session* get_session(icua_engine* eng, int s) {
+    if (s < 0 || s >= (int)eng->sessions.size()) return nullptr;
+    return &eng->sessions[s];
+}
+
+icua_status sync_and_check(icua_engine* eng, Session& S) {
+    CK(cudaStreamSynchronize(eng->stream));
+    DevState hs;
+    CK(cudaMemcpy(&hs, S.st, sizeof hs, cudaMemcpyDeviceToHost));
+    S.pos = hs.pos;
+    S.step = hs.step;
+    S.done = hs.done;
+    if (hs.error) {
+        eng->failed = true;
+        return fail(eng, ICUA_ERR_TIMEOUT, "a bounded device wait gave up (flags 0x%x)", hs.error);
+    }
+    return ICUA_OK;
+}
+
+// ---- weights --------------------------------------------------------------------------------
+size_t expected_bytes(const icua_engine* e, int id) {
+    const int fmt = e->cfg.format;
+    const size_t V = (size_t)e->cfg.vocab;
+    if (id == ICUA_TID_EMBED) return V * H;            // q8 codes
+    if (id == ICUA_TID_EMBED_SB) return V * (H / 32) * 2;
+    if (id == ICUA_TID_FINAL_NORM) return H * 4;
+    const int rel = id - ICUA_TID_LAYER_BASE;
+    const int slot = rel % ICUA_TID_PER_LAYER;
+    auto mat = [&](int rows, int k) -> size_t { return fmt == ICUA_FMT_Q4S ? (size_t)rows * k / 2 : (size_t)rows * k; };
+    auto sb = [&](int rows, int k) -> size_t { return (size_t)rows * (k / 32) * 2; };
+    switch (slot) {
+        case ICUA_SLOT_ATTN_NORM:
+        case ICUA_SLOT_MLP_NORM: return H * 4;
+        case ICUA_SLOT_Q_NORM:
+        case ICUA_SLOT_K_NORM: return HD * 4;
+        case ICUA_SLOT_WQKV: return mat(QKV_ROWS, H);
+        case ICUA_SLOT_WQKV_SB: return sb(QKV_ROWS, H);
+        case ICUA_SLOT_WO: return mat(H, H);
+        case ICUA_SLOT_WO_SB: return sb(H, H);
+        case ICUA_SLOT_WGU: return mat(GU_ROWS, H);
+        case ICUA_SLOT_WGU_SB: return sb(GU_ROWS, H);
+        case ICUA_SLOT_WD: return mat(H, FF);
+        case ICUA_SLOT_WD_SB: return sb(H, FF);
+        default: return 0;
+    }
+}
+
+bool id_used(const icua_engine* e, int id) {
+    if (id == ICUA_TID_EMBED || id == ICUA_TID_EMBED_SB || id == ICUA_TID_FINAL_NORM) return true;
+    const int rel = id - ICUA_TID_LAYER_BASE;
+    if (rel < 0 || rel >= e->cfg.n_layers * ICUA_TID_PER_LAYER) return false;
+    return (rel % ICUA_TID_PER_LAYER) <= ICUA_SLOT_WD_SB;
+}
+
+icua_status upload_f32(icua_engine* eng, float** dst, const std::vector<uint8_t>& src) {
+    icua_status s = dalloc(eng, reinterpret_cast<void**>(dst), src.size());
+    if (s != ICUA_OK) return s;
+    CK(cudaMemcpy(*dst, src.data(), src.size(), cudaMemcpyHostToDevice));
+    return ICUA_OK;
+}
+
+icua_status upload_matrix(icua_engine* eng, Matrix& m, int fmt, int rows, int k, const std::vector<uint8_t>& codes,
+                          const std::vector<uint8_t>& sb, const int* row_map) {
+    setup_matrix(m, fmt, rows, k, eng->n_workers);
+    const size_t bytes = icua_packed_bytes(fmt, rows, k);
+    std::vector<uint8_t> packed(bytes);
+    if (fmt == FMT_Q4S)
+        icua_host::pack_q4s(rows, k, codes.data(), reinterpret_cast<const uint16_t*>(sb.data()), row_map, packed.data());
+    else
+        icua_host::pack_q8(rows, k, reinterpret_cast<const int8_t*>(codes.data()),
+                           reinterpret_cast<const uint16_t*>(sb.data()), row_map, packed.data());
+    icua_status s = dalloc(eng, reinterpret_cast<void**>(&m.dev), bytes);
+    if (s != ICUA_OK) return s;
+    CK(cudaMemcpy(m.dev, packed.data(), bytes, cudaMemcpyHostToDevice));
+    return ICUA_OK;
+}
+
+icua_status try_finalize(icua_engine* eng) {
+    if (eng->uploaded) return ICUA_OK;
+    for (int id = 0; id < ICUA_TENSOR_COUNT; ++id)
+        if (id_used(eng, id) && !eng->staged.count(id)) return ICUA_OK;  // not complete yet
+    CK(cudaSetDevice(eng->cfg.device));
+    icua_status s;
+    auto& st = eng->staged;
+    const int fmt = FMT_Q4S;
+    if ((s = upload_matrix(eng, eng->embed, FMT_Q8, eng->cfg.vocab, H, st[ICUA_TID_EMBED], st[ICUA_TID_EMBED_SB],
+                           nullptr)) != ICUA_OK)
+        return s;
+    if ((s = upload_f32(eng, &eng->final_norm, st[ICUA_TID_FINAL_NORM])) != ICUA_OK) return s;
+    std::vector<int> gu_map(GU_ROWS);
+    for (int d = 0; d < GU_ROWS; ++d) {
+        const int tile = d / 16, r = d % 16;
+        gu_map[d] = r < 8 ? tile * 8 + r : FF + tile * 8 + (r - 8);
+    }
+    for (int l = 0; l < eng->cfg.n_layers; ++l) {
+        Layer& ly = eng->layers[l];
+        auto id = [&](int slot) { return ICUA_TID_LAYER_BASE + l * ICUA_TID_PER_LAYER + slot; };
+        if ((s = upload_f32(eng, &ly.attn_norm, st[id(ICUA_SLOT_ATTN_NORM)])) != ICUA_OK) return s;
+        if ((s = upload_f32(eng, &ly.q_norm, st[id(ICUA_SLOT_Q_NORM)])) != ICUA_OK) return s;
+        if ((s = upload_f32(eng, &ly.k_norm, st[id(ICUA_SLOT_K_NORM)])) != ICUA_OK) return s;
+        if ((s = upload_f32(eng, &ly.mlp_norm, st[id(ICUA_SLOT_MLP_NORM)])) != ICUA_OK) return s;
+        if ((s = upload_matrix(eng, ly.qkv, fmt, QKV_ROWS, H, st[id(ICUA_SLOT_WQKV)], st[id(ICUA_SLOT_WQKV_SB)],
+                               nullptr)) != ICUA_OK)
+            return s;
+        if ((s = upload_matrix(eng, ly.o, fmt, H, H, st[id(ICUA_SLOT_WO)], st[id(ICUA_SLOT_WO_SB)], nullptr)) != ICUA_OK)
+            return s;
+        if ((s = upload_matrix(eng, ly.gu, fmt, GU_ROWS, H, st[id(ICUA_SLOT_WGU)], st[id(ICUA_SLOT_WGU_SB)],
+                               gu_map.data())) != ICUA_OK)
+            return s;
+        if ((s = upload_matrix(eng, ly.d, fmt, H, FF, st[id(ICUA_SLOT_WD)], st[id(ICUA_SLOT_WD_SB)], nullptr)) != ICUA_OK)
+            return s;
+    }
+    eng->staged.clear();
+    eng->uploaded = true;
+    return ICUA_OK;
+}
+
+}  // namespace
+
+// =================================================================================================
+// C ABI
+extern "C" {
+
+const char* icua_global_error(void) { return g_error.c_str(); }
+const char* icua_last_error(const icua_engine* eng) { return eng ? eng->err.c_str() : g_error.c_str(); }
+
+void icua_default_config(icua_config* c) {
+    if (!c) return;
+    c->device = 0;
+    c->n_layers = 28;
+    c->vocab = 151936;
+    c->max_context = 2048;
+    c->max_pass = 512;
+    c->max_steps = 256;
+    c->max_sessions = 1;
+    c->format = ICUA_FMT_Q4S;
+    c->kv_dtype = ICUA_KV_F16;
+    c->steps_per_graph = 8;
+}
+
+icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
+    if (!cfg || !out) return fail(nullptr, ICUA_ERR_INVALID, "null argument");
+    *out = nullptr;
+    if (cfg->format != ICUA_FMT_Q4S)
+        return fail(nullptr, ICUA_ERR_UNSUPPORTED, "weight format %d is not implemented by the kernels", cfg->format);
+    if (cfg->n_layers < 1 || cfg->n_layers > 28 || cfg->vocab < 16 || cfg->vocab % 16 || cfg->max_context < 2 ||
+        cfg->max_pass < 1 || cfg->max_steps < 1 || cfg->max_sessions < 1 || cfg->steps_per_graph < 1 ||
+        (cfg->kv_dtype != ICUA_KV_F16 && cfg->kv_dtype != ICUA_KV_BF16))
+        return fail(nullptr, ICUA_ERR_INVALID, "invalid configuration");
+    icua_engine* eng = new icua_engine();
+    eng->cfg = *cfg;
+    cudaError_t e = cudaSetDevice(cfg->device);
+    if (e != cudaSuccess) {
+        delete eng;
+        return fail(nullptr, ICUA_ERR_CUDA, "cudaSetDevice(%d): %s", cfg->device, cudaGetErrorString(e));
+    }
+    int dev = cfg->device;
+    cudaDeviceGetAttribute(&eng->n_sm, cudaDevAttrMultiProcessorCount, dev);
+    eng->n_workers = eng->n_sm * 8;
+    eng->att_split = std::max(1, eng->n_sm / NKV);
+    for (int i = 0; i < 64; ++i) {
+        const float a = (float)(2 * i) / 128.0f;
+        eng->inv_freq[i] = 1.0f / powf(5000000.0f, a);
+    }
+    icua_status s = ICUA_OK;
+#define TRY(x)                       \
+    do {                             \
+        if ((s = (x)) != ICUA_OK) {  \
+            g_error = eng->err;      \
+            icua_engine_destroy(eng); \
+            return s;                \
+        }                            \
+    } while (0)
+    if ((e = set_smem_attrs()) != cudaSuccess) {
+        fail(eng, ICUA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        s = ICUA_ERR_CUDA;
+        g_error = eng->err;
+        icua_engine_destroy(eng);
+        return s;
+    }
+    if ((e = cudaStreamCreateWithFlags(&eng->stream, cudaStreamNonBlocking)) != cudaSuccess) {
+        delete eng;
+        return fail(nullptr, ICUA_ERR_CUDA, "stream: %s", cudaGetErrorString(e));
+    }
+    for (int i = 0; i < 4; ++i) cudaEventCreate(&eng->ev[i]);
+    eng->layers.resize(cfg->n_layers);
+    TRY(dalloc_t(eng, &eng->x, H));
+    TRY(dalloc_t(eng, &eng->qkv, QKV_ROWS));
+    TRY(dalloc_t(eng, &eng->attn, H));
+    TRY(dalloc_t(eng, &eng->h, FF));
+    TRY(dalloc_t(eng, &eng->logits, (size_t)cfg->vocab));
+    TRY(dalloc_t(eng, &eng->pooler, (size_t)cfg->max_pass * H));
+    for (int i = 0; i < 3; ++i) TRY(dalloc_t(eng, &eng->deepstack[i], (size_t)cfg->max_pass * H));
+    TRY(dalloc_t(eng, &eng->partials, (size_t)eng->n_workers * 32));
+    TRY(dalloc_t(eng, &eng->tile_cnt, (size_t)cfg->vocab / 16 + 1024));
+    TRY(dalloc_t(eng, &eng->att_part, (size_t)NKV * eng->att_split * ATT_PART));
+    TRY(dalloc_t(eng, &eng->att_cnt, 64));
+    TRY(dalloc_t(eng, &eng->cta_best_v, (size_t)eng->n_sm));
+    TRY(dalloc_t(eng, &eng->cta_best_i, (size_t)eng->n_sm));
+    TRY(dalloc_t(eng, &eng->cta_done, 16));
+    cudaMemset(eng->tile_cnt, 0, ((size_t)cfg->vocab / 16 + 1024) * sizeof(unsigned));
+    cudaMemset(eng->att_cnt, 0, 64 * sizeof(unsigned));
+    cudaMemset(eng->cta_done, 0, 16 * sizeof(unsigned));
+    eng->sessions.resize(cfg->max_sessions);
+    const size_t kv_elems = (size_t)cfg->n_layers * NKV * cfg->max_context * HD;
+    for (auto& S : eng->sessions) {
+        TRY(dalloc_t(eng, &S.st, 1));
+        TRY(dalloc_t(eng, &S.prompt, (size_t)cfg->max_pass));
+        TRY(dalloc_t(eng, &S.out_tokens, (size_t)cfg->max_steps + 64));
+        TRY(dalloc_t(eng, &S.rope, (size_t)cfg->max_context * 64));
+        TRY(dalloc(eng, &S.kc, kv_elems * 2));
+        TRY(dalloc(eng, &S.vc, kv_elems * 2));
+        cudaMemset(S.st, 0, sizeof(DevState));
+    }
+#undef TRY
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        fail(eng, ICUA_ERR_CUDA, "init: %s", cudaGetErrorString(e));
+        g_error = eng->err;
+        icua_engine_destroy(eng);
+        return ICUA_ERR_CUDA;
+    }
+    *out = eng;
+    for (int i = 0; i < cfg->max_sessions; ++i) icua_reset_session(eng, i);
+    return ICUA_OK;
+}
+
+void icua_engine_destroy(icua_engine* eng) {
+    if (!eng) return;
+    cudaSetDevice(eng->cfg.device);
+    if (eng->stream) cudaStreamSynchronize(eng->stream);
+    for (auto& S : eng->sessions) drop_graphs(S);
+    for (void* p : eng->allocations) cudaFree(p);
+    for (int i = 0; i < 4; ++i)
+        if (eng->ev[i]) cudaEventDestroy(eng->ev[i]);
+    if (eng->stream) cudaStreamDestroy(eng->stream);
+    delete eng;
+}
+
+icua_status icua_engine_set_tensor(icua_engine* eng, int32_t id, const void* data, uint64_t bytes) {
+    if (!eng || !data) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    if (eng->uploaded) return fail(eng, ICUA_ERR_STATE, "weights already uploaded");
+    if (id < 0 || id >= ICUA_TENSOR_COUNT) return fail(eng, ICUA_ERR_INVALID, "tensor id %d out of range", id);
+    if (!id_used(eng, id)) return ICUA_OK;  // vision tensors and unused slots are ignored
+    const size_t want = expected_bytes(eng, id);
+    if (bytes != want)
+        return fail(eng, ICUA_ERR_FORMAT, "tensor %d: %llu bytes, expected %zu", id, (unsigned long long)bytes, want);
+    eng->staged[id] = std::vector<uint8_t>((const uint8_t*)data, (const uint8_t*)data + bytes);
+    return try_finalize(eng);
+}
+
+icua_status icua_engine_ready(icua_engine* eng) {
+    if (!eng) return fail(nullptr, ICUA_ERR_INVALID, "null engine");
+    return eng->uploaded ? ICUA_OK : fail(eng, ICUA_ERR_STATE, "weights incomplete");
+}
+
+icua_status icua_engine_load_file(icua_engine* eng, const char* path) {
+    if (!eng || !path) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return fail(eng, ICUA_ERR_IO, "cannot open %s", path);
+    struct stat sb;
+    if (fstat(fd, &sb) != 0) {
+        close(fd);
+        return fail(eng, ICUA_ERR_IO, "cannot stat %s", path);
+    }
+    const size_t size = (size_t)sb.st_size;
+    if (size < 16384 || size % 16384) {
+        close(fd);
+        return fail(eng, ICUA_ERR_FORMAT, "%s: bad size %zu", path, size);
+    }
+    void* p = mmap(nullptr, size, PROT_READ, MAP_SHARED, fd, 0);
+    close(fd);
+    if (p == MAP_FAILED) return fail(eng, ICUA_ERR_IO, "mmap failed for %s", path);
+    const uint8_t* base = (const uint8_t*)p;
+    uint32_t hdr[4];
+    memcpy(hdr, base, 16);
+    icua_status s = ICUA_OK;
+    if (hdr[0] != 0x31554349u)
+        s = fail(eng, ICUA_ERR_FORMAT, "%s: not an instantcua model", path);
+    else if (hdr[1] != 1)
+        s = fail(eng, ICUA_ERR_FORMAT, "%s: unsupported version", path);
+    else if ((int)hdr[2] != eng->cfg.format)
+        s = fail(eng, ICUA_ERR_FORMAT, "%s: format %u does not match the engine format %d", path, hdr[2], eng->cfg.format);
+    else if (hdr[3] != (uint32_t)ICUA_TENSOR_COUNT)
+        s = fail(eng, ICUA_ERR_FORMAT, "%s: tensor table mismatch", path);
+    for (int id = 0; s == ICUA_OK && id < ICUA_TENSOR_COUNT; ++id) {
+        if (!id_used(eng, id)) continue;
+        uint64_t off, sz;
+        memcpy(&off, base + 16 + 16 * id, 8);
+        memcpy(&sz, base + 16 + 16 * id + 8, 8);
+        if (off + sz > size) {
+            s = fail(eng, ICUA_ERR_FORMAT, "%s: tensor %d outside the file", path, id);
+            break;
+        }
+        s = icua_engine_set_tensor(eng, id, base + off, sz);
+    }
+    munmap(p, size);
+    if (s == ICUA_OK && !eng->uploaded) s = fail(eng, ICUA_ERR_FORMAT, "%s: tensors missing", path);
+    return s;
+}
+
+icua_status icua_set_eos(icua_engine* eng, int32_t eos0, int32_t eos1, int32_t stop) {
+    if (!eng) return fail(nullptr, ICUA_ERR_INVALID, "null engine");
+    eng->eos0 = eos0;
+    eng->eos1 = eos1;
+    eng->stop_on_eos = stop ? 1 : 0;
+    return ICUA_OK;
+}
+
+icua_status icua_reset_session(icua_engine* eng, int32_t session) {
+    if (!eng) return fail(nullptr, ICUA_ERR_INVALID, "null engine");
+    Session* S = get_session(eng, session);
+    if (!S) return fail(eng, ICUA_ERR_INVALID, "session %d out of range", session);
+    CK(cudaSetDevice(eng->cfg.device));
+    S->pos = 0;
+    S->step = 0;
+    S->done = 0;
+    S->rope_delta = 0;
+    std::vector<float2> tab((size_t)eng->cfg.max_context * 64);
+    fill_rope(eng, tab, 0, -1, 0, 0, 0);
+    CK(cudaMemcpy(S->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    DevState hs{};
+    hs.vis_offset = -1;
+    hs.session = session;
+    CK(cudaMemcpy(S->st, &hs, sizeof hs, cudaMemcpyHostToDevice));
+    return ICUA_OK;
+}
+
+icua_status icua_session_position(icua_engine* eng, int32_t session, int32_t* pos) {
+    Session* S = eng ? get_session(eng, session) : nullptr;
+    if (!S || !pos) return fail(eng, ICUA_ERR_INVALID, "bad argument");
+    *pos = S->pos;
+    return ICUA_OK;
+}
+
+icua_status icua_inject_kv(icua_engine* eng, int32_t session, const float* k, const float* v, int32_t n_pos) {
+    Session* S = eng ? get_session(eng, session) : nullptr;
+    if (!S || !k || !v || n_pos < 0) return fail(eng, ICUA_ERR_INVALID, "bad argument");
+    if (n_pos >= eng->cfg.max_context) return fail(eng, ICUA_ERR_CAPACITY, "%d positions exceed max_context", n_pos);
+    CK(cudaSetDevice(eng->cfg.device));
+    const int L = eng->cfg.n_layers, C = eng->cfg.max_context;
+    std::vector<uint16_t> kb((size_t)NKV * n_pos * HD), vb((size_t)NKV * n_pos * HD);
+    for (int l = 0; l < L; ++l) {
+        for (int p = 0; p < n_pos; ++p)
+            for (int h = 0; h < NKV; ++h)
+                for (int d = 0; d < HD; ++d) {
+                    const size_t src = (((size_t)l * n_pos + p) * NKV + h) * HD + d;
+                    const size_t dst = ((size_t)h * n_pos + p) * HD + d;
+                    if (eng->cfg.kv_dtype == ICUA_KV_F16) {
+                        kb[dst] = icua_host::f32_to_f16_bits(k[src]);
+                        vb[dst] = icua_host::f32_to_f16_bits(v[src]);
+                    } else {
+                        auto bf = [](float f) {
+                            uint32_t u;
+                            memcpy(&u, &f, 4);
+                            u += 0x7FFFu + ((u >> 16) & 1u);
+                            return (uint16_t)(u >> 16);
+                        };
+                        kb[dst] = bf(k[src]);
+                        vb[dst] = bf(v[src]);
+                    }
+                }
+        for (int h = 0; h < NKV; ++h) {
+            const size_t off = (((size_t)l * NKV + h) * C) * HD * 2;
+            CK(cudaMemcpy((uint8_t*)S->kc + off, kb.data() + (size_t)h * n_pos * HD, (size_t)n_pos * HD * 2,
+                          cudaMemcpyHostToDevice));
+            CK(cudaMemcpy((uint8_t*)S->vc + off, vb.data() + (size_t)h * n_pos * HD, (size_t)n_pos * HD * 2,
+                          cudaMemcpyHostToDevice));
+        }
+    }
+    S->pos = n_pos;
+    return ICUA_OK;
+}
+
+icua_status icua_inject_kv_random(icua_engine* eng, int32_t session, int32_t n_pos, uint64_t seed) {
+    Session* S = eng ? get_session(eng, session) : nullptr;
+    if (!S || n_pos < 0) return fail(eng, ICUA_ERR_INVALID, "bad argument");
+    if (n_pos >= eng->cfg.max_context) return fail(eng, ICUA_ERR_CAPACITY, "%d positions exceed max_context", n_pos);
+    CK(cudaSetDevice(eng->cfg.device));
+    if (eng->cfg.kv_dtype == ICUA_KV_F16)
+        kv_fill_random_kernel<__half><<<eng->n_sm * 8, 256, 0, eng->stream>>>(
+            (__half*)S->kc, (__half*)S->vc, eng->cfg.n_layers, eng->cfg.max_context, n_pos, seed);
+    else
+        kv_fill_random_kernel<__nv_bfloat16><<<eng->n_sm * 8, 256, 0, eng->stream>>>(
+            (__nv_bfloat16*)S->kc, (__nv_bfloat16*)S->vc, eng->cfg.n_layers, eng->cfg.max_context, n_pos, seed);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(eng->stream));
+    S->pos = n_pos;
+    return ICUA_OK;
+}
+
+icua_status icua_capture_step_logits(icua_engine* eng, float* host_out, int32_t cap) {
+    if (!eng) return fail(nullptr, ICUA_ERR_INVALID, "null engine");
+    CK(cudaSetDevice(eng->cfg.device));
+    if (host_out == nullptr) {
+        eng->step_logits_host = nullptr;
+        eng->step_logits_cap = 0;
+        return ICUA_OK;
+    }
+    if (cap < 1 || cap > eng->cfg.max_steps) return fail(eng, ICUA_ERR_CAPACITY, "capacity %d", cap);
+    if (!eng->step_logits) {
+        icua_status s = dalloc_t(eng, &eng->step_logits, (size_t)(eng->cfg.max_steps + 64) * eng->cfg.vocab);
+        if (s != ICUA_OK) return s;
+        for (auto& S : eng->sessions) drop_graphs(S);  // graphs bake the capture pointer
+    }
+    eng->step_logits_host = host_out;
+    eng->step_logits_cap = cap;
+    return ICUA_OK;
+}
+
+// Writes the prompt, visual rows, RoPE table and loop state; returns via *pos0 the start position.
+static icua_status prepare_prefill(icua_engine* eng, Session& S, int session, const int32_t* tokens, int n,
+                                   const icua_visual* vis, int write_logits) {
+    const int C = eng->cfg.max_context;
+    if (n < 1 || n > eng->cfg.max_pass) return fail(eng, ICUA_ERR_CAPACITY, "prompt of %d tokens (max_pass %d)", n, eng->cfg.max_pass);
+    if (S.pos + n + 1 > C) return fail(eng, ICUA_ERR_CAPACITY, "context %d + %d exceeds max_context %d", S.pos, n, C);
+    int vis_off = -1;
+    for (int i = 0; i < n; ++i) {
+        if (tokens[i] < 0 || (tokens[i] >= eng->cfg.vocab && tokens[i] != IMAGE_PAD_ID))
+            return fail(eng, ICUA_ERR_INVALID, "token %d at %d out of range", tokens[i], i);
+        if (tokens[i] == IMAGE_PAD_ID && vis_off < 0) vis_off = i;
+    }
+    if (vis_off >= 0 && (!vis || !vis->pooler))
+        return fail(eng, ICUA_ERR_INVALID, "IMAGE_PAD tokens without visual inputs");
+    CK(cudaMemcpyAsync(S.prompt, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, eng->stream));
+    std::vector<float2> tab((size_t)C * 64);
+    CK(cudaMemcpy(tab.data(), S.rope, tab.size() * sizeof(float2), cudaMemcpyDeviceToHost));
+    int n_vis = 0;
+    if (vis_off >= 0) {
+        n_vis = vis->n_vis;
+        if (n_vis < 1 || n_vis != vis->llm_h * vis->llm_w || vis_off + n_vis > n)
+            return fail(eng, ICUA_ERR_INVALID, "visual block of %d rows (grid %dx%d) does not fit the prompt", n_vis,
+                        vis->llm_h, vis->llm_w);
+        for (int i = vis_off; i < vis_off + n_vis; ++i)
+            if (tokens[i] != IMAGE_PAD_ID) return fail(eng, ICUA_ERR_INVALID, "visual block is not contiguous");
+        CK(cudaMemcpyAsync(eng->pooler, vis->pooler, (size_t)n_vis * H * 4, cudaMemcpyHostToDevice, eng->stream));
+        for (int d = 0; d < 3; ++d) {
+            if (vis->deepstack[d])
+                CK(cudaMemcpyAsync(eng->deepstack[d], vis->deepstack[d], (size_t)n_vis * H * 4, cudaMemcpyHostToDevice,
+                                   eng->stream));
+            else
+                CK(cudaMemsetAsync(eng->deepstack[d], 0, (size_t)n_vis * H * 4, eng->stream));
+        }
+        const int vis_abs = S.pos + vis_off;
+        S.rope_delta = std::max(vis->llm_h, vis->llm_w) - n_vis;
+        fill_rope(eng, tab, S.pos, vis_abs, vis->llm_h, vis->llm_w, S.rope_delta);
+    } else {
+        fill_rope(eng, tab, S.pos, -1, 0, 0, S.rope_delta);
+    }
+    CK(cudaMemcpyAsync(S.rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, eng->stream));
+    DevState hs{};
+    hs.pos = S.pos;
+    hs.step = 0;
+    hs.done = 0;
+    hs.max_steps = 1;
+    hs.eos0 = eng->eos0;
+    hs.eos1 = eng->eos1;
+    hs.stop_on_eos = eng->stop_on_eos;
+    hs.cur_token = 0;
+    hs.prompt_idx = 0;
+    hs.prompt_len = n;
+    hs.vis_offset = vis_off;
+    hs.n_vis = n_vis;
+    hs.write_logits = write_logits ? 1 : 0;
+    hs.session = session;
+    CK(cudaMemcpyAsync(S.st, &hs, sizeof hs, cudaMemcpyHostToDevice, eng->stream));
+    CK(cudaStreamSynchronize(eng->stream));  // host staging buffers go out of scope
+    S.step = 0;
+    S.done = 0;
+    return ICUA_OK;
+}
+
+icua_status icua_prefill(icua_engine* eng, int32_t session, const int32_t* tokens, int32_t n, const icua_visual* vis,
+                         int32_t write_logits, int32_t* first_token) {
+    if (!eng || !tokens) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    icua_status s;
+    if ((s = check_ready(eng)) != ICUA_OK) return s;
+    Session* S = get_session(eng, session);
+    if (!S) return fail(eng, ICUA_ERR_INVALID, "session %d out of range", session);
+    CK(cudaSetDevice(eng->cfg.device));
+    if ((s = ensure_graphs(eng, *S)) != ICUA_OK) return s;
+    if ((s = prepare_prefill(eng, *S, session, tokens, n, vis, write_logits)) != ICUA_OK) return s;
+    CK(cudaEventRecord(eng->ev[0], eng->stream));
+    for (int i = 0; i < n - 1; ++i) CK(cudaGraphLaunch(S->g_prefill_tok, eng->stream));
+    CK(cudaGraphLaunch(S->g_step1, eng->stream));
+    CK(cudaEventRecord(eng->ev[1], eng->stream));
+    if ((s = sync_and_check(eng, *S)) != ICUA_OK) return s;
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, eng->ev[0], eng->ev[1]);
+    eng->timing.prefill_ms = ms;
+    eng->timing.prefill_tokens = n;
+    int tok = 0;
+    CK(cudaMemcpy(&tok, S->out_tokens, 4, cudaMemcpyDeviceToHost));
+    if (eng->step_logits_host) CK(cudaMemcpy(eng->step_logits_host, eng->step_logits, (size_t)eng->cfg.vocab * 4, cudaMemcpyDeviceToHost));
+    if (first_token) *first_token = tok;
+    // the write-logits request applies to the prompt pass only
+    const int zero = 0;
+    CK(cudaMemcpy(&S->st->write_logits, &zero, 4, cudaMemcpyHostToDevice));
+    return ICUA_OK;
+}
+
+icua_status icua_decode(icua_engine* eng, int32_t session, int32_t max_new, int32_t* out, int32_t* n_out) {
+    if (!eng || !out || !n_out) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    icua_status s;
+    if ((s = check_ready(eng)) != ICUA_OK) return s;
+    Session* S = get_session(eng, session);
+    if (!S) return fail(eng, ICUA_ERR_INVALID, "session %d out of range", session);
+    *n_out = 0;
+    if (max_new <= 0) return ICUA_OK;
+    CK(cudaSetDevice(eng->cfg.device));
+    if ((s = ensure_graphs(eng, *S)) != ICUA_OK) return s;
+    if (S->step < 1) return fail(eng, ICUA_ERR_STATE, "decode before prefill");
+    if (S->done && S->step >= 1) {
+        // a finished prefill (max_steps reached) is resumed; an EOS stop is final
+        int last = 0;
+        CK(cudaMemcpy(&last, S->out_tokens + S->step - 1, 4, cudaMemcpyDeviceToHost));
+        if (eng->stop_on_eos && (last == eng->eos0 || last == eng->eos1)) return ICUA_OK;
+    }
+    const int base_step = S->step;
+    if (base_step + max_new > eng->cfg.max_steps + 1)
+        return fail(eng, ICUA_ERR_CAPACITY, "%d steps exceed max_steps %d", base_step + max_new, eng->cfg.max_steps);
+    if (S->pos + max_new + eng->cfg.steps_per_graph > eng->cfg.max_context)
+        return fail(eng, ICUA_ERR_CAPACITY, "context %d + %d exceeds max_context", S->pos, max_new);
+    const int ms_val = base_step + max_new, zero = 0;
+    CK(cudaMemcpyAsync(&S->st->max_steps, &ms_val, 4, cudaMemcpyHostToDevice, eng->stream));
+    CK(cudaMemcpyAsync(&S->st->done, &zero, 4, cudaMemcpyHostToDevice, eng->stream));
+    const auto t0 = std::chrono::steady_clock::now();
+    CK(cudaEventRecord(eng->ev[2], eng->stream));
+    const int spg = eng->cfg.steps_per_graph;
+    int launched = 0;
+    while (launched + spg <= max_new) {
+        CK(cudaGraphLaunch(S->g_stepn, eng->stream));
+        launched += spg;
+    }
+    while (launched < max_new) {
+        CK(cudaGraphLaunch(S->g_step1, eng->stream));
+        launched += 1;
+    }
+    CK(cudaEventRecord(eng->ev[3], eng->stream));
+    if ((s = sync_and_check(eng, *S)) != ICUA_OK) return s;
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, eng->ev[2], eng->ev[3]);
+    eng->timing.decode_ms = ms;
+    const int got = S->step - base_step;
+    std::vector<int32_t> toks(got > 0 ? got : 1);
+    if (got > 0) CK(cudaMemcpy(toks.data(), S->out_tokens + base_step, (size_t)got * 4, cudaMemcpyDeviceToHost));
+    int n = 0;
+    for (int i = 0; i < got; ++i) {
+        if (eng->stop_on_eos && (toks[i] == eng->eos0 || toks[i] == eng->eos1)) break;
+        out[n++] = toks[i];
+    }
+    *n_out = n;
+    if (eng->step_logits_host && got > 0) {
+        const int rows = std::min(got, eng->step_logits_cap);
+        CK(cudaMemcpy(eng->step_logits_host, eng->step_logits + (size_t)base_step * eng->cfg.vocab,
+                      (size_t)rows * eng->cfg.vocab * 4, cudaMemcpyDeviceToHost));
+    }
+    eng->timing.generated_tokens = n;
+    eng->timing.total_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return ICUA_OK;
+}
+
+icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token, int32_t* out_token) {
+    if (!eng || !out_token) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    icua_status s;
+    if ((s = check_ready(eng)) != ICUA_OK) return s;
+    Session* S = get_session(eng, session);
+    if (!S) return fail(eng, ICUA_ERR_INVALID, "session %d out of range", session);
+    if (in_token < 0 || in_token >= eng->cfg.vocab) return fail(eng, ICUA_ERR_INVALID, "token %d out of range", in_token);
+    if (S->pos + 1 >= eng->cfg.max_context) return fail(eng, ICUA_ERR_CAPACITY, "context full");
+    CK(cudaSetDevice(eng->cfg.device));
+    if ((s = ensure_graphs(eng, *S)) != ICUA_OK) return s;
+    if (S->step >= eng->cfg.max_steps) S->step = 0;  // wrap the output slot for long host-driven loops
+    // one small state write (H2D) per step: input token, step budget, no prompt rows left
+    struct {
+        int step, done, max_steps;
+    } head = {S->step, 0, S->step + 1};
+    CK(cudaMemcpyAsync(&S->st->step, &head, sizeof head, cudaMemcpyHostToDevice, eng->stream));
+    CK(cudaMemcpyAsync(&S->st->cur_token, &in_token, 4, cudaMemcpyHostToDevice, eng->stream));
+    const int big = 1 << 30, one = 1;
+    CK(cudaMemcpyAsync(&S->st->prompt_idx, &big, 4, cudaMemcpyHostToDevice, eng->stream));
+    CK(cudaMemcpyAsync(&S->st->write_logits, &one, 4, cudaMemcpyHostToDevice, eng->stream));
+    CK(cudaGraphLaunch(S->g_step1, eng->stream));
+    CK(cudaMemcpyAsync(out_token, S->out_tokens + S->step, 4, cudaMemcpyDeviceToHost, eng->stream));
+    CK(cudaStreamSynchronize(eng->stream));
+    S->step += 1;
+    S->pos += 1;
+    return ICUA_OK;
+}
+
+icua_status icua_generate(icua_engine* eng, int32_t session, const int32_t* tokens, int32_t n, const icua_visual* vis,
+                          int32_t max_new, int32_t write_first_logits, int32_t* out, int32_t* n_out) {
+    if (!eng || !tokens || !out || !n_out) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    const auto t0 = std::chrono::steady_clock::now();
+    icua_status s = icua_reset_session(eng, session);
+    if (s != ICUA_OK) return s;
+    int first = 0;
+    if ((s = icua_prefill(eng, session, tokens, n, vis, write_first_logits, &first)) != ICUA_OK) return s;
+    *n_out = 0;
+    if (max_new <= 0) return ICUA_OK;
+    if (eng->stop_on_eos && (first == eng->eos0 || first == eng->eos1)) {
+        eng->timing.decode_ms = 0;
+        eng->timing.generated_tokens = 0;
+    } else {
+        out[0] = first;
+        int m = 0;
+        if (max_new > 1) {
+            if ((s = icua_decode(eng, session, max_new - 1, out + 1, &m)) != ICUA_OK) return s;
+        } else {
+            eng->timing.decode_ms = 0;
+        }
+        *n_out = 1 + m;
+        eng->timing.generated_tokens = 1 + m;
+    }
+    eng->timing.total_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return ICUA_OK;
+}
+
+icua_status icua_get_logits(icua_engine* eng, float* host_out) {
+    if (!eng || !host_out) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    CK(cudaSetDevice(eng->cfg.device));
+    CK(cudaMemcpy(host_out, eng->logits, (size_t)eng->cfg.vocab * 4, cudaMemcpyDeviceToHost));
+    return ICUA_OK;
+}
+
+icua_status icua_get_timing(icua_engine* eng, icua_timing* out) {
+    if (!eng || !out) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    *out = eng->timing;
+    return ICUA_OK;
+}
+
+// ---- kernel-level entry points ------------------------------------------------------------------
+uint64_t icua_gemv_scratch_bytes(int32_t fmt, int32_t n_rows, int32_t k) {
+    int dev = 0, n_sm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    const uint64_t workers = (uint64_t)n_sm * 8;
+    return workers * 32 * 4 + (uint64_t)(n_rows / 16 + 16) * 4;
+}
+
+icua_status icua_gemv(int32_t fmt, int32_t n_rows, int32_t k, const void* packed, const void* x, int32_t x_dtype,
+                      float* y, void* scratch, void* stream) {
+    icua_engine* eng = nullptr;
+    if (!packed || !x || !y || !scratch) return fail(nullptr, ICUA_ERR_INVALID, "null argument");
+    if ((fmt != ICUA_FMT_Q4S && fmt != ICUA_FMT_Q8) || n_rows < 16 || n_rows % 16 || k < 1024 || k % 1024 ||
+        (x_dtype != 0 && x_dtype != 1))
+        return fail(nullptr, ICUA_ERR_INVALID, "unsupported gemv shape or type (rows %% 16, k %% 1024)");
+    CK(set_smem_attrs());
+    int dev = 0, n_sm = 0;
+    CK(cudaGetDevice(&dev));
+    CK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+    Matrix m;
+    setup_matrix(m, fmt, n_rows, k, n_sm * 8);
+    GemvParams p{};
+    p.w = (const uint8_t*)packed;
+    p.n_units = m.n_units;
+    p.n_rows = n_rows;
+    p.k = k;
+    p.upt = k / 64;
+    p.slot_units = m.slot_units;
+    p.n_slots = m.n_slots;
+    p.in_mode = x_dtype == 0 ? IN_F32 : IN_BF16;
+    p.x = x;
+    p.out = y;
+    p.partials = (float*)scratch;
+    p.tile_cnt = (unsigned*)((uint8_t*)scratch + (size_t)n_sm * 8 * 32 * 4);
+    p.st = nullptr;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (fmt == ICUA_FMT_Q4S)
+        CK(launch(gemv_kernel<FMT_Q4S, EPI_STORE>, n_sm, 256, m.smem, s, p, false));
+    else
+        CK(launch(gemv_kernel<FMT_Q8, EPI_STORE>, n_sm, 256, m.smem, s, p, false));
+    return ICUA_OK;
+}
+
+icua_status icua_dequant(int32_t fmt, int32_t n_rows, int32_t k, const void* packed, float* out, void* stream) {
+    icua_engine* eng = nullptr;
+    if (!packed || !out || icua_packed_bytes(fmt, n_rows, k) == 0) return fail(nullptr, ICUA_ERR_INVALID, "bad argument");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (fmt == ICUA_FMT_Q4S)
+        dequant_kernel<FMT_Q4S><<<1184, 256, 0, s>>>((const uint8_t*)packed, n_rows, k, out);
+    else
+        dequant_kernel<FMT_Q8><<<1184, 256, 0, s>>>((const uint8_t*)packed, n_rows, k, out);
+    CK(cudaGetLastError());
+    return ICUA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,83 @@
+// Small kernels around the decode step: prompt cursor advance, bit-exact dequantisation of the
+// tile layout, KV cache fill.
+#pragma once
+#include "common.cuh"
+
+namespace icua {
+
+// Moves the prompt cursor after a prompt row that needs no logits (prefill token), the
+// counterpart of `st->pos += st->n` in the reference commit (Shaders.swift:1537).
+__global__ void advance_kernel(DevState* st) {
+    pdl_wait();
+    pdl_launch_dependents();
+    if (threadIdx.x == 0 && !st->done) {
+        st->pos += 1;
+        st->prompt_idx += 1;
+    }
+}
+
+// fp32 value of element (row, k) of a q4s tile-packed [n, K] matrix: float(scale) * (u - 8).
+__device__ __forceinline__ float q4s_tile_value(const uint8_t* tiles, int K, int row, int k) {
+    const long long unit = (long long)(row >> 4) * (K / UNIT_K) + (k >> 6);
+    const uint8_t* ub = tiles + unit * Q4_UNIT_BYTES;
+    const int rt = row & 15, gq = rt & 7, up = rt >> 3;
+    const int kin = k & 63, step = kin >> 4, kk = kin & 15;
+    const int t = (kk & 7) >> 1, odd = kk & 1, hi8 = kk >> 3;
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(ub + (gq * 4 + t) * 16 + step * 4);
+    const int u = (w >> (odd * 16 + hi8 * 8 + up * 4)) & 0xF;
+    const __half2 s2 = *reinterpret_cast<const __half2*>(ub + 512 + gq * 8 + (kin >> 5) * 4);
+    const float s = up ? __high2float(s2) : __low2float(s2);
+    return s * (float)(u - 8);
+}
+
+__device__ __forceinline__ float q8_tile_value_k(const uint8_t* tiles, int K, int row, int k) {
+    const long long unit = (long long)(row >> 4) * (K / UNIT_K) + (k >> 6);
+    const uint8_t* ub = tiles + unit * Q8_UNIT_BYTES;
+    const int rt = row & 15, gq = rt & 7, up = rt >> 3;
+    const int kin = k & 63, step = kin >> 4, kk = kin & 15;
+    const int t = (kk & 7) >> 1, odd = kk & 1, hi8 = kk >> 3;
+    const uint8_t* wp = ub + (step >> 1) * 512 + (gq * 4 + t) * 16 + ((step & 1) * 2 + hi8) * 4;
+    const int u = wp[odd * 2 + up];
+    const __half2 s2 = *reinterpret_cast<const __half2*>(ub + 1024 + gq * 8 + (kin >> 5) * 4);
+    const float s = up ? __high2float(s2) : __low2float(s2);
+    return s * (float)(u - 128);
+}
+
+template <int FMT>
+__global__ void dequant_kernel(const uint8_t* tiles, int n_rows, int K, float* out) {
+    const long long total = (long long)n_rows * K;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int row = (int)(i / K), k = (int)(i % K);
+        out[i] = FMT == FMT_Q4S ? q4s_tile_value(tiles, K, row, k) : q8_tile_value_k(tiles, K, row, k);
+    }
+}
+
+// Counter-based N(0,1) (splitmix64 hash + Box-Muller) for filling a long KV cache on the device.
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+template <typename KVT>
+__global__ void kv_fill_random_kernel(KVT* kc, KVT* vc, int n_layers, int max_ctx, int n_pos, uint64_t seed) {
+    const long long per_layer = (long long)NKV * n_pos * HD;
+    const long long total = (long long)n_layers * per_layer;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int l = (int)(i / per_layer);
+        long long r = i % per_layer;
+        const int h = (int)(r / ((long long)n_pos * HD));
+        r %= (long long)n_pos * HD;
+        const int p = (int)(r / HD), d = (int)(r % HD);
+        const long long dst = (((long long)l * NKV + h) * max_ctx + p) * HD + d;
+        const uint64_t a = splitmix64(seed ^ (uint64_t)(2 * i)), b = splitmix64(seed ^ (uint64_t)(2 * i + 1));
+        const float u1 = ((float)(a >> 40) + 1.0f) * (1.0f / 16777217.0f);
+        const float u2 = (float)(b >> 40) * (1.0f / 16777216.0f);
+        const float rad = sqrtf(-2.0f * logf(u1));
+        kc[dst] = float_to_kv<KVT>(rad * cosf(6.283185307179586f * u2));
+        vc[dst] = float_to_kv<KVT>(rad * sinf(6.283185307179586f * u2));
+    }
+}
+
+}  // namespace icua

@@ -1,0 +1,191 @@
+"""Python mirror of the reference ``Engine`` (Sources/Engine/Engine.swift) over the C ABI.
+
+Same names and meaning as the Swift class where the path overlaps:
+``Engine(model_path, max_context, max_pass, max_steps)``, ``generate_vision`` (generateVision
+without the ViT: visual rows are inputs), ``last_timing`` (Engine.Timing), ``eos``.  Errors
+raise :class:`IcuaError` carrying the engine's message (the reference throws EngineError).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib as L
+from ._lib import IcuaError  # noqa: F401  (re-export)
+
+IMAGE_PAD = 151655
+
+
+@dataclass
+class Timing:
+    vision_ms: float = 0.0
+    prefill_ms: float = 0.0
+    decode_ms: float = 0.0
+    total_ms: float = 0.0
+    prefill_tokens: int = 0
+    generated_tokens: int = 0
+
+
+class Engine:
+    """One engine per CUDA device (replicas for multi-GPU)."""
+
+    def __init__(self, model_path: str | None = None, tensors: dict | None = None, *, max_context: int = 2048,
+                 max_pass: int = 512, max_steps: int = 256, n_layers: int = 28, vocab: int = 151936,
+                 max_sessions: int = 1, kv_dtype: str = "f16", steps_per_graph: int = 8, device: int = 0):
+        self._lib = L.lib()
+        cfg = L.IcuaConfig()
+        self._lib.icua_default_config(C.byref(cfg))
+        cfg.device = device
+        cfg.n_layers = n_layers
+        cfg.vocab = vocab
+        cfg.max_context = max_context
+        cfg.max_pass = max_pass
+        cfg.max_steps = max_steps
+        cfg.max_sessions = max_sessions
+        cfg.format = L.FMT_Q4S
+        cfg.kv_dtype = {"f16": L.KV_F16, "bf16": L.KV_BF16}[kv_dtype]
+        cfg.steps_per_graph = steps_per_graph
+        self.cfg = cfg
+        h = C.c_void_p()
+        L.check(self._lib.icua_engine_create(C.byref(cfg), C.byref(h)))
+        self._h = h
+        self._eos = (151645, 151643)
+        self._stop_on_eos = True
+        if model_path is not None:
+            L.check(self._lib.icua_engine_load_file(self._h, model_path.encode()), self._h)
+        if tensors is not None:
+            self.set_tensors(tensors)
+
+    # -- weights ---------------------------------------------------------------------------------
+    def set_tensors(self, tensors: dict) -> None:
+        for tid in sorted(tensors):
+            data = tensors[tid]
+            buf = C.create_string_buffer(data, len(data)) if isinstance(data, (bytes, bytearray)) else data
+            L.check(self._lib.icua_engine_set_tensor(self._h, tid, buf, len(data)), self._h)
+        L.check(self._lib.icua_engine_ready(self._h), self._h)
+
+    # -- reference properties ----------------------------------------------------------------------
+    @property
+    def eos(self):
+        return self._eos
+
+    @eos.setter
+    def eos(self, pair):
+        self._eos = (int(pair[0]), int(pair[1]))
+        L.check(self._lib.icua_set_eos(self._h, self._eos[0], self._eos[1], int(self._stop_on_eos)), self._h)
+
+    @property
+    def stop_on_eos(self) -> bool:
+        return self._stop_on_eos
+
+    @stop_on_eos.setter
+    def stop_on_eos(self, v: bool):
+        self._stop_on_eos = bool(v)
+        L.check(self._lib.icua_set_eos(self._h, self._eos[0], self._eos[1], int(self._stop_on_eos)), self._h)
+
+    @property
+    def last_timing(self) -> Timing:
+        t = L.IcuaTiming()
+        L.check(self._lib.icua_get_timing(self._h, C.byref(t)), self._h)
+        return Timing(t.vision_ms, t.prefill_ms, t.decode_ms, t.total_ms, t.prefill_tokens, t.generated_tokens)
+
+    # -- token loop --------------------------------------------------------------------------------
+    @staticmethod
+    def _visual(pooler, deepstack, grid):
+        if pooler is None:
+            return None, []
+        keep = [np.ascontiguousarray(pooler, np.float32)]
+        v = L.IcuaVisual()
+        v.pooler = keep[0].ctypes.data_as(L._FP)
+        for i in range(3):
+            if deepstack is not None and i < len(deepstack) and deepstack[i] is not None:
+                a = np.ascontiguousarray(deepstack[i], np.float32)
+                keep.append(a)
+                v.deepstack[i] = a.ctypes.data_as(L._FP)
+            else:
+                v.deepstack[i] = None
+        v.n_vis = keep[0].shape[0]
+        v.llm_h, v.llm_w = int(grid[0]), int(grid[1])
+        return v, keep
+
+    def generate_vision(self, tokens, max_new_tokens: int = 64, pooler=None, deepstack=None, grid=(0, 0),
+                        write_first_logits: bool = False, session: int = 0) -> list:
+        """Prefill + greedy decode (Engine.generateVision minus the ViT); returns generated tokens
+        without the EOS token."""
+        toks = np.ascontiguousarray(tokens, np.int32)
+        vis, keep = self._visual(pooler, deepstack, grid)
+        out = np.zeros(max(max_new_tokens, 1), np.int32)
+        n = C.c_int32()
+        L.check(self._lib.icua_generate(self._h, session, toks.ctypes.data_as(L._IP), len(toks),
+                                        C.byref(vis) if vis is not None else None, max_new_tokens,
+                                        int(write_first_logits), out.ctypes.data_as(L._IP), C.byref(n)), self._h)
+        del keep
+        return out[: n.value].tolist()
+
+    def reset(self, session: int = 0) -> None:
+        L.check(self._lib.icua_reset_session(self._h, session), self._h)
+
+    def prefill(self, tokens, pooler=None, deepstack=None, grid=(0, 0), write_logits: bool = False,
+                session: int = 0) -> int:
+        toks = np.ascontiguousarray(tokens, np.int32)
+        vis, keep = self._visual(pooler, deepstack, grid)
+        first = C.c_int32()
+        L.check(self._lib.icua_prefill(self._h, session, toks.ctypes.data_as(L._IP), len(toks),
+                                       C.byref(vis) if vis is not None else None, int(write_logits),
+                                       C.byref(first)), self._h)
+        del keep
+        return first.value
+
+    def decode(self, max_new: int, session: int = 0) -> list:
+        out = np.zeros(max(max_new, 1), np.int32)
+        n = C.c_int32()
+        L.check(self._lib.icua_decode(self._h, session, max_new, out.ctypes.data_as(L._IP), C.byref(n)), self._h)
+        return out[: n.value].tolist()
+
+    def decode_step(self, in_token: int, session: int = 0) -> int:
+        o = C.c_int32()
+        L.check(self._lib.icua_decode_step(self._h, session, int(in_token), C.byref(o)), self._h)
+        return o.value
+
+    def logits(self) -> np.ndarray:
+        out = np.empty(self.cfg.vocab, np.float32)
+        L.check(self._lib.icua_get_logits(self._h, out.ctypes.data_as(L._FP)), self._h)
+        return out
+
+    def capture_step_logits(self, steps: int | None):
+        """Returns a host array the next prefill / decode fills with per-step logits (or None)."""
+        if steps is None:
+            L.check(self._lib.icua_capture_step_logits(self._h, None, 0), self._h)
+            self._cap = None
+            return None
+        self._cap = np.zeros((steps, self.cfg.vocab), np.float32)
+        L.check(self._lib.icua_capture_step_logits(self._h, self._cap.ctypes.data_as(L._FP), steps), self._h)
+        return self._cap
+
+    def inject_kv(self, k: np.ndarray, v: np.ndarray, session: int = 0) -> None:
+        """k, v: fp32 [n_layers, n_pos, 8, 128]."""
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        L.check(self._lib.icua_inject_kv(self._h, session, k.ctypes.data_as(L._FP), v.ctypes.data_as(L._FP),
+                                         k.shape[1]), self._h)
+
+    def inject_kv_random(self, n_pos: int, seed: int = 2, session: int = 0) -> None:
+        L.check(self._lib.icua_inject_kv_random(self._h, session, n_pos, seed), self._h)
+
+    def position(self, session: int = 0) -> int:
+        p = C.c_int32()
+        L.check(self._lib.icua_session_position(self._h, session, C.byref(p)), self._h)
+        return p.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.icua_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,146 @@
+"""Model tensors for the engine: seeded synthetic weights, quantization through the C ABI and the
+``.icua`` container (reference ``Sources/Engine/ModelFile.swift``).
+
+Synthetic weights follow the BASELINE configs: matrices N(0, 0.02) drawn from one
+``np.random.default_rng(seed)`` stream in reference TensorID order (embed, then per layer wqkv,
+wo, wgu, wd), norm weights 1.0; decoder matrices quantized q4s (symmetric int4, groups of 32,
+fp16 scale), the tied embedding / lm_head q8.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import struct
+
+import numpy as np
+
+from . import _lib as L
+
+H, FF, QKV_ROWS, GU_ROWS, HD = 2048, 6144, 4096, 12288, 128
+MAGIC = 0x31554349  # "ICU1"
+HEADER = 16384
+
+
+def layer_tid(l: int, slot: str) -> int:
+    return L.TID_LAYER_BASE + l * L.TID_PER_LAYER + L.SLOT[slot]
+
+
+def quantize_q8(w: np.ndarray):
+    """Reference q8 (Convert.swift:215-241) through the C ABI: int8 codes, fp16 scale bits."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, cols = w.shape
+    codes = np.empty((rows, cols), np.int8)
+    scales = np.empty((rows, cols // 32), np.uint16)
+    L.check(L.lib().icua_quantize_q8(w.ctypes.data_as(L._FP), rows, cols, codes.ctypes.data, scales.ctypes.data))
+    return codes, scales
+
+
+def quantize_q4s(w: np.ndarray):
+    """BASELINE q4s through the C ABI: packed nibbles (u = q + 8), fp16 scale bits."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, cols = w.shape
+    packed = np.empty((rows, cols // 2), np.uint8)
+    scales = np.empty((rows, cols // 32), np.uint16)
+    L.check(L.lib().icua_quantize_q4s(w.ctypes.data_as(L._FP), rows, cols, packed.ctypes.data, scales.ctypes.data))
+    return packed, scales
+
+
+def synthetic_fp32(seed: int = 0, n_layers: int = 28, vocab: int = 151936, std: float = 0.02):
+    """Yields (tensor id(s), fp32 array) in TensorID order; matrices N(0, std), norms 1.0."""
+    rng = np.random.default_rng(seed)
+    sd = np.float32(std)
+
+    def mat(r, c):
+        return rng.standard_normal((r, c), dtype=np.float32) * sd
+
+    yield (L.TID_EMBED, L.TID_EMBED_SB), mat(vocab, H)
+    yield L.TID_FINAL_NORM, np.ones(H, np.float32)
+    for l in range(n_layers):
+        yield layer_tid(l, "attn_norm"), np.ones(H, np.float32)
+        yield (layer_tid(l, "wqkv"), layer_tid(l, "wqkv_sb")), mat(QKV_ROWS, H)
+        yield layer_tid(l, "q_norm"), np.ones(HD, np.float32)
+        yield layer_tid(l, "k_norm"), np.ones(HD, np.float32)
+        yield (layer_tid(l, "wo"), layer_tid(l, "wo_sb")), mat(H, H)
+        yield layer_tid(l, "mlp_norm"), np.ones(H, np.float32)
+        yield (layer_tid(l, "wgu"), layer_tid(l, "wgu_sb")), mat(GU_ROWS, H)
+        yield (layer_tid(l, "wd"), layer_tid(l, "wd_sb")), mat(H, FF)
+
+
+def synthetic_fp32_fast(seed: int = 0, n_layers: int = 28, vocab: int = 151936, std: float = 0.02, device: int = 0):
+    """Same shapes and distribution as :func:`synthetic_fp32` (seeded N(0, std), norms 1.0), drawn
+    with torch's CUDA generator, for benchmarks where generating 1.7e9 numpy normals on the host
+    would dominate the run.  The values differ from the numpy stream; parity tests use the latter."""
+    import torch
+
+    g = torch.Generator(device=f"cuda:{device}")
+    g.manual_seed(seed)
+
+    def mat(r, c):
+        t = torch.randn((r, c), generator=g, device=f"cuda:{device}", dtype=torch.float32)
+        return (t * std).cpu().numpy()
+
+    yield (L.TID_EMBED, L.TID_EMBED_SB), mat(vocab, H)
+    yield L.TID_FINAL_NORM, np.ones(H, np.float32)
+    for l in range(n_layers):
+        yield layer_tid(l, "attn_norm"), np.ones(H, np.float32)
+        yield (layer_tid(l, "wqkv"), layer_tid(l, "wqkv_sb")), mat(QKV_ROWS, H)
+        yield layer_tid(l, "q_norm"), np.ones(HD, np.float32)
+        yield layer_tid(l, "k_norm"), np.ones(HD, np.float32)
+        yield (layer_tid(l, "wo"), layer_tid(l, "wo_sb")), mat(H, H)
+        yield layer_tid(l, "mlp_norm"), np.ones(H, np.float32)
+        yield (layer_tid(l, "wgu"), layer_tid(l, "wgu_sb")), mat(GU_ROWS, H)
+        yield (layer_tid(l, "wd"), layer_tid(l, "wd_sb")), mat(H, FF)
+
+
+def quantize_stream(fp32_stream, keep_fp32: bool = False):
+    """Quantizes a (tid, array) stream to {tensor id: bytes} in the .icua tensor layout.
+
+    ``keep_fp32`` also returns the fp32 arrays (by tensor id of the codes) for checkers.
+    """
+    out, raw = {}, {}
+    for tid, w in fp32_stream:
+        if isinstance(tid, tuple):
+            codes_id, sb_id = tid
+            if codes_id == L.TID_EMBED:
+                codes, scales = quantize_q8(w)
+            else:
+                codes, scales = quantize_q4s(w)
+            out[codes_id] = codes.tobytes()
+            out[sb_id] = scales.tobytes()
+            if keep_fp32:
+                raw[codes_id] = w
+        else:
+            out[tid] = np.ascontiguousarray(w, np.float32).tobytes()
+            if keep_fp32:
+                raw[tid] = w
+    return (out, raw) if keep_fp32 else out
+
+
+def write_icua(path: str, tensors: dict, fmt: int = L.FMT_Q4S) -> None:
+    """Writes an .icua file (ModelFile.swift:164-195 layout): 16 KiB header with magic, version 1,
+    format, tensor count and an (offset, size) u64 table; tensors 256-byte aligned; the file
+    padded to a multiple of 16 KiB."""
+    table = [(0, 0)] * L.TENSOR_COUNT
+    cursor = HEADER
+    layout = []
+    for tid in sorted(tensors):
+        data = tensors[tid]
+        cursor = (cursor + 255) & ~255
+        table[tid] = (cursor, len(data))
+        layout.append((cursor, data))
+        cursor += len(data)
+    total = (cursor + HEADER - 1) // HEADER * HEADER
+    with open(path, "wb") as f:
+        hdr = bytearray(HEADER)
+        struct.pack_into("<IIII", hdr, 0, MAGIC, 1, fmt, L.TENSOR_COUNT)
+        for i, (o, s) in enumerate(table):
+            struct.pack_into("<QQ", hdr, 16 + 16 * i, o, s)
+        f.write(hdr)
+        pos = HEADER
+        for off, data in layout:
+            if off > pos:
+                f.write(b"\0" * (off - pos))
+            f.write(data)
+            pos = off + len(data)
+        if total > pos:
+            f.write(b"\0" * (total - pos))
