@@ -26,16 +26,16 @@ sys.path.insert(0, ROOT)
 CTX = 4096
 SEED = 0
 METRIC = "q4 decode tokens/s (batch 1, 4K ctx)"
-H, FF, V, L = 2048, 6144, 151936, 28
+H, FF, V, NL = 2048, 6144, 151936, 28
 Q4_LAYER_BYTES = (4096 * 2048 + 2048 * 2048 + 12288 * 2048 + 2048 * 6144) * 9 // 16  # 0.5625 B / weight
 Q8_HEAD_BYTES = V * 2048 * 17 // 16                                                  # 1.0625 B / weight
-NORM_BYTES = (L * (2 * 2048 + 2 * 128) + 2048) * 4
-KV_BYTES_PER_POS = L * 8 * 128 * 2 * 2
+NORM_BYTES = (NL * (2 * 2048 + 2 * 128) + 2048) * 4
+KV_BYTES_PER_POS = NL * 8 * 128 * 2 * 2
 
 
 def step_bytes(ctx: int) -> int:
     """Algorithmic HBM bytes of one decode token at context ctx (weights + norms + KV read)."""
-    return L * Q4_LAYER_BYTES + Q8_HEAD_BYTES + NORM_BYTES + KV_BYTES_PER_POS * ctx
+    return NL * Q4_LAYER_BYTES + Q8_HEAD_BYTES + NORM_BYTES + KV_BYTES_PER_POS * ctx
 
 
 def peaks():
@@ -193,7 +193,7 @@ def run_ours(args):
                               "note": f"whole decode token: weights + norms + KV at ctx {int(ctx_mid)}; peak {peak_kind}"},
             "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 24, "d2h_bytes_per_step": 4,
                     "api": "icua_decode_step (host token in, host token out, synchronised per step)", "steps": KE},
-            "gpu_launches": K * (5 * L + 1),
+            "gpu_launches": K * (5 * NL + 2),
             "clocks": clk.summary(),
         }
     if dist is not None:
@@ -218,12 +218,11 @@ def lm_head_roofline(torch, L, peak):
     units[:, 1024:] = torch.tensor([0x1419], dtype=torch.int16, device="cuda").view(torch.uint8).repeat(32)
     x = torch.randn(k, device="cuda")
     y = torch.empty(n, device="cuda")
-    scratch = torch.zeros(L.lib().icua_gemv_scratch_bytes(L.FMT_Q8, n, k), dtype=torch.uint8, device="cuda")
     s = torch.cuda.current_stream()
 
     def run():
         L.check(L.lib().icua_gemv(L.FMT_Q8, n, k, C.c_void_p(w.data_ptr()), C.c_void_p(x.data_ptr()), 0,
-                                  C.c_void_p(y.data_ptr()), C.c_void_p(scratch.data_ptr()), C.c_void_p(s.cuda_stream)))
+                                  C.c_void_p(y.data_ptr()), C.c_void_p(s.cuda_stream)))
 
     for _ in range(5):
         run()
@@ -251,8 +250,8 @@ def cpu_baseline(path, steps: int = 3):
     import numpy as np
 
     rng = np.random.default_rng(5)
-    kc = [rng.standard_normal((sample_ctx, 8, 128), dtype=np.float32) for _ in range(L)]
-    vc = [rng.standard_normal((sample_ctx, 8, 128), dtype=np.float32) for _ in range(L)]
+    kc = [rng.standard_normal((sample_ctx, 8, 128), dtype=np.float32) for _ in range(NL)]
+    vc = [rng.standard_normal((sample_ctx, 8, 128), dtype=np.float32) for _ in range(NL)]
     model.inject_kv(kc, vc)
     model.decode_step(1)  # warm-up
     t1 = time.perf_counter()
@@ -284,7 +283,7 @@ def oracle_model_from_file(path):
                                get(LB.TID_EMBED_SB).view(np.float16).reshape(V, H // 32)),
          "final_norm": get(LB.TID_FINAL_NORM).view(np.float32)}
     shapes = {"wqkv": (4096, 2048), "wo": (2048, 2048), "wgu": (12288, 2048), "wd": (2048, 6144)}
-    for l in range(L):
+    for l in range(NL):
         for nm in ("attn_norm", "q_norm", "k_norm", "mlp_norm"):
             w[f"l{l}.{nm}"] = get(layer_tid(l, nm)).view(np.float32)
         for nm, (r, c) in shapes.items():

@@ -168,12 +168,11 @@ uint64_t icua_packed_bytes(int32_t fmt, int32_t n_rows, int32_t k);
 /* Repacks reference-layout host codes + scales into the device tile layout (host to host). */
 icua_status icua_pack_matrix(int32_t fmt, int32_t n_rows, int32_t k, const void* codes,
                              const uint16_t* scales, void* packed_out);
-/* y[n_rows] = W x on the device; x is fp32 [k] (x_dtype 0) or bf16 [k] (x_dtype 1).
- * scratch_dev must hold icua_gemv_scratch_bytes(); stream is a cudaStream_t or NULL. */
-uint64_t icua_gemv_scratch_bytes(int32_t fmt, int32_t n_rows, int32_t k);
+/* y[n_rows] = W x on the device (the decode GEMV kernel with a plain store epilogue); x is fp32 [k]
+ * (x_dtype 0) or bf16 [k] (x_dtype 1); k a multiple of 1024 up to 6144; stream is a cudaStream_t
+ * or NULL.  No scratch memory: every CTA owns whole 16-row tiles. */
 icua_status icua_gemv(int32_t fmt, int32_t n_rows, int32_t k, const void* packed_dev,
-                      const void* x_dev, int32_t x_dtype, float* y_dev, void* scratch_dev,
-                      void* stream);
+                      const void* x_dev, int32_t x_dtype, float* y_dev, void* stream);
 /* Bit-exact dequantization of a packed device matrix to fp32 row-major [n_rows, k]. */
 icua_status icua_dequant(int32_t fmt, int32_t n_rows, int32_t k, const void* packed_dev, float* out_dev,
                          void* stream);

@@ -70,8 +70,7 @@ PROTOTYPES = {
     "icua_session_position": (_I, [_P, _I, _IP]),
     "icua_packed_bytes": (C.c_uint64, [_I, _I, _I]),
     "icua_pack_matrix": (_I, [_I, _I, _I, _P, _P, _P]),
-    "icua_gemv_scratch_bytes": (C.c_uint64, [_I, _I, _I]),
-    "icua_gemv": (_I, [_I, _I, _I, _P, _P, _I, _P, _P, _P]),
+    "icua_gemv": (_I, [_I, _I, _I, _P, _P, _I, _P, _P]),
     "icua_dequant": (_I, [_I, _I, _I, _P, _P, _P]),
     "icua_quantize_q8": (_I, [_FP, _I, _I, _P, _P]),
     "icua_quantize_q4s": (_I, [_FP, _I, _I, _P, _P]),

@@ -4,22 +4,29 @@
 // cos/sin table, fp16 K/V write at `pos`, Shaders.swift:790-834) and k_attention (softmax over
 // the whole context in threadgroup memory, context <= 2048, Shaders.swift:1219-1289).
 //
-// Design (B200): one CTA per (kv head, split) pair, so the two query heads of a GQA group share
-// every K/V byte read.  The static positions [0, pos) of a split are streamed into a ring of
-// shared-memory stages with 1-D bulk copies; the first stages are requested before
-// griddepcontrol.wait (the cache rows do not depend on the previous kernel).  The new position
-// is computed in the CTA from the QKV projection output, rounded to the cache type exactly as it
-// is stored, and the last split folds it in.  Split results (running max, sum, output) are
-// combined by the last arriving CTA of each kv head in split order (deterministic); no spin
-// waits.  Context length is bounded only by the cache allocation.
+// Design (B200): the context of each kv head is split over n_split CTAs grouped in thread-block
+// clusters; each CTA handles the two query heads of its GQA group, so every K/V byte is read once.
+// Each warp streams its own contiguous run of cache rows through a ring of shared-memory slots
+// with 1-D bulk copies (the first slots are requested before griddepcontrol.wait: cache rows
+// [0, pos) do not depend on the previous kernel) and runs an online softmax in registers.  Warp
+// results meet in shared memory, CTA results meet across the cluster through distributed shared
+// memory, and each cluster writes one (max, sum, output) part that the o-proj GEMV folds in while
+// loading its input.  The new position is normalised, rotated and rounded to the cache type in the
+// CTA (as the reference reads it back from the fp16 cache) and folded in by the last split.  No
+// global atomics, fences or spin waits.  Context length is bounded only by the cache allocation.
 #pragma once
 #include "common.cuh"
+#include "gemv.cuh"
 
 namespace icua {
 
-constexpr int ATT_CH = 32;      // positions per stage
-constexpr int ATT_STAGES = 4;
-constexpr int ATT_PART = 4 + 2 * HD;  // m[2], l[2], o[2][128]
+constexpr int ATT_SLOT = 16;   // cache rows per ring slot (one MMA block)
+constexpr int ATT_NS = 2;      // ring slots per warp
+
+// KV rows are stored with their sixteen 16-byte chunks permuted by the row's position:
+// element d of position p lives at chunk (d / 8) ^ (p & 7).  Eight consecutive rows then cover
+// eight different bank groups, so ldmatrix reads from bulk-copied rows are conflict-free.
+__host__ __device__ __forceinline__ int kv_swz(int d, int pos) { return (((d >> 3) ^ (pos & 7)) << 3) | (d & 7); }
 
 template <typename KVT>
 struct AttnParams {
@@ -27,106 +34,159 @@ struct AttnParams {
     const float* q_norm;     // [128]
     const float* k_norm;     // [128]
     const float2* rope;      // [max_ctx][64] (cos, sin) per cache slot
-    KVT* kc;                 // this layer: [NKV][max_ctx][128]
+    KVT* kc;                 // this layer: [NKV][max_ctx][128] (swizzled rows)
     KVT* vc;
     int max_ctx;
-    int n_split;
-    float* attn_out;         // [2048]
-    float* part;             // scratch [NKV][n_split][ATT_PART]
-    unsigned* cnt;           // scratch [NKV]
+    int n_split;             // CTAs per kv head (multiple of the cluster size)
+    int cluster;             // CTAs per cluster
+    float* part;             // out: [NKV][n_split / cluster][ATT_PART]
     DevState* st;
 };
 
 template <typename KVT>
 struct AttnSmem {
-    static constexpr int stage_bytes = 2 * ATT_CH * HD * (int)sizeof(KVT);
+    static constexpr int row_bytes = HD * (int)sizeof(KVT);
+    static constexpr int slot_bytes = 2 * ATT_SLOT * row_bytes;   // K rows then V rows
+    static constexpr int ring_warp = ATT_NS * slot_bytes;
     static constexpr int ring_off = 0;
-    static constexpr int new_off = ATT_STAGES * stage_bytes;                 // K,V of the new position
-    static constexpr int q_off = new_off + 2 * HD * (int)sizeof(KVT);        // float q[2][128]
-    static constexpr int kv_off = q_off + 2 * HD * 4;                        // float k[128], v[128] scratch
-    static constexpr int sc_off = kv_off + 2 * HD * 4;                       // float sc[2][ATT_CH]
-    static constexpr int ml_off = sc_off + 2 * ATT_CH * 4;                   // float m[2], l[2], corr[2], red[8]
-    static constexpr int red_off = ml_off + 16 * 4;                          // float red[8][2][128]
-    static constexpr int bars_off = red_off + 8 * 2 * HD * 4;
-    static constexpr int total = bars_off + ATT_STAGES * 8 + 16;
+    static constexpr int new_off = 8 * ring_warp;                 // K, V rows of the new position
+    static constexpr int q_off = new_off + 2 * row_bytes;         // float q[2][128] (scaled)
+    static constexpr int wpart_off = q_off + 2 * HD * 4;          // float [8][ATT_PART]
+    static constexpr int cpart_off = wpart_off + 8 * ATT_PART * 4;  // float [ATT_PART]
+    static constexpr int bars_off = cpart_off + ATT_PART * 4;
+    static constexpr int total = bars_off + 8 * ATT_NS * 8;
 };
 
-// Processes `n` positions whose K rows start at Ks and V rows at Vs (row stride 128).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ float ld_dsmem(const float* local_ptr, uint32_t rank) {
+    uint32_t a = smem_u32(local_ptr), ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
 template <typename KVT>
-__device__ __forceinline__ void attn_chunk(const KVT* Ks, const KVT* Vs, int n, const float (&qr)[2][16], float* sc,
-                                           float* ml, float (&acc)[2][4]) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // scores: warp w covers positions 4w..4w+3; lane = (p_sub, dpart) with 16 dims per lane
+__device__ __forceinline__ void mma_kv(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void mma_kv<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    mma_16816(d, a, b0, b1);
+}
+template <>
+__device__ __forceinline__ void mma_kv<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <typename KVT>
+__device__ __forceinline__ uint32_t pack2(KVT lo, KVT hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(__half lo, __half hi) {
+    return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(__nv_bfloat16 lo, __nv_bfloat16 hi) {
+    return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+}
+
+// hi (part 0) or lo (part 1) of v in the cache type
+template <typename KVT>
+__device__ __forceinline__ KVT split_part(float v, int part) {
+    const KVT hi = float_to_kv<KVT>(v);
+    return part ? float_to_kv<KVT>(v - kv_to_float(hi)) : hi;
+}
+
+// Warp state of the online softmax: lane (g, t) tracks query head t & 1; o holds dims
+// 16*db + g (o[db][0..1], hi/lo columns) and 16*db + g + 8 (o[db][2..3]).
+struct AttnAcc {
+    float m, l;
+    float o[8][4];
+};
+
+// One block of up to 16 cache rows (rows [0, n) of a slot whose first row is position r0) with
+// tensor-core QK^T and PV.  Row addresses past n are clamped to row n-1 (finite data, p = 0).
+template <typename KVT>
+__device__ __forceinline__ void attn_block(uint32_t kslot, uint32_t vslot, int r0, int n, const uint32_t (&qb)[8][2],
+                                           AttnAcc& acc, int lane) {
+    constexpr int RB = HD * (int)sizeof(KVT);
+    const int g = lane >> 2, t = lane & 3;
+    // ---- scores S[16 rows][cols: h0 hi, h0 lo, h1 hi, h1 lo, dup x4] ----
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
     {
-        const int pp = warp * 4 + (lane >> 3), dp = lane & 7;
-        float s0 = 0.f, s1 = 0.f;
-        if (pp < n) {
-            const KVT* kr = Ks + pp * HD;
-            const uint4 ka = *reinterpret_cast<const uint4*>(kr + 8 * dp);
-            const uint4 kb = *reinterpret_cast<const uint4*>(kr + 64 + 8 * dp);
-            const KVT* ea = reinterpret_cast<const KVT*>(&ka);
-            const KVT* eb = reinterpret_cast<const KVT*>(&kb);
+        const int row = min((lane & 7) + ((lane >> 3) & 1) * 8, n - 1);
+        const int key = (r0 + row) & 7;
+        const uint32_t rowaddr = kslot + row * RB;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float k0 = kv_to_float(ea[i]), k1 = kv_to_float(eb[i]);
-                s0 = fmaf(qr[0][i], k0, s0);
-                s0 = fmaf(qr[0][8 + i], k1, s0);
-                s1 = fmaf(qr[1][i], k0, s1);
-                s1 = fmaf(qr[1][8 + i], k1, s1);
-            }
-        }
-        s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-        s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-        s0 += __shfl_xor_sync(0xffffffffu, s0, 4);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, 4);
-        if (dp == 0) {
-            sc[pp] = pp < n ? s0 : -INFINITY;
-            sc[ATT_CH + pp] = pp < n ? s1 : -INFINITY;
+        for (int kk = 0; kk < 8; ++kk) {
+            const int chunk = 2 * kk + (lane >> 4);
+            uint32_t a[4];
+            ldsm_x4(a, rowaddr + ((chunk ^ key) << 4));
+            mma_kv<KVT>(d, a, qb[kk][0], qb[kk][1]);
         }
     }
-    __syncthreads();
-    // online softmax: warp h handles query head h
-    if (warp < 2) {
-        const float v = sc[warp * ATT_CH + lane];
-        const float mc = warp_max(v);
-        const float m_old = ml[warp];
-        const float m_new = fmaxf(m_old, mc);
-        const float corr = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-        const float pv = (v == -INFINITY) ? 0.f : expf(v - m_new);
-        const float ps = warp_sum(pv);
-        sc[warp * ATT_CH + lane] = pv;
-        __syncwarp();
-        if (lane == 0) {
-            ml[warp] = m_new;
-            ml[2 + warp] = ml[2 + warp] * corr + ps;
-            ml[4 + warp] = corr;
-        }
-    }
-    __syncthreads();
-    // P.V: thread (dq = 4 dims, psub = position phase)
+    const bool va = g < n, vb = g + 8 < n;
+    const float sa = va ? d[0] + d[1] : -INFINITY;
+    const float sb = vb ? d[2] + d[3] : -INFINITY;
+    float mb = fmaxf(sa, sb);
+    mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 4));
+    mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 8));
+    mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 16));
+    const float mn = fmaxf(acc.m, mb);
+    const float corr = (acc.m == -INFINITY) ? 0.f : expf(acc.m - mn);
+    const float pa = va ? expf(sa - mn) : 0.f;
+    const float pb = vb ? expf(sb - mn) : 0.f;
+    acc.m = mn;
+    acc.l = fmaf(acc.l, corr, pa + pb);
+    // ---- P as the B operand: lane (g, t) needs rows 2t, 2t+1, 2t+8, 2t+9 of column g ----
+    const int hh = (g >> 1) & 1, part = g & 1;
+    const int src0 = (2 * t) * 4 + hh, src1 = (2 * t + 1) * 4 + hh;
+    const float p0 = __shfl_sync(0xffffffffu, pa, src0);
+    const float p1 = __shfl_sync(0xffffffffu, pa, src1);
+    const float p8 = __shfl_sync(0xffffffffu, pb, src0);
+    const float p9 = __shfl_sync(0xffffffffu, pb, src1);
+    const uint32_t pb0 = pack2<KVT>(split_part<KVT>(p0, part), split_part<KVT>(p1, part));
+    const uint32_t pb1 = pack2<KVT>(split_part<KVT>(p8, part), split_part<KVT>(p9, part));
+    // the O columns of this lane (2t, 2t+1) belong to head t & 1, whose running max this lane keeps
+    const float c = corr;
+    // ---- O[16 dims x 8 cols] += V^T[dims x rows] P[rows x cols], 8 blocks of 16 dims ----
     {
-        const int dq = tid & 31, ps = tid >> 5;
-        const float c0 = ml[4], c1 = ml[5];
+        const int row = min((lane & 7) + ((lane >> 4) & 1) * 8, n - 1);
+        const int key = (r0 + row) & 7;
+        const uint32_t rowaddr = vslot + row * RB;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            acc[0][i] *= c0;
-            acc[1][i] *= c1;
-        }
-        for (int pp = ps; pp < n; pp += 8) {
-            const uint2 vv = *reinterpret_cast<const uint2*>(Vs + pp * HD + 4 * dq);
-            const KVT* e = reinterpret_cast<const KVT*>(&vv);
-            const float p0 = sc[pp], p1 = sc[ATT_CH + pp];
+        for (int db = 0; db < 8; ++db) {
+            const int chunk = 2 * db + ((lane >> 3) & 1);
+            uint32_t a[4];
+            ldsm_x4_trans(a, rowaddr + ((chunk ^ key) << 4));
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float vf = kv_to_float(e[i]);
-                acc[0][i] = fmaf(p0, vf, acc[0][i]);
-                acc[1][i] = fmaf(p1, vf, acc[1][i]);
-            }
+            for (int i = 0; i < 4; ++i) acc.o[db][i] *= c;
+            mma_kv<KVT>(acc.o[db], a, pb0, pb1);
         }
     }
-    __syncthreads();
 }
 
 template <typename KVT>
@@ -134,196 +194,207 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
     extern __shared__ __align__(128) uint8_t smem[];
     using S = AttnSmem<KVT>;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int S_ = p.n_split;
-    const int h = blockIdx.x / S_, j = blockIdx.x % S_;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bars_off);
+    const int NSP = p.n_split;
+    const int h = blockIdx.x / NSP, j = blockIdx.x % NSP;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bars_off) + warp * ATT_NS;
+    uint8_t* ring = smem + S::ring_off + warp * S::ring_warp;
     float* qs = reinterpret_cast<float*>(smem + S::q_off);
-    float* kvs = reinterpret_cast<float*>(smem + S::kv_off);
-    float* sc = reinterpret_cast<float*>(smem + S::sc_off);
-    float* ml = reinterpret_cast<float*>(smem + S::ml_off);
-    float* red = reinterpret_cast<float*>(smem + S::red_off);
+    float* wpart = reinterpret_cast<float*>(smem + S::wpart_off);
+    float* cpart = reinterpret_cast<float*>(smem + S::cpart_off);
     KVT* knew = reinterpret_cast<KVT*>(smem + S::new_off);
     KVT* vnew = knew + HD;
 
-    // The cache position was written by a kernel at least two launches earlier (the commit of
-    // the previous step), so it can be read before griddepcontrol.wait.
+    // The cache position was written by a kernel at least two launches earlier (the commit or
+    // the prompt cursor advance of the previous step), so it can be read before the wait.
     const int pos = *(volatile int*)&p.st->pos;
     const long long Ls = pos;
-    const int p0 = (int)(Ls * j / S_), p1 = (int)(Ls * (j + 1) / S_);
-    const int n_chunks = (p1 - p0 + ATT_CH - 1) / ATT_CH;
+    const int p0 = (int)(Ls * j / NSP), p1 = (int)(Ls * (j + 1) / NSP);
+    const int a = p0 + (int)((long long)(p1 - p0) * warp / 8), b = p0 + (int)((long long)(p1 - p0) * (warp + 1) / 8);
+    const int n_chunks = (b - a + ATT_SLOT - 1) / ATT_SLOT;
     const KVT* kbase = p.kc + (long long)h * p.max_ctx * HD;
     const KVT* vbase = p.vc + (long long)h * p.max_ctx * HD;
 
     auto issue = [&](int c) {
-        const int a = p0 + c * ATT_CH;
-        const int n = min(ATT_CH, p1 - a);
+        const int r0 = a + c * ATT_SLOT;
+        const int n = min(ATT_SLOT, b - r0);
         const uint32_t bytes = (uint32_t)(n * HD * sizeof(KVT));
-        uint8_t* st = smem + S::ring_off + (c % ATT_STAGES) * S::stage_bytes;
-        uint64_t* bar = &bars[c % ATT_STAGES];
+        uint8_t* dst = ring + (c % ATT_NS) * S::slot_bytes;
+        uint64_t* bar = &bars[c % ATT_NS];
         mbar_expect_tx(bar, 2 * bytes);
-        bulk_g2s(st, kbase + (long long)a * HD, bytes, bar);
-        bulk_g2s(st + ATT_CH * HD * sizeof(KVT), vbase + (long long)a * HD, bytes, bar);
+        bulk_g2s(dst, kbase + (long long)r0 * HD, bytes, bar);
+        bulk_g2s(dst + ATT_SLOT * S::row_bytes, vbase + (long long)r0 * HD, bytes, bar);
     };
-    if (tid == 0) {
-        for (int s = 0; s < ATT_STAGES; ++s) mbar_init(&bars[s], 1);
+    if (lane == 0) {
+        for (int s = 0; s < ATT_NS; ++s) mbar_init(&bars[s], 1);
         fence_mbar_init();
-        for (int c = 0; c < min(ATT_STAGES, n_chunks); ++c) issue(c);
+        for (int c = 0; c < min(ATT_NS, n_chunks); ++c) issue(c);
     }
-    __syncthreads();
+    // norm weights and this position's rotation are inputs that do not depend on the producer
+    float nw[4] = {1.f, 1.f, 1.f, 1.f};
+    float2 cs4[4];
+    if (warp < 3) {
+        const float4 w4 = *reinterpret_cast<const float4*>((warp < 2 ? p.q_norm : p.k_norm) + 4 * lane);
+        nw[0] = w4.x; nw[1] = w4.y; nw[2] = w4.z; nw[3] = w4.w;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) cs4[e] = p.rope[(long long)pos * 64 + 4 * (lane & 15) + e];
+    }
+    __syncwarp();
 
     pdl_wait();
-    pdl_launch_dependents();
 
-    if (*(volatile int*)&p.st->done) {
-        for (int c = 0; c < min(ATT_STAGES, n_chunks); ++c) mbar_wait_bounded(&bars[c], 0);
+    if (*(volatile int*)&p.st->done) {  // uniform over the grid: no CTA reaches the cluster barriers
+        pdl_launch_dependents();
+        if (lane == 0)
+            for (int c = 0; c < min(ATT_NS, n_chunks); ++c) mbar_wait_bounded(&bars[c], 0);
         return;
     }
 
-    // ---- q/k norm + RoPE for the new position (heads 2h, 2h+1 and kv head h) ----------------
-    {
-        // threads 0..127: element tid of q0, q1, k; threads 128..255: v
-        float q0 = 0.f, q1 = 0.f, kk = 0.f;
-        if (tid < HD) {
-            q0 = p.qkv[(2 * h) * HD + tid];
-            q1 = p.qkv[(2 * h + 1) * HD + tid];
-            kk = p.qkv[2048 + h * HD + tid];
-            float a = warp_sum(q0 * q0), b = warp_sum(q1 * q1), c = warp_sum(kk * kk);
-            if (lane == 0) {
-                red[warp * 3 + 0] = a;
-                red[warp * 3 + 1] = b;
-                red[warp * 3 + 2] = c;
+    // ---- q/k norm + RoPE for the new position: warp 0/1 -> q heads 2h, 2h+1, warp 2 -> k, 3 -> v ----
+    if (warp < 4) {
+        const int base = warp < 2 ? (2 * h + warp) * HD : (warp == 2 ? 2048 + h * HD : 3072 + h * HD);
+        const float4 x4 = *reinterpret_cast<const float4*>(p.qkv + base + 4 * lane);
+        float x[4] = {x4.x, x4.y, x4.z, x4.w};
+        if (warp < 3) {
+            const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
+            const float r = 1.0f / sqrtf(ss / (float)HD + EPS);
+            float y[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) x[e] = x[e] * r * nw[e];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
+                const float2 cs = cs4[e];
+                y[e] = lane < 16 ? x[e] * cs.x - partner * cs.y : x[e] * cs.x + partner * cs.y;
+            }
+            if (warp < 2) {
+                const float sc = 0.08838834764831845f;  // 1 / sqrt(128)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) qs[warp * HD + 4 * lane + e] = y[e] * sc;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) knew[kv_swz(4 * lane + e, pos)] = float_to_kv<KVT>(y[e]);
             }
         } else {
-            const float v = p.qkv[3072 + h * HD + (tid - HD)];
-            const KVT vr = float_to_kv<KVT>(v);
-            vnew[tid - HD] = vr;
-        }
-        __syncthreads();
-        if (tid < HD) {
-            float a = 0.f, b = 0.f, c = 0.f;
 #pragma unroll
-            for (int w2 = 0; w2 < 4; ++w2) {
-                a += red[w2 * 3 + 0];
-                b += red[w2 * 3 + 1];
-                c += red[w2 * 3 + 2];
-            }
-            const float ra = 1.0f / sqrtf(a / (float)HD + EPS);
-            const float rb = 1.0f / sqrtf(b / (float)HD + EPS);
-            const float rc = 1.0f / sqrtf(c / (float)HD + EPS);
-            const float qn = p.q_norm[tid], kn = p.k_norm[tid];
-            qs[tid] = q0 * ra * qn;
-            qs[HD + tid] = q1 * rb * qn;
-            kvs[tid] = kk * rc * kn;
+            for (int e = 0; e < 4; ++e) vnew[kv_swz(4 * lane + e, pos)] = float_to_kv<KVT>(x[e]);
         }
-        __syncthreads();
-        if (tid < 64) {
-            const float2 cs = p.rope[(long long)pos * 64 + tid];
-            const float scale = 0.08838834764831845f;  // 1 / sqrt(128)
-            float a = qs[tid], b = qs[tid + 64];
-            const float a0 = (a * cs.x - b * cs.y) * scale, b0 = (b * cs.x + a * cs.y) * scale;
-            a = qs[HD + tid];
-            b = qs[HD + tid + 64];
-            const float a1 = (a * cs.x - b * cs.y) * scale, b1 = (b * cs.x + a * cs.y) * scale;
-            a = kvs[tid];
-            b = kvs[tid + 64];
-            const KVT ka = float_to_kv<KVT>(a * cs.x - b * cs.y);
-            const KVT kb = float_to_kv<KVT>(b * cs.x + a * cs.y);
-            __syncwarp(0xffffffffu);
-            qs[tid] = a0;
-            qs[tid + 64] = b0;
-            qs[HD + tid] = a1;
-            qs[HD + tid + 64] = b1;
-            knew[tid] = ka;
-            knew[tid + 64] = kb;
-        }
-        if (tid < 2) {
-            ml[tid] = -INFINITY;
-            ml[2 + tid] = 0.f;
-        }
-        __syncthreads();
-        if (j == 0 && tid < HD) {
-            p.kc[((long long)h * p.max_ctx + pos) * HD + tid] = knew[tid];
-            p.vc[((long long)h * p.max_ctx + pos) * HD + tid] = vnew[tid];
-        }
+    }
+    __syncthreads();
+    pdl_launch_dependents();  // after the latency-bound q/k/v loads
+    if (j == 0 && tid < HD) {  // append the new row (already in the swizzled order)
+        p.kc[((long long)h * p.max_ctx + pos) * HD + tid] = knew[tid];
+        p.vc[((long long)h * p.max_ctx + pos) * HD + tid] = vnew[tid];
     }
 
-    // per-lane query registers for the score phase: dims {8dp..8dp+7} and {64+8dp..}
-    float qr[2][16];
+    // ---- per-warp flash-decode over rows [a, b) ------------------------------------------------
+    // B operand of QK^T: columns (h0 hi, h0 lo, h1 hi, h1 lo) repeated; lane (g, t) holds rows
+    // (dims) 2t, 2t+1, 2t+8, 2t+9 of column g for each 16-dim step.
+    uint32_t qb[8][2];
     {
-        const int dp = lane & 7;
+        const int g = lane >> 2, t = lane & 3;
+        const int hh = (g >> 1) & 1, part = g & 1;
+        const float* q = qs + hh * HD;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            qr[0][i] = qs[8 * dp + i];
-            qr[0][8 + i] = qs[64 + 8 * dp + i];
-            qr[1][i] = qs[HD + 8 * dp + i];
-            qr[1][8 + i] = qs[HD + 64 + 8 * dp + i];
+        for (int kk = 0; kk < 8; ++kk) {
+            const int d0 = 16 * kk + 2 * t;
+            qb[kk][0] = pack2<KVT>(split_part<KVT>(q[d0], part), split_part<KVT>(q[d0 + 1], part));
+            qb[kk][1] = pack2<KVT>(split_part<KVT>(q[d0 + 8], part), split_part<KVT>(q[d0 + 9], part));
         }
     }
-    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    bool failed = false;
+    AttnAcc acc;
+    acc.m = -INFINITY;
+    acc.l = 0.f;
+#pragma unroll
+    for (int db = 0; db < 8; ++db)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc.o[db][i] = 0.f;
     for (int c = 0; c < n_chunks; ++c) {
-        const int slot = c % ATT_STAGES;
-        if (!mbar_wait_bounded(&bars[slot], (uint32_t)((c / ATT_STAGES) & 1))) {
-            if (tid == 0) atomicOr(&p.st->error, ERR_WAIT_ATTN);
-            failed = true;
+        const int slot = c % ATT_NS;
+        if (!mbar_wait_bounded(&bars[slot], (uint32_t)((c / ATT_NS) & 1))) {
+            if (lane == 0) atomicOr(&p.st->error, ERR_WAIT_ATTN);
+            break;  // keep going to the cluster barriers with what we have
         }
-        if (__syncthreads_or(failed)) {
-            failed = true;
-            break;
-        }
-        const KVT* Ks = reinterpret_cast<const KVT*>(smem + S::ring_off + slot * S::stage_bytes);
-        const KVT* Vs = Ks + ATT_CH * HD;
-        const int n = min(ATT_CH, p1 - (p0 + c * ATT_CH));
-        attn_chunk<KVT>(Ks, Vs, n, qr, sc, ml, acc);
-        if (tid == 0 && c + ATT_STAGES < n_chunks) {
+        const uint32_t kslot = smem_u32(ring + slot * S::slot_bytes);
+        const int r0 = a + c * ATT_SLOT;
+        attn_block<KVT>(kslot, kslot + ATT_SLOT * S::row_bytes, r0, min(ATT_SLOT, b - r0), qb, acc, lane);
+        __syncwarp();
+        if (lane == 0 && c + ATT_NS < n_chunks) {
             fence_proxy_async_smem();
-            issue(c + ATT_STAGES);
+            issue(c + ATT_NS);
         }
     }
-    if (failed) return;
-    if (j == S_ - 1) attn_chunk<KVT>(knew, vnew, 1, qr, sc, ml, acc);
+    if (j == NSP - 1 && warp == 7) {
+        const uint32_t kn = smem_u32(knew);
+        attn_block<KVT>(kn, kn + S::row_bytes, pos, 1, qb, acc, lane);
+    }
 
-    // reduce the 8 position phases and write this split's partial
+    // warp result: lanes with t = 0 / 1 own head 0 / 1
     {
-        const int dq = tid & 31, ps = tid >> 5;
+        const int g = lane >> 2, t = lane & 3;
+        float l = acc.l;
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        float* wp = wpart + warp * ATT_PART;
+        if (t < 2) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            red[(ps * 2 + 0) * HD + 4 * dq + i] = acc[0][i];
-            red[(ps * 2 + 1) * HD + 4 * dq + i] = acc[1][i];
+            for (int db = 0; db < 8; ++db) {
+                wp[4 + t * HD + 16 * db + g] = acc.o[db][0] + acc.o[db][1];
+                wp[4 + t * HD + 16 * db + g + 8] = acc.o[db][2] + acc.o[db][3];
+            }
+            if (g == 0) {
+                wp[t] = acc.m;
+                wp[2 + t] = l;
+            }
         }
     }
     __syncthreads();
-    float* part = p.part + ((long long)h * S_ + j) * ATT_PART;
+    // CTA combine of the 8 warps: thread (hh, d)
     {
         const int hh = tid >> 7, d = tid & 127;
-        float o = 0.f;
-#pragma unroll
-        for (int s = 0; s < 8; ++s) o += red[(s * 2 + hh) * HD + d];
-        part[4 + hh * HD + d] = o;
-        if (tid < 4) part[tid] = ml[tid];
-    }
-    __threadfence();
-    __syncthreads();
-    __shared__ unsigned last_s;
-    if (tid == 0) last_s = atomicAdd(&p.cnt[h], 1u);
-    __syncthreads();
-    if (last_s != (unsigned)(S_ - 1)) return;
-    __threadfence();
-    {
-        const int hh = tid >> 7, d = tid & 127;
-        const float* base = p.part + (long long)h * S_ * ATT_PART;
         float M = -INFINITY;
-        for (int s = 0; s < S_; ++s) M = fmaxf(M, __ldcg(&base[s * ATT_PART + hh]));
+#pragma unroll
+        for (int w2 = 0; w2 < 8; ++w2) M = fmaxf(M, wpart[w2 * ATT_PART + hh]);
         float Lsum = 0.f, O = 0.f;
-        for (int s = 0; s < S_; ++s) {
-            const float m = __ldcg(&base[s * ATT_PART + hh]);
-            const float f = (m == -INFINITY) ? 0.f : expf(m - M);
-            Lsum = fmaf(__ldcg(&base[s * ATT_PART + 2 + hh]), f, Lsum);
-            O = fmaf(__ldcg(&base[s * ATT_PART + 4 + hh * HD + d]), f, O);
+#pragma unroll
+        for (int w2 = 0; w2 < 8; ++w2) {
+            const float mw = wpart[w2 * ATT_PART + hh];
+            const float f = (mw == -INFINITY) ? 0.f : expf(mw - M);
+            Lsum = fmaf(wpart[w2 * ATT_PART + 2 + hh], f, Lsum);
+            O = fmaf(wpart[w2 * ATT_PART + 4 + hh * HD + d], f, O);
         }
-        p.attn_out[(2 * h + hh) * HD + d] = O / Lsum;
-        if (tid == 0) p.cnt[h] = 0;
+        cpart[4 + hh * HD + d] = O;
+        if (d == 0) {
+            cpart[hh] = M;
+            cpart[2 + hh] = Lsum;
+        }
     }
+    // cluster combine through distributed shared memory; every CTA reaches both barriers
+    cluster_sync_all();
+    {
+        const int CL = p.cluster;
+        const uint32_t rank = cluster_ctarank();
+        const int per = (2 * HD) / CL;  // outputs combined by this CTA
+        float* out = p.part + ((long long)h * (NSP / CL) + j / CL) * ATT_PART;
+        if (tid < per) {
+            const int idx = rank * per + tid, hh = idx >> 7, d = idx & 127;
+            float M = -INFINITY;
+            for (int q = 0; q < CL; ++q) M = fmaxf(M, ld_dsmem(&cpart[hh], q));
+            float Lsum = 0.f, O = 0.f;
+            for (int q = 0; q < CL; ++q) {
+                const float mq = ld_dsmem(&cpart[hh], q);
+                const float f = (mq == -INFINITY) ? 0.f : expf(mq - M);
+                Lsum = fmaf(ld_dsmem(&cpart[2 + hh], q), f, Lsum);
+                O = fmaf(ld_dsmem(&cpart[4 + hh * HD + d], q), f, O);
+            }
+            out[4 + hh * HD + d] = O;
+            if (d == 0) {
+                out[hh] = M;
+                out[2 + hh] = Lsum;
+            }
+        }
+    }
+    cluster_sync_all();  // peers may still be reading this CTA's shared memory
 }
 
 }  // namespace icua

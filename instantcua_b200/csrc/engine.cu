@@ -44,8 +44,9 @@ thread_local std::string g_error;
 struct Matrix {
     uint8_t* dev = nullptr;
     int fmt = 0, n_rows = 0, k = 0;
-    long long n_units = 0;
-    int slot_units = 1, n_slots = 1;
+    int n_tiles = 0, grid = 0;
+    bool stream = false;      // streaming (ring) path; otherwise all tiles of a CTA in one copy
+    int n_slots = 1, chunk = 1;
     size_t smem = 0;
 };
 
@@ -74,8 +75,8 @@ struct Session {
 struct icua_engine {
     icua_config cfg{};
     int n_sm = 0;
-    int n_workers = 0;
-    int att_split = 1;
+    int att_split = 16;   // CTAs per kv head in the decode attention
+    int att_cluster = 8;  // CTAs per cluster (att_split / att_cluster parts per kv head)
     cudaStream_t stream = nullptr;
     std::string err;
     bool failed = false;
@@ -91,14 +92,10 @@ struct icua_engine {
     float* step_logits = nullptr;
     float* step_logits_host = nullptr;
     int step_logits_cap = 0;
-    // scratch
-    float* partials = nullptr;
-    unsigned* tile_cnt = nullptr;
-    float* att_part = nullptr;
-    unsigned* att_cnt = nullptr;
-    float* cta_best_v = nullptr;
+    // intermediate results passed between kernels of a step
+    float* att_part = nullptr;    // attention (max, sum, output) parts per kv head
+    float* cta_best_v = nullptr;  // lm_head per-CTA argmax partials
     int* cta_best_i = nullptr;
-    unsigned* cta_done = nullptr;
     std::vector<Session> sessions;
     std::vector<void*> allocations;
     int eos0 = 151645, eos1 = 151643, stop_on_eos = 1;
@@ -138,33 +135,27 @@ icua_status dalloc_t(icua_engine* eng, T** p, size_t count) {
     return dalloc(eng, reinterpret_cast<void**>(p), count * sizeof(T));
 }
 
-int kv_elem_bytes(const icua_engine* e) { return 2; }
-
-void ring_geometry(int fmt, long long n_units, int n_workers, int& su, int& ns) {
-    const int ub = unit_bytes(fmt);
-    const long long R = (n_units + n_workers - 1) / n_workers;
-    if (R * ub <= 16384) {
-        ns = (int)std::min<long long>(4, std::max<long long>(R, 1));
-        su = (int)((R + ns - 1) / ns);
-        if (su < 1) su = 1;
-    } else {
-        su = std::max(1, 4096 / ub);
-        ns = 3;
-    }
-}
-
-void setup_matrix(Matrix& m, int fmt, int n_rows, int k, int n_workers) {
+// Grid, path and shared memory of a GEMV: CTAs own whole 16-row tiles, each warp one K slice of
+// every tile.  Up to SMALL_MAX_TILES tiles per CTA the whole weight slice of a warp is one bulk
+// copy requested before the kernel waits on its producer; longer matrices stream one tile per
+// ring slot.
+void setup_matrix(Matrix& m, int fmt, int n_rows, int k, int n_sm) {
     m.fmt = fmt;
     m.n_rows = n_rows;
     m.k = k;
-    m.n_units = (long long)(n_rows / 16) * (k / 64);
-    ring_geometry(fmt, m.n_units, n_workers, m.slot_units, m.n_slots);
-    GemvSmem L{k, m.n_slots, m.slot_units, unit_bytes(fmt)};
-    m.smem = (size_t)L.total();
+    m.n_tiles = n_rows / 16;
+    m.grid = std::min(n_sm, m.n_tiles);
+    const int tpc = gemv_tiles_per_cta(m.n_tiles, m.grid);
+    const int nw = fmt_slices(fmt), ku = k / 64 / nw;
+    m.stream = fmt == FMT_Q8 || tpc > SMALL_MAX_TILES;  // q8 kernels are built for the streaming path only
+    m.chunk = m.stream ? 1 : tpc;
+    m.n_slots = m.stream ? 2 : 1;
+    GemvSmem L{k, nw, m.n_slots, m.chunk, unit_bytes(fmt), ku, tpc, 0};
+    m.smem = (size_t)L.total();  // without the RMSNorm weight copy; launch_gemv adds it
 }
 
-template <typename Kern, typename P>
-cudaError_t launch(Kern kernel, int grid, int block, size_t smem, cudaStream_t s, const P& params, bool pdl) {
+template <typename Kern, typename... A>
+cudaError_t launch(Kern kernel, int grid, int block, size_t smem, cudaStream_t s, bool pdl, A... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(block);
@@ -175,31 +166,64 @@ cudaError_t launch(Kern kernel, int grid, int block, size_t smem, cudaStream_t s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <typename Kern, typename P>
+cudaError_t launch_cluster(Kern kernel, int grid, int cluster, int block, size_t smem, cudaStream_t s, const P& params) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, kernel, params);
 }
 
-template <int FMT, int EPI>
-cudaError_t launch_gemv(icua_engine* e, const Matrix& m, const GemvParams& p, cudaStream_t s) {
-    return launch(gemv_kernel<FMT, EPI>, e->n_sm, 256, m.smem, s, p, true);
+template <int FMT, int EPI, int KMAX, bool STREAM, int IN>
+cudaError_t launch_gemv(const Matrix& m, const GemvParams& p, cudaStream_t s, bool pdl = true) {
+    const int nt = fmt_slices(FMT) * 32;
+    const size_t smem = m.smem + (p.norm_w != nullptr ? (size_t)m.k * 4 : 0);
+    if (m.stream != STREAM || p.in_mode != IN) return cudaErrorInvalidValue;
+    return launch(gemv_kernel<FMT, EPI, KMAX, STREAM, IN>, m.grid, nt, smem, s, pdl, p);
 }
-
-bool g_attrs_set[16] = {false};
 
 cudaError_t set_smem_attrs() {
     static bool done = false;
     if (done) return cudaSuccess;
     const int big = 220 * 1024;
     cudaError_t e;
-#define SETA(K)                                                                     \
-    e = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, big); \
+    // Every kernel asks for the largest shared-memory carveout: an SM configured for a kernel
+    // with a small carveout cannot take the next kernel's CTAs until it drains, which would defeat
+    // programmatic dependent launch (the next kernel's weight prefetch overlapping this one).
+#define SETA(K)                                                                                           \
+    e = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, big);                       \
+    if (e != cudaSuccess) return e;                                                                      \
+    e = cudaFuncSetAttribute(K, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared); \
     if (e != cudaSuccess) return e;
-    SETA((gemv_kernel<FMT_Q4S, EPI_STORE>));
-    SETA((gemv_kernel<FMT_Q4S, EPI_RESID>));
-    SETA((gemv_kernel<FMT_Q4S, EPI_SWIGLU>));
-    SETA((gemv_kernel<FMT_Q8, EPI_LOGITS>));
-    SETA((gemv_kernel<FMT_Q8, EPI_STORE>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_STORE, 2048, false, IN_F32>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_STORE, 2048, false, IN_EMBED>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_RESID, 2048, false, IN_ATTN>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_SWIGLU, 2048, false, IN_F32>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_RESID, 6144, false, IN_F32>));
+    SETA((gemv_kernel<FMT_Q8, EPI_LOGITS, 2048, true, IN_F32>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_STORE, 2048, false, IN_BF16>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_STORE, 6144, false, IN_F32>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_STORE, 6144, false, IN_BF16>));
+    SETA((gemv_kernel<FMT_Q8, EPI_STORE, 2048, true, IN_F32>));
+    SETA((gemv_kernel<FMT_Q8, EPI_STORE, 2048, true, IN_BF16>));
     SETA((attn_decode_kernel<__half>));
     SETA((attn_decode_kernel<__nv_bfloat16>));
+    SETA(commit_kernel);
+    SETA(advance_kernel);
 #undef SETA
     done = true;
     return cudaSuccess;
@@ -208,14 +232,14 @@ cudaError_t set_smem_attrs() {
 GemvParams base_params(icua_engine* e, const Matrix& m) {
     GemvParams p{};
     p.w = m.dev;
-    p.n_units = m.n_units;
     p.n_rows = m.n_rows;
     p.k = m.k;
     p.upt = m.k / 64;
-    p.slot_units = m.slot_units;
+    p.n_tiles = m.n_tiles;
     p.n_slots = m.n_slots;
-    p.partials = e->partials;
-    p.tile_cnt = e->tile_cnt;
+    p.chunk = m.chunk;
+    p.embed = e->embed.dev;
+    p.embed_tiles = e->embed.n_tiles;
     return p;
 }
 
@@ -236,8 +260,10 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.x_resid = e->x;
         p.out = e->qkv;
         p.st = S.st;
-        if ((err = launch_gemv<FMT_Q4S, EPI_STORE>(e, ly.qkv, p, e->stream)) != cudaSuccess) return err;
-        // 2. QK norm + RoPE + KV append + split-K attention
+        err = (l == 0) ? launch_gemv<FMT_Q4S, EPI_STORE, 2048, false, IN_EMBED>(ly.qkv, p, e->stream)
+                       : launch_gemv<FMT_Q4S, EPI_STORE, 2048, false, IN_F32>(ly.qkv, p, e->stream);
+        if (err != cudaSuccess) return err;
+        // 2. QK norm + RoPE + KV append + split-K attention (clusters combine the splits)
         const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
         if (e->cfg.kv_dtype == ICUA_KV_BF16) {
             AttnParams<__nv_bfloat16> a{};
@@ -249,12 +275,11 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
             a.vc = reinterpret_cast<__nv_bfloat16*>(S.vc) + kv_layer * l;
             a.max_ctx = e->cfg.max_context;
             a.n_split = e->att_split;
-            a.attn_out = e->attn;
+            a.cluster = e->att_cluster;
             a.part = e->att_part;
-            a.cnt = e->att_cnt;
             a.st = S.st;
-            err = launch(attn_decode_kernel<__nv_bfloat16>, NKV * e->att_split, 256, AttnSmem<__nv_bfloat16>::total,
-                         e->stream, a, true);
+            err = launch_cluster(attn_decode_kernel<__nv_bfloat16>, NKV * e->att_split, e->att_cluster, 256,
+                                 AttnSmem<__nv_bfloat16>::total, e->stream, a);
         } else {
             AttnParams<__half> a{};
             a.qkv = e->qkv;
@@ -265,21 +290,21 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
             a.vc = reinterpret_cast<__half*>(S.vc) + kv_layer * l;
             a.max_ctx = e->cfg.max_context;
             a.n_split = e->att_split;
-            a.attn_out = e->attn;
+            a.cluster = e->att_cluster;
             a.part = e->att_part;
-            a.cnt = e->att_cnt;
             a.st = S.st;
-            err = launch(attn_decode_kernel<__half>, NKV * e->att_split, 256, AttnSmem<__half>::total, e->stream, a,
-                         true);
+            err = launch_cluster(attn_decode_kernel<__half>, NKV * e->att_split, e->att_cluster, 256,
+                                 AttnSmem<__half>::total, e->stream, a);
         }
         if (err != cudaSuccess) return err;
         // 3. o-proj + residual
         p = base_params(e, ly.o);
-        p.in_mode = IN_F32;
-        p.x = e->attn;
+        p.in_mode = IN_ATTN;
+        p.att_part = e->att_part;
+        p.att_parts = e->att_split / e->att_cluster;
         p.x_resid = e->x;
         p.st = S.st;
-        if ((err = launch_gemv<FMT_Q4S, EPI_RESID>(e, ly.o, p, e->stream)) != cudaSuccess) return err;
+        if ((err = launch_gemv<FMT_Q4S, EPI_RESID, 2048, false, IN_ATTN>(ly.o, p, e->stream)) != cudaSuccess) return err;
         // 4. RMSNorm + gate/up + SwiGLU
         p = base_params(e, ly.gu);
         p.in_mode = IN_F32;
@@ -287,7 +312,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.norm_w = ly.mlp_norm;
         p.out = e->h;
         p.st = S.st;
-        if ((err = launch_gemv<FMT_Q4S, EPI_SWIGLU>(e, ly.gu, p, e->stream)) != cudaSuccess) return err;
+        if ((err = launch_gemv<FMT_Q4S, EPI_SWIGLU, 2048, false, IN_F32>(ly.gu, p, e->stream)) != cudaSuccess) return err;
         // 5. down + residual (+ DeepStack rows after layers 0..2 while prefilling visual rows)
         p = base_params(e, ly.d);
         p.in_mode = IN_F32;
@@ -295,7 +320,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.x_resid = e->x;
         p.deepstack = (l < 3) ? e->deepstack[l] : nullptr;
         p.st = S.st;
-        if ((err = launch_gemv<FMT_Q4S, EPI_RESID>(e, ly.d, p, e->stream)) != cudaSuccess) return err;
+        if ((err = launch_gemv<FMT_Q4S, EPI_RESID, 6144, false, IN_F32>(ly.d, p, e->stream)) != cudaSuccess) return err;
     }
     return cudaSuccess;
 }
@@ -308,11 +333,12 @@ cudaError_t record_head(icua_engine* e, Session& S) {
     p.logits = e->logits;
     p.cta_best_v = e->cta_best_v;
     p.cta_best_i = e->cta_best_i;
-    p.cta_done = e->cta_done;
-    p.out_tokens = S.out_tokens;
     p.step_logits = e->step_logits;
     p.st = S.st;
-    return launch_gemv<FMT_Q8, EPI_LOGITS>(e, e->embed, p, e->stream);
+    cudaError_t err = launch_gemv<FMT_Q8, EPI_LOGITS, 2048, true, IN_F32>(e->embed, p, e->stream);
+    if (err != cudaSuccess) return err;
+    return launch(commit_kernel, 1, 256, 0, e->stream, true, (const float*)e->cta_best_v, (const int*)e->cta_best_i,
+                  e->embed.grid, S.out_tokens, S.st);
 }
 
 icua_status build_graph(icua_engine* eng, Session& S, int kind, cudaGraphExec_t* out) {
@@ -322,7 +348,7 @@ icua_status build_graph(icua_engine* eng, Session& S, int kind, cudaGraphExec_t*
     cudaError_t err = cudaSuccess;
     if (kind == 0) {
         err = record_layers(eng, S);
-        if (err == cudaSuccess) err = launch(advance_kernel, 1, 32, 0, eng->stream, S.st, true);
+        if (err == cudaSuccess) err = launch(advance_kernel, 1, 32, 0, eng->stream, true, S.st);
     } else {
         const int n = kind == 1 ? 1 : eng->cfg.steps_per_graph;
         for (int i = 0; i < n && err == cudaSuccess; ++i) {
@@ -454,7 +480,7 @@ icua_status upload_f32(icua_engine* eng, float** dst, const std::vector<uint8_t>
 
 icua_status upload_matrix(icua_engine* eng, Matrix& m, int fmt, int rows, int k, const std::vector<uint8_t>& codes,
                           const std::vector<uint8_t>& sb, const int* row_map) {
-    setup_matrix(m, fmt, rows, k, eng->n_workers);
+    setup_matrix(m, fmt, rows, k, eng->n_sm);
     const size_t bytes = icua_packed_bytes(fmt, rows, k);
     std::vector<uint8_t> packed(bytes);
     if (fmt == FMT_Q4S)
@@ -549,8 +575,33 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
     }
     int dev = cfg->device;
     cudaDeviceGetAttribute(&eng->n_sm, cudaDevAttrMultiProcessorCount, dev);
-    eng->n_workers = eng->n_sm * 8;
-    eng->att_split = std::max(1, eng->n_sm / NKV);
+    // 16 splits per kv head; the cluster that combines them is the largest size (8, 4, 2) whose
+    // clusters all fit on the GPU at once (a cluster needs its CTAs in one GPC, and GPCs differ
+    // in SM count, so large clusters can leave one cluster waiting for a second wave).
+    eng->att_split = 16;
+    eng->att_cluster = 2;
+    if ((e = set_smem_attrs()) == cudaSuccess) {
+        for (int cl : {4, 2}) {
+            cudaLaunchConfig_t lc = {};
+            lc.gridDim = dim3(NKV * eng->att_split);
+            lc.blockDim = dim3(256);
+            lc.dynamicSmemBytes = AttnSmem<__half>::total;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = cl;
+            at[0].val.clusterDim.y = 1;
+            at[0].val.clusterDim.z = 1;
+            lc.attrs = at;
+            lc.numAttrs = 1;
+            int n_clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&n_clusters, attn_decode_kernel<__half>, &lc) == cudaSuccess &&
+                n_clusters >= NKV * eng->att_split / cl) {
+                eng->att_cluster = cl;
+                break;
+            }
+        }
+        cudaGetLastError();
+    }
     for (int i = 0; i < 64; ++i) {
         const float a = (float)(2 * i) / 128.0f;
         eng->inv_freq[i] = 1.0f / powf(5000000.0f, a);
@@ -584,16 +635,9 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
     TRY(dalloc_t(eng, &eng->logits, (size_t)cfg->vocab));
     TRY(dalloc_t(eng, &eng->pooler, (size_t)cfg->max_pass * H));
     for (int i = 0; i < 3; ++i) TRY(dalloc_t(eng, &eng->deepstack[i], (size_t)cfg->max_pass * H));
-    TRY(dalloc_t(eng, &eng->partials, (size_t)eng->n_workers * 32));
-    TRY(dalloc_t(eng, &eng->tile_cnt, (size_t)cfg->vocab / 16 + 1024));
     TRY(dalloc_t(eng, &eng->att_part, (size_t)NKV * eng->att_split * ATT_PART));
-    TRY(dalloc_t(eng, &eng->att_cnt, 64));
     TRY(dalloc_t(eng, &eng->cta_best_v, (size_t)eng->n_sm));
     TRY(dalloc_t(eng, &eng->cta_best_i, (size_t)eng->n_sm));
-    TRY(dalloc_t(eng, &eng->cta_done, 16));
-    cudaMemset(eng->tile_cnt, 0, ((size_t)cfg->vocab / 16 + 1024) * sizeof(unsigned));
-    cudaMemset(eng->att_cnt, 0, 64 * sizeof(unsigned));
-    cudaMemset(eng->cta_done, 0, 16 * sizeof(unsigned));
     eng->sessions.resize(cfg->max_sessions);
     const size_t kv_elems = (size_t)cfg->n_layers * NKV * cfg->max_context * HD;
     for (auto& S : eng->sessions) {
@@ -738,7 +782,7 @@ icua_status icua_inject_kv(icua_engine* eng, int32_t session, const float* k, co
             for (int h = 0; h < NKV; ++h)
                 for (int d = 0; d < HD; ++d) {
                     const size_t src = (((size_t)l * n_pos + p) * NKV + h) * HD + d;
-                    const size_t dst = ((size_t)h * n_pos + p) * HD + d;
+                    const size_t dst = ((size_t)h * n_pos + p) * HD + kv_swz(d, p);  // cache row order
                     if (eng->cfg.kv_dtype == ICUA_KV_F16) {
                         kb[dst] = icua_host::f32_to_f16_bits(k[src]);
                         vb[dst] = icua_host::f32_to_f16_bits(v[src]);
@@ -762,6 +806,7 @@ icua_status icua_inject_kv(icua_engine* eng, int32_t session, const float* k, co
         }
     }
     S->pos = n_pos;
+    CK(cudaMemcpy(&S->st->pos, &n_pos, 4, cudaMemcpyHostToDevice));
     return ICUA_OK;
 }
 
@@ -779,6 +824,7 @@ icua_status icua_inject_kv_random(icua_engine* eng, int32_t session, int32_t n_p
     CK(cudaGetLastError());
     CK(cudaStreamSynchronize(eng->stream));
     S->pos = n_pos;
+    CK(cudaMemcpy(&S->st->pos, &n_pos, 4, cudaMemcpyHostToDevice));
     return ICUA_OK;
 }
 
@@ -1023,46 +1069,50 @@ icua_status icua_get_timing(icua_engine* eng, icua_timing* out) {
 }
 
 // ---- kernel-level entry points ------------------------------------------------------------------
-uint64_t icua_gemv_scratch_bytes(int32_t fmt, int32_t n_rows, int32_t k) {
-    int dev = 0, n_sm = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
-    const uint64_t workers = (uint64_t)n_sm * 8;
-    return workers * 32 * 4 + (uint64_t)(n_rows / 16 + 16) * 4;
-}
-
 icua_status icua_gemv(int32_t fmt, int32_t n_rows, int32_t k, const void* packed, const void* x, int32_t x_dtype,
-                      float* y, void* scratch, void* stream) {
+                      float* y, void* stream) {
     icua_engine* eng = nullptr;
-    if (!packed || !x || !y || !scratch) return fail(nullptr, ICUA_ERR_INVALID, "null argument");
+    if (!packed || !x || !y) return fail(nullptr, ICUA_ERR_INVALID, "null argument");
     if ((fmt != ICUA_FMT_Q4S && fmt != ICUA_FMT_Q8) || n_rows < 16 || n_rows % 16 || k < 1024 || k % 1024 ||
-        (x_dtype != 0 && x_dtype != 1))
-        return fail(nullptr, ICUA_ERR_INVALID, "unsupported gemv shape or type (rows %% 16, k %% 1024)");
+        k > 6144 || (x_dtype != 0 && x_dtype != 1))
+        return fail(nullptr, ICUA_ERR_INVALID, "unsupported gemv shape or type (rows %% 16, k %% 1024, k <= 6144)");
     CK(set_smem_attrs());
     int dev = 0, n_sm = 0;
     CK(cudaGetDevice(&dev));
     CK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
     Matrix m;
-    setup_matrix(m, fmt, n_rows, k, n_sm * 8);
+    setup_matrix(m, fmt, n_rows, k, n_sm);
+    if (m.stream && fmt == ICUA_FMT_Q4S)
+        return fail(nullptr, ICUA_ERR_INVALID, "q4s gemv supports up to %d rows", 16 * SMALL_MAX_TILES * n_sm);
     GemvParams p{};
     p.w = (const uint8_t*)packed;
-    p.n_units = m.n_units;
     p.n_rows = n_rows;
     p.k = k;
     p.upt = k / 64;
-    p.slot_units = m.slot_units;
+    p.n_tiles = m.n_tiles;
     p.n_slots = m.n_slots;
+    p.chunk = m.chunk;
     p.in_mode = x_dtype == 0 ? IN_F32 : IN_BF16;
     p.x = x;
     p.out = y;
-    p.partials = (float*)scratch;
-    p.tile_cnt = (unsigned*)((uint8_t*)scratch + (size_t)n_sm * 8 * 32 * 4);
     p.st = nullptr;
     cudaStream_t s = (cudaStream_t)stream;
-    if (fmt == ICUA_FMT_Q4S)
-        CK(launch(gemv_kernel<FMT_Q4S, EPI_STORE>, n_sm, 256, m.smem, s, p, false));
-    else
-        CK(launch(gemv_kernel<FMT_Q8, EPI_STORE>, n_sm, 256, m.smem, s, p, false));
+    const bool small = k <= 2048;
+    cudaError_t err;
+    const bool f32 = x_dtype == 0;
+    if (fmt == ICUA_FMT_Q4S) {
+        if (small)
+            err = f32 ? launch_gemv<FMT_Q4S, EPI_STORE, 2048, false, IN_F32>(m, p, s, false)
+                      : launch_gemv<FMT_Q4S, EPI_STORE, 2048, false, IN_BF16>(m, p, s, false);
+        else
+            err = f32 ? launch_gemv<FMT_Q4S, EPI_STORE, 6144, false, IN_F32>(m, p, s, false)
+                      : launch_gemv<FMT_Q4S, EPI_STORE, 6144, false, IN_BF16>(m, p, s, false);
+    } else {
+        if (!small) return fail(nullptr, ICUA_ERR_INVALID, "q8 gemv supports k <= 2048");
+        err = f32 ? launch_gemv<FMT_Q8, EPI_STORE, 2048, true, IN_F32>(m, p, s, false)
+                  : launch_gemv<FMT_Q8, EPI_STORE, 2048, true, IN_BF16>(m, p, s, false);
+    }
+    CK(err);
     return ICUA_OK;
 }
 

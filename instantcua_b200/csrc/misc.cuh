@@ -2,6 +2,7 @@
 // tile layout, KV cache fill.
 #pragma once
 #include "common.cuh"
+#include "gemv.cuh"
 
 namespace icua {
 
@@ -16,39 +17,12 @@ __global__ void advance_kernel(DevState* st) {
     }
 }
 
-// fp32 value of element (row, k) of a q4s tile-packed [n, K] matrix: float(scale) * (u - 8).
-__device__ __forceinline__ float q4s_tile_value(const uint8_t* tiles, int K, int row, int k) {
-    const long long unit = (long long)(row >> 4) * (K / UNIT_K) + (k >> 6);
-    const uint8_t* ub = tiles + unit * Q4_UNIT_BYTES;
-    const int rt = row & 15, gq = rt & 7, up = rt >> 3;
-    const int kin = k & 63, step = kin >> 4, kk = kin & 15;
-    const int t = (kk & 7) >> 1, odd = kk & 1, hi8 = kk >> 3;
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(ub + (gq * 4 + t) * 16 + step * 4);
-    const int u = (w >> (odd * 16 + hi8 * 8 + up * 4)) & 0xF;
-    const __half2 s2 = *reinterpret_cast<const __half2*>(ub + 512 + gq * 8 + (kin >> 5) * 4);
-    const float s = up ? __high2float(s2) : __low2float(s2);
-    return s * (float)(u - 8);
-}
-
-__device__ __forceinline__ float q8_tile_value_k(const uint8_t* tiles, int K, int row, int k) {
-    const long long unit = (long long)(row >> 4) * (K / UNIT_K) + (k >> 6);
-    const uint8_t* ub = tiles + unit * Q8_UNIT_BYTES;
-    const int rt = row & 15, gq = rt & 7, up = rt >> 3;
-    const int kin = k & 63, step = kin >> 4, kk = kin & 15;
-    const int t = (kk & 7) >> 1, odd = kk & 1, hi8 = kk >> 3;
-    const uint8_t* wp = ub + (step >> 1) * 512 + (gq * 4 + t) * 16 + ((step & 1) * 2 + hi8) * 4;
-    const int u = wp[odd * 2 + up];
-    const __half2 s2 = *reinterpret_cast<const __half2*>(ub + 1024 + gq * 8 + (kin >> 5) * 4);
-    const float s = up ? __high2float(s2) : __low2float(s2);
-    return s * (float)(u - 128);
-}
-
 template <int FMT>
 __global__ void dequant_kernel(const uint8_t* tiles, int n_rows, int K, float* out) {
     const long long total = (long long)n_rows * K;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
         const int row = (int)(i / K), k = (int)(i % K);
-        out[i] = FMT == FMT_Q4S ? q4s_tile_value(tiles, K, row, k) : q8_tile_value_k(tiles, K, row, k);
+        out[i] = FMT == FMT_Q4S ? q4s_tile_value(tiles, n_rows / 16, K, row, k) : q8_tile_value(tiles, n_rows / 16, K, row, k);
     }
 }
 

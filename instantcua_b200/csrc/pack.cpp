@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "../../include/icua.h"
+#include "layout.h"
 
 namespace icua_host {
 
@@ -103,7 +104,7 @@ static void quant_sym_g32(const float* w, int rows, int cols, int qmax, int8_t* 
     });
 }
 
-// ---- repack to the device tile layout ---------------------------------------------------------
+// ---- repack to the device tile layout (layout.h) ----------------------------------------------
 // Unit = 16 rows x 64 columns; per lane (g = lane / 4, t = lane % 4) and k16 step, the A fragment
 // of mma.m16n8k16 holds rows g and g+8 at columns 2t, 2t+1, 2t+8, 2t+9.
 
@@ -113,7 +114,7 @@ void pack_q4s(int n_rows, int k, const uint8_t* packed, const uint16_t* scales, 
     const int upt = k / 64, groups = k / 32;
     parallel_rows(n_rows / 16, [&](int tile) {
         for (int kk = 0; kk < upt; ++kk) {
-            uint8_t* ub = out + ((long long)tile * upt + kk) * 576;
+            uint8_t* ub = out + icua_layout::unit_offset(icua_layout::FMT_Q4S, n_rows / 16, upt, tile, kk);
             for (int lane = 0; lane < 32; ++lane) {
                 const int g = lane >> 2, t = lane & 3;
                 const int ra = src_row(row_map, tile * 16 + g), rb = src_row(row_map, tile * 16 + g + 8);
@@ -146,7 +147,7 @@ void pack_q8(int n_rows, int k, const int8_t* codes, const uint16_t* scales, con
     const int upt = k / 64, groups = k / 32;
     parallel_rows(n_rows / 16, [&](int tile) {
         for (int kk = 0; kk < upt; ++kk) {
-            uint8_t* ub = out + ((long long)tile * upt + kk) * 1088;
+            uint8_t* ub = out + icua_layout::unit_offset(icua_layout::FMT_Q8, n_rows / 16, upt, tile, kk);
             for (int lane = 0; lane < 32; ++lane) {
                 const int g = lane >> 2, t = lane & 3;
                 const int ra = src_row(row_map, tile * 16 + g), rb = src_row(row_map, tile * 16 + g + 8);
@@ -203,7 +204,7 @@ icua_status icua_quantize_q4s(const float* w, int32_t rows, int32_t cols, uint8_
 }
 
 uint64_t icua_packed_bytes(int32_t fmt, int32_t n_rows, int32_t k) {
-    if (n_rows <= 0 || k <= 0 || n_rows % 16 || k % 64) return 0;
+    if (n_rows <= 0 || k <= 0 || n_rows % 16 || k % 1024) return 0;
     const uint64_t units = (uint64_t)(n_rows / 16) * (uint64_t)(k / 64);
     if (fmt == ICUA_FMT_Q4S) return units * 576;
     if (fmt == ICUA_FMT_Q8) return units * 1088;

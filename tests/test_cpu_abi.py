@@ -68,11 +68,18 @@ def test_tiny_model_tensors_match_pinned_hashes(golden):
 
 
 def decode_tiles(fmt, packed, n_rows, k):
-    """numpy decoder of the device tile layout (independent of the CUDA value functions)."""
+    """numpy decoder of the device tile layout (independent of the CUDA value functions).
+
+    Units of 16 rows x 64 columns, stored slice-major: K is split into `slices` slices (16 for
+    q4s, 8 for q8); unit (tile, kk) of slice w = kk // ku lives at ((w * tiles + tile) * ku + kk % ku).
+    """
     ub = 576 if fmt == L.FMT_Q4S else 1088
     wb = 512 if fmt == L.FMT_Q4S else 1024
-    upt = k // 64
-    units = packed.reshape(n_rows // 16, upt, ub)
+    slices = 16 if fmt == L.FMT_Q4S else 8
+    upt, tiles = k // 64, n_rows // 16
+    ku = upt // slices
+    raw = packed.reshape(slices, tiles, ku, ub)
+    units = raw.transpose(1, 0, 2, 3).reshape(tiles, upt, ub)  # [tile][kk]
     out = np.zeros((n_rows, k), np.float32)
     lanes = np.arange(32)
     g, t = lanes >> 2, lanes & 3
@@ -80,17 +87,17 @@ def decode_tiles(fmt, packed, n_rows, k):
         for (dk, rowoff) in ((0, 0), (1, 0), (8, 0), (9, 0), (0, 8), (1, 8), (8, 8), (9, 8)):
             kin = step * 16 + 2 * t + dk
             if fmt == L.FMT_Q4S:
-                words = units[:, :, :wb].reshape(n_rows // 16, upt, 32, 4, 4)[:, :, :, step, :].copy().view(np.uint32)[..., 0]
+                words = units[:, :, :wb].reshape(tiles, upt, 32, 4, 4)[:, :, :, step, :].copy().view(np.uint32)[..., 0]
                 shift = (dk & 1) * 16 + (dk >> 3) * 8 + (rowoff >> 3) * 4
                 u = ((words >> shift) & 0xF).astype(np.int32) - 8
             else:
-                grp16 = units[:, :, (step >> 1) * 512:(step >> 1) * 512 + 512].reshape(n_rows // 16, upt, 32, 16)
+                grp16 = units[:, :, (step >> 1) * 512:(step >> 1) * 512 + 512].reshape(tiles, upt, 32, 16)
                 byte = (step & 1) * 8 + (dk >> 3) * 4 + (dk & 1) * 2 + (rowoff >> 3)
                 u = grp16[..., byte].astype(np.int32) - 128
-            sc = units[:, :, wb:wb + 64].reshape(n_rows // 16, upt, 8, 2, 4).copy().view(np.float16)
+            sc = units[:, :, wb:wb + 64].reshape(tiles, upt, 8, 2, 4).copy().view(np.float16)
             grp = kin >> 5
             s = sc[:, :, g, grp, (rowoff >> 3)]  # [tiles, upt, 32]
-            rows = (np.arange(n_rows // 16)[:, None, None] * 16 + g[None, None, :] + rowoff)
+            rows = (np.arange(tiles)[:, None, None] * 16 + g[None, None, :] + rowoff)
             cols = np.arange(upt)[None, :, None] * 64 + kin[None, None, :]
             out[np.broadcast_to(rows, u.shape), np.broadcast_to(cols, u.shape)] = s.astype(np.float32) * u
     return out
@@ -98,7 +105,7 @@ def decode_tiles(fmt, packed, n_rows, k):
 
 @pytest.mark.parametrize("fmt", [L.FMT_Q4S, L.FMT_Q8])
 def test_pack_layout_roundtrip(fmt):
-    rows, k = 64, 256
+    rows, k = 48, 2048
     w = (np.random.default_rng(3).standard_normal((rows, k)) * 0.02).astype(np.float32)
     if fmt == L.FMT_Q4S:
         codes, scales = model.quantize_q4s(w)
@@ -130,7 +137,8 @@ def test_icua_file_layout(tmp_path):
 def test_invalid_arguments_are_errors_not_crashes():
     lib = L.lib()
     assert lib.icua_quantize_q8(None, 1, 32, None, None) == L.ERR_INVALID
-    assert lib.icua_packed_bytes(L.FMT_Q4S, 15, 64) == 0
+    assert lib.icua_packed_bytes(L.FMT_Q4S, 15, 1024) == 0
+    assert lib.icua_packed_bytes(L.FMT_Q4S, 16, 512) == 0  # K must split into the 16 slices
     assert lib.icua_packed_bytes(L.FMT_F16, 16, 64) == 0
     cfg = L.IcuaConfig()
     lib.icua_default_config(C.byref(cfg))

@@ -43,10 +43,9 @@ def _packed(fmt, n, k, seed):
 
 
 def _gemv(torch, fmt, n, k, dev_w, x, x_dtype=0):
-    scratch = torch.zeros(L.lib().icua_gemv_scratch_bytes(fmt, n, k), dtype=torch.uint8, device="cuda")
     y = torch.empty(n, dtype=torch.float32, device="cuda")
     L.check(L.lib().icua_gemv(fmt, n, k, C.c_void_p(dev_w.data_ptr()), C.c_void_p(x.data_ptr()), x_dtype,
-                              C.c_void_p(y.data_ptr()), C.c_void_p(scratch.data_ptr()), None))
+                              C.c_void_p(y.data_ptr()), None))
     torch.cuda.synchronize()
     return y
 
@@ -88,7 +87,7 @@ def test_gemv_matches_fp64_reference(torch_cuda, fmt, shape):
     want = ref.astype(np.float64) @ x.astype(np.float64)
     err = np.abs(y - want).max() / np.abs(want).max()
     assert err <= GEMV_TOL, err
-    # deterministic: a second launch gives the same bits (split tiles reduce in a fixed order)
+    # deterministic: a second launch gives the same bits (K slices reduce in a fixed order)
     y2 = _gemv(torch, fmt, n, k, dev, torch.from_numpy(x).cuda()).cpu().numpy()
     assert np.array_equal(y, y2)
 
@@ -106,5 +105,5 @@ def test_gemv_bf16_activations(torch_cuda):
 
 def test_gemv_rejects_bad_shapes(torch_cuda):
     lib = L.lib()
-    assert lib.icua_gemv(L.FMT_Q4S, 15, 2048, C.c_void_p(1), C.c_void_p(1), 0, C.c_void_p(1), C.c_void_p(1), None) == L.ERR_INVALID
-    assert lib.icua_gemv(L.FMT_Q4S, 16, 1000, C.c_void_p(1), C.c_void_p(1), 0, C.c_void_p(1), C.c_void_p(1), None) == L.ERR_INVALID
+    assert lib.icua_gemv(L.FMT_Q4S, 15, 2048, C.c_void_p(1), C.c_void_p(1), 0, C.c_void_p(1), None) == L.ERR_INVALID
+    assert lib.icua_gemv(L.FMT_Q4S, 16, 1000, C.c_void_p(1), C.c_void_p(1), 0, C.c_void_p(1), None) == L.ERR_INVALID
