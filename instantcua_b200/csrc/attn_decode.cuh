@@ -41,6 +41,7 @@ struct AttnParams {
     int cluster;             // CTAs per cluster
     float* part;             // out: [NKV][n_split / cluster][ATT_PART]
     DevState* st;
+    L2Plan l2;               // data of later kernels to prefetch into L2
 };
 
 template <typename KVT>
@@ -229,6 +230,7 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
         fence_mbar_init();
         for (int c = 0; c < min(ATT_NS, n_chunks); ++c) issue(c);
     }
+    if (tid == 32) l2_prefetch_plan(p.l2, pos);
     // norm weights and this position's rotation are inputs that do not depend on the producer
     float nw[4] = {1.f, 1.f, 1.f, 1.f};
     float2 cs4[4];

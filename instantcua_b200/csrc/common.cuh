@@ -108,6 +108,50 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     return false;
 }
 
+// L2 prefetch plan of a kernel: byte ranges that a later kernel of the step will read (weights,
+// cache rows), split evenly over this kernel's CTAs and requested before griddepcontrol.wait, so
+// HBM streams ahead of the dependency chain.  Ranges: `n` plain ranges, plus optionally the
+// [0, pos) rows of every kv head of one layer's K and V cache.
+struct L2Plan {
+    const uint8_t* ptr[2];
+    uint64_t bytes[2];
+    int n;
+    const uint8_t* kv_k;     // cache rows of the layer to prefetch, or nullptr
+    const uint8_t* kv_v;
+    uint64_t kv_head_stride;  // bytes between kv heads (max_ctx * 128 * elem)
+    int kv_row_bytes;
+};
+
+__device__ __forceinline__ void l2_prefetch_range(const uint8_t* base, uint64_t begin, uint64_t end) {
+    begin &= ~uint64_t(15);
+    end = (end + 15) & ~uint64_t(15);
+    while (begin < end) {
+        const uint64_t n = min(end - begin, (uint64_t)(1u << 20));
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + begin), "r"((uint32_t)n) : "memory");
+        begin += n;
+    }
+}
+
+// Issues this CTA's share of the plan (one thread).  `pos` bounds the cache rows.
+__device__ __forceinline__ void l2_prefetch_plan(const L2Plan& pl, int pos) {
+    const uint64_t G = gridDim.x, c = blockIdx.x;
+    for (int i = 0; i < pl.n; ++i) {
+        const uint64_t b = pl.bytes[i];
+        if (b) l2_prefetch_range(pl.ptr[i], b * c / G, b * (c + 1) / G);
+    }
+    if (pl.kv_k != nullptr && pos > 0) {
+        // 16 ranges (8 kv heads x K, V) of pos rows each, concatenated and split over the CTAs
+        const uint64_t per = (uint64_t)pos * pl.kv_row_bytes, total = 16 * per;
+        uint64_t a = total * c / G, e = total * (c + 1) / G;
+        while (a < e) {
+            const uint64_t r = a / per, off = a - r * per, n = min(e - a, per - off);
+            const uint8_t* base = (r < 8 ? pl.kv_k : pl.kv_v) + (r & 7) * pl.kv_head_stride;
+            l2_prefetch_range(base, off, off + n);
+            a += n;
+        }
+    }
+}
+
 // Programmatic dependent launch: wait for the producing grid, then let the next grid start.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {

@@ -244,6 +244,26 @@ GemvParams base_params(icua_engine* e, const Matrix& m) {
 }
 
 // ---- one decode / prefill step ------------------------------------------------------------------
+// L2 prefetch two launches ahead: QKV(l) -> O(l) weights, attention(l) -> GU(l), O(l) -> D(l),
+// GU(l) -> QKV(l+1), D(l) -> cache rows of layer l+1 (or the lm_head after the last layer).
+L2Plan plan_weights(const Matrix& m) {
+    L2Plan pl{};
+    pl.ptr[0] = m.dev;
+    pl.bytes[0] = icua_packed_bytes(m.fmt, m.n_rows, m.k);
+    pl.n = 1;
+    return pl;
+}
+
+L2Plan plan_kv(icua_engine* e, Session& S, int layer) {
+    L2Plan pl{};
+    const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD * 2;
+    pl.kv_k = reinterpret_cast<const uint8_t*>(S.kc) + kv_layer * layer;
+    pl.kv_v = reinterpret_cast<const uint8_t*>(S.vc) + kv_layer * layer;
+    pl.kv_head_stride = (uint64_t)e->cfg.max_context * HD * 2;
+    pl.kv_row_bytes = HD * 2;
+    return pl;
+}
+
 cudaError_t record_layers(icua_engine* e, Session& S) {
     cudaError_t err;
     const int L = e->cfg.n_layers;
@@ -260,6 +280,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.x_resid = e->x;
         p.out = e->qkv;
         p.st = S.st;
+        p.l2 = plan_weights(ly.o);
         err = (l == 0) ? launch_gemv<FMT_Q4S, EPI_STORE, 2048, false, IN_EMBED>(ly.qkv, p, e->stream)
                        : launch_gemv<FMT_Q4S, EPI_STORE, 2048, false, IN_F32>(ly.qkv, p, e->stream);
         if (err != cudaSuccess) return err;
@@ -278,6 +299,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
             a.cluster = e->att_cluster;
             a.part = e->att_part;
             a.st = S.st;
+            a.l2 = plan_weights(ly.gu);
             err = launch_cluster(attn_decode_kernel<__nv_bfloat16>, NKV * e->att_split, e->att_cluster, 256,
                                  AttnSmem<__nv_bfloat16>::total, e->stream, a);
         } else {
@@ -293,6 +315,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
             a.cluster = e->att_cluster;
             a.part = e->att_part;
             a.st = S.st;
+            a.l2 = plan_weights(ly.gu);
             err = launch_cluster(attn_decode_kernel<__half>, NKV * e->att_split, e->att_cluster, 256,
                                  AttnSmem<__half>::total, e->stream, a);
         }
@@ -304,6 +327,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.att_parts = e->att_split / e->att_cluster;
         p.x_resid = e->x;
         p.st = S.st;
+        p.l2 = plan_weights(ly.d);
         if ((err = launch_gemv<FMT_Q4S, EPI_RESID, 2048, false, IN_ATTN>(ly.o, p, e->stream)) != cudaSuccess) return err;
         // 4. RMSNorm + gate/up + SwiGLU
         p = base_params(e, ly.gu);
@@ -312,6 +336,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.norm_w = ly.mlp_norm;
         p.out = e->h;
         p.st = S.st;
+        if (l + 1 < L) p.l2 = plan_weights(e->layers[l + 1].qkv);
         if ((err = launch_gemv<FMT_Q4S, EPI_SWIGLU, 2048, false, IN_F32>(ly.gu, p, e->stream)) != cudaSuccess) return err;
         // 5. down + residual (+ DeepStack rows after layers 0..2 while prefilling visual rows)
         p = base_params(e, ly.d);
@@ -320,6 +345,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.x_resid = e->x;
         p.deepstack = (l < 3) ? e->deepstack[l] : nullptr;
         p.st = S.st;
+        p.l2 = (l + 1 < L) ? plan_kv(e, S, l + 1) : plan_weights(e->embed);
         if ((err = launch_gemv<FMT_Q4S, EPI_RESID, 6144, false, IN_F32>(ly.d, p, e->stream)) != cudaSuccess) return err;
     }
     return cudaSuccess;

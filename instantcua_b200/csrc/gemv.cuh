@@ -64,6 +64,7 @@ struct GemvParams {
     float* cta_best_v;       // EPI_LOGITS: per-CTA argmax partials [gridDim.x]
     int* cta_best_i;
     DevState* st;            // nullptr for standalone GEMV
+    L2Plan l2;               // data of later kernels to prefetch into L2
 };
 
 __host__ __device__ inline int gemv_tiles_per_cta(int n_tiles, int grid) { return (n_tiles + grid - 1) / grid; }
@@ -400,6 +401,7 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
         }
         for (int c = 0; c < min(NS, n_chunks); ++c) issue(c);
     }
+    if (threadIdx.x == 32) l2_prefetch_plan(p.l2, p.st ? *(volatile int*)&p.st->pos : 0);
     if (STREAM)
         for (int i = threadIdx.x; i < tpc; i += NT) cnt[i] = 0;
     InputRegs<KMAX, NT> in;
