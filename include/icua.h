@@ -173,6 +173,17 @@ icua_status icua_pack_matrix(int32_t fmt, int32_t n_rows, int32_t k, const void*
  * or NULL.  No scratch memory: every CTA owns whole 16-row tiles. */
 icua_status icua_gemv(int32_t fmt, int32_t n_rows, int32_t k, const void* packed_dev,
                       const void* x_dev, int32_t x_dtype, float* y_dev, void* stream);
+/* Greedy head on the device: token = argmax_v (embed_v . RMSNorm(x) * norm_w), the tied q8 lm_head
+ * of the reference (k_lm_head + k_commit, Shaders.swift:1452-1547; lowest index wins ties).
+ * packed_embed_dev: q8 [vocab, 2048] in the device layout (icua_pack_matrix); x_dev fp32 [2048];
+ * norm_w_dev fp32 [2048] or NULL (no norm); logits_dev fp32 [vocab] or NULL; token_dev int32 [1].
+ * scratch_dev: icua_greedy_head_scratch_bytes(vocab) bytes of device memory for the per-CTA argmax
+ * partials (no initialisation needed). */
+uint64_t icua_greedy_head_scratch_bytes(int32_t vocab);
+icua_status icua_greedy_head(int32_t vocab, const void* packed_embed_dev, const float* x_dev,
+                             const float* norm_w_dev, float* logits_dev, int32_t* token_dev,
+                             void* scratch_dev, void* stream);
+
 /* Bit-exact dequantization of a packed device matrix to fp32 row-major [n_rows, k]. */
 icua_status icua_dequant(int32_t fmt, int32_t n_rows, int32_t k, const void* packed_dev, float* out_dev,
                          void* stream);

@@ -224,6 +224,7 @@ cudaError_t set_smem_attrs() {
     SETA((attn_decode_kernel<__nv_bfloat16>));
     SETA(commit_kernel);
     SETA(advance_kernel);
+    SETA(argmax_parts_kernel);
 #undef SETA
     done = true;
     return cudaSuccess;
@@ -1140,6 +1141,63 @@ icua_status icua_gemv(int32_t fmt, int32_t n_rows, int32_t k, const void* packed
     }
     CK(err);
     return ICUA_OK;
+}
+
+// ---- greedy head: final RMSNorm + tied q8 lm_head GEMV + argmax (reference k_lm_head + k_commit) --
+static icua_status greedy_head_args(int32_t vocab, const void* packed, const float* x, int32_t* token, int& n_sm,
+                                    Matrix& m) {
+    icua_engine* eng = nullptr;
+    if (!packed || !x || !token) return fail(nullptr, ICUA_ERR_INVALID, "null argument");
+    if (vocab < 16 || vocab % 16) return fail(nullptr, ICUA_ERR_INVALID, "vocab %d is not a positive multiple of 16", vocab);
+    CK(set_smem_attrs());
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    CK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+    setup_matrix(m, FMT_Q8, vocab, H, n_sm);
+    return ICUA_OK;
+}
+
+static icua_status greedy_head_launch(const Matrix& m, const void* packed, const float* x, const float* norm_w,
+                                      float* logits, int32_t* token, float* best_v, int* best_i, cudaStream_t s) {
+    icua_engine* eng = nullptr;
+    GemvParams p{};
+    p.w = (const uint8_t*)packed;
+    p.n_rows = m.n_rows;
+    p.k = H;
+    p.upt = H / 64;
+    p.n_tiles = m.n_tiles;
+    p.n_slots = m.n_slots;
+    p.chunk = m.chunk;
+    p.in_mode = IN_F32;
+    p.x = x;
+    p.norm_w = norm_w;
+    p.logits = logits;
+    p.cta_best_v = best_v;
+    p.cta_best_i = best_i;
+    p.st = nullptr;
+    CK((launch_gemv<FMT_Q8, EPI_LOGITS, 2048, true, IN_F32>(m, p, s, false)));
+    CK(launch(argmax_parts_kernel, 1, 256, 0, s, true, (const float*)best_v, (const int*)best_i, m.grid, token));
+    return ICUA_OK;
+}
+
+uint64_t icua_greedy_head_scratch_bytes(int32_t vocab) {
+    int dev = 0, n_sm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = std::min(n_sm, std::max(vocab, 16) / 16);
+    return (uint64_t)grid * 8;
+}
+
+icua_status icua_greedy_head(int32_t vocab, const void* packed, const float* x, const float* norm_w, float* logits,
+                             int32_t* token, void* scratch, void* stream) {
+    if (!scratch) return fail(nullptr, ICUA_ERR_INVALID, "null scratch");
+    int n_sm = 0;
+    Matrix m;
+    icua_status st = greedy_head_args(vocab, packed, x, token, n_sm, m);
+    if (st != ICUA_OK) return st;
+    float* best_v = (float*)scratch;
+    int* best_i = (int*)((uint8_t*)scratch + (size_t)m.grid * 4);
+    return greedy_head_launch(m, packed, x, norm_w, logits, token, best_v, best_i, (cudaStream_t)stream);
 }
 
 icua_status icua_dequant(int32_t fmt, int32_t n_rows, int32_t k, const void* packed, float* out, void* stream) {

@@ -420,7 +420,7 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
         if (threadIdx.x == 0 && p.norm_w != nullptr) mbar_wait_bounded(nbar, 0);
         return;
     }
-    int write_logits = 0, step = 0;
+    int write_logits = (p.logits != nullptr && p.st == nullptr) ? 1 : 0, step = 0;
     float ds = 0.f;
     if (p.st != nullptr && (EPI == EPI_LOGITS || (EPI == EPI_RESID && p.deepstack != nullptr))) {
         const DevState* st = p.st;
@@ -557,6 +557,29 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
             p.cta_best_v[blockIdx.x] = bv;
             p.cta_best_i[blockIdx.x] = bi;
         }
+    }
+}
+
+// Reduces per-CTA argmax partials to one token id (standalone greedy head): one CTA.
+__global__ void __launch_bounds__(256) argmax_parts_kernel(const float* best_v, const int* best_i, int n_parts,
+                                                           int* token) {
+    pdl_wait();
+    pdl_launch_dependents();
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n_parts; i += blockDim.x) argmax_merge(bv, bi, best_v[i], best_i[i]);
+    warp_argmax(bv, bi);
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w2 = 1; w2 < (int)(blockDim.x >> 5); ++w2) argmax_merge(sv[0], si[0], sv[w2], si[w2]);
+        *token = si[0];
     }
 }
 

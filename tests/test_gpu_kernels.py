@@ -107,3 +107,36 @@ def test_gemv_rejects_bad_shapes(torch_cuda):
     lib = L.lib()
     assert lib.icua_gemv(L.FMT_Q4S, 15, 2048, C.c_void_p(1), C.c_void_p(1), 0, C.c_void_p(1), None) == L.ERR_INVALID
     assert lib.icua_gemv(L.FMT_Q4S, 16, 1000, C.c_void_p(1), C.c_void_p(1), 0, C.c_void_p(1), None) == L.ERR_INVALID
+
+
+@pytest.mark.parametrize("vocab", [151936, 4096])
+def test_greedy_head_matches_fp64_reference(torch_cuda, vocab):
+    """Final RMSNorm + tied q8 lm_head + argmax (reference k_lm_head + k_commit)."""
+    torch = torch_cuda
+    buf, ref = _packed(L.FMT_Q8, vocab, 2048, seed=vocab)
+    dev = torch.from_numpy(buf).cuda()
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal(2048).astype(np.float32) * 3
+    w = (1 + 0.1 * rng.standard_normal(2048)).astype(np.float32)
+    xd, wd = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
+    logits = torch.empty(vocab, dtype=torch.float32, device="cuda")
+    token = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    scratch = torch.empty(L.lib().icua_greedy_head_scratch_bytes(vocab), dtype=torch.uint8, device="cuda")
+    L.check(L.lib().icua_greedy_head(vocab, C.c_void_p(dev.data_ptr()), C.c_void_p(xd.data_ptr()),
+                                     C.c_void_p(wd.data_ptr()), C.c_void_p(logits.data_ptr()),
+                                     C.c_void_p(token.data_ptr()), C.c_void_p(scratch.data_ptr()), None))
+    torch.cuda.synchronize()
+    h = x.astype(np.float64) / np.sqrt(np.mean(x.astype(np.float64) ** 2) + 1e-6) * w
+    want = ref.astype(np.float64) @ h
+    got = logits.cpu().numpy()
+    assert np.abs(got - want).max() / np.abs(want).max() <= GEMV_TOL
+    tok = int(token.item())
+    assert tok == int(np.argmax(got))  # lowest index among equal maxima, like np.argmax
+    assert want[tok] >= want.max() - 1e-4 * np.abs(want).max()
+    # logits are optional
+    token.fill_(-1)
+    L.check(L.lib().icua_greedy_head(vocab, C.c_void_p(dev.data_ptr()), C.c_void_p(xd.data_ptr()),
+                                     C.c_void_p(wd.data_ptr()), None, C.c_void_p(token.data_ptr()),
+                                     C.c_void_p(scratch.data_ptr()), None))
+    torch.cuda.synchronize()
+    assert int(token.item()) == tok
