@@ -184,6 +184,20 @@ icua_status icua_greedy_head(int32_t vocab, const void* packed_embed_dev, const 
                              const float* norm_w_dev, float* logits_dev, int32_t* token_dev,
                              void* scratch_dev, void* stream);
 
+/* icua_greedy_head for callers that cannot allocate device memory (a host that owns all device
+ * memory through its own pool, a plugin that may not call cudaMalloc after start-up, a real-time
+ * loop that must stay out of the allocator).  No reference counterpart: the reference engine
+ * allocates its pval/pidx buffers at init (Engine.swift:116-117).  Same arguments and results as
+ * icua_greedy_head minus the scratch: the per-CTA partials live in a fixed 8 KiB device array of
+ * the library (room for 1024 CTA partials; larger grids are rejected with ICUA_ERR_CAPACITY),
+ * which every GPU that loads the library keeps until exit.  The first call on a device looks up
+ * that array's address (cudaGetSymbolAddress) with the device current; make that first call
+ * before any stream capture.  All calls share the array, so calls that overlap on the GPU (on
+ * different streams or devices sharing nothing else) race; serialise them. */
+icua_status icua_greedy_head_noalloc(int32_t vocab, const void* packed_embed_dev, const float* x_dev,
+                                     const float* norm_w_dev, float* logits_dev, int32_t* token_dev,
+                                     void* stream);
+
 /* Bit-exact dequantization of a packed device matrix to fp32 row-major [n_rows, k]. */
 icua_status icua_dequant(int32_t fmt, int32_t n_rows, int32_t k, const void* packed_dev, float* out_dev,
                          void* stream);

@@ -19,6 +19,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1197,6 +1198,49 @@ icua_status icua_greedy_head(int32_t vocab, const void* packed, const float* x, 
     if (st != ICUA_OK) return st;
     float* best_v = (float*)scratch;
     int* best_i = (int*)((uint8_t*)scratch + (size_t)m.grid * 4);
+    return greedy_head_launch(m, packed, x, norm_w, logits, token, best_v, best_i, (cudaStream_t)stream);
+}
+
+// ---- greedy head without allocation ------------------------------------------------------------
+// Some callers cannot call cudaMalloc at all: code running under a host allocator or memory
+// pool that owns all device memory, a plugin loaded into a process that forbids allocation
+// after start-up, or a real-time loop that must not enter the driver's allocator.  For them the
+// per-CTA argmax partials live in this fixed file-scope device array instead of caller scratch.
+// Every GPU that loads the library keeps these bytes until the process exits.
+constexpr int NOALLOC_MAX_PARTS = 1024;  // CTA partials (8 bytes each): grids up to 1024 CTAs
+static __device__ __align__(256) uint8_t g_greedy_head_scratch[NOALLOC_MAX_PARTS * 8];
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[64];  // device address of the array, per device ordinal
+
+icua_status icua_greedy_head_noalloc(int32_t vocab, const void* packed, const float* x, const float* norm_w,
+                                     float* logits, int32_t* token, void* stream) {
+    icua_engine* eng = nullptr;
+    int n_sm = 0;
+    Matrix m;
+    icua_status st = greedy_head_args(vocab, packed, x, token, n_sm, m);
+    if (st != ICUA_OK) return st;
+    if (m.grid > NOALLOC_MAX_PARTS)
+        return fail(nullptr, ICUA_ERR_CAPACITY, "greedy head needs %d CTA partials, the fixed scratch holds %d",
+                    m.grid, NOALLOC_MAX_PARTS);
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(nullptr, ICUA_ERR_INVALID, "device ordinal %d out of range", dev);
+    void* base = nullptr;
+    {
+        // first call on a device: look up the array's device address with that device current
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (g_noalloc_addr[dev] == nullptr) {
+            void* a = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&a, g_greedy_head_scratch);
+            if (e != cudaSuccess)
+                return fail(nullptr, ICUA_ERR_CUDA, "cudaGetSymbolAddress(greedy head scratch): %s", cudaGetErrorString(e));
+            g_noalloc_addr[dev] = a;
+        }
+        base = g_noalloc_addr[dev];
+    }
+    // every partial is written by its CTA before it is read: nothing needs clearing between calls
+    float* best_v = (float*)base;
+    int* best_i = (int*)((uint8_t*)base + (size_t)NOALLOC_MAX_PARTS * 4);
     return greedy_head_launch(m, packed, x, norm_w, logits, token, best_v, best_i, (cudaStream_t)stream);
 }
 
