@@ -205,41 +205,108 @@ def run_ours(args):
         print(json.dumps(out))
 
 
-def lm_head_roofline(torch, L, peak):
+def fill_units(torch, w, fmt):
+    """Random codes with valid fp16 scales (0x1419, about 1.06e-3) in every unit's scale block, so
+    the arithmetic is representative."""
+    ub, wb = (1088, 1024) if fmt == 1 else (576, 512)
+    units = w.view(-1, ub)
+    units[:, wb:] = torch.tensor([0x1419], dtype=torch.int16, device=w.device).view(torch.uint8).repeat(32)
+
+
+def time_gemv(torch, L, fmt, n, k, x_dtype=0, reps=50, min_bytes=0):
+    """Times icua_gemv with CUDA events: `reps` launches captured back to back in one CUDA graph
+    (so the host's launch rate is not what is measured), replayed 5 times.  When min_bytes > 0
+    the weights are replicated until the copies exceed it and the launches rotate through them
+    (L2 defeated).  Returns (ms per launch, algorithmic bytes per launch, copies)."""
     import ctypes as C
 
-    import numpy as np
-
-    n, k = V, 2048
-    nbytes = L.lib().icua_packed_bytes(L.FMT_Q8, n, k)
-    w = torch.randint(0, 255, (nbytes,), dtype=torch.uint8, device="cuda")
-    # valid fp16 scales (1e-3) in every unit's scale block so the arithmetic is representative
-    units = w.view(-1, 1088)
-    units[:, 1024:] = torch.tensor([0x1419], dtype=torch.int16, device="cuda").view(torch.uint8).repeat(32)
-    x = torch.randn(k, device="cuda")
+    nbytes = L.lib().icua_packed_bytes(fmt, n, k)
+    copies = max(1, -(-min_bytes // nbytes)) if min_bytes else 1
+    w = torch.randint(0, 255, (copies * nbytes,), dtype=torch.uint8, device="cuda")
+    fill_units(torch, w, fmt)
+    x = torch.randn(k, device="cuda", dtype=torch.bfloat16 if x_dtype == 1 else torch.float32)
     y = torch.empty(n, device="cuda")
-    s = torch.cuda.current_stream()
+    base = w.data_ptr()
 
-    def run():
-        L.check(L.lib().icua_gemv(L.FMT_Q8, n, k, C.c_void_p(w.data_ptr()), C.c_void_p(x.data_ptr()), 0,
-                                  C.c_void_p(y.data_ptr()), C.c_void_p(s.cuda_stream)))
+    def run(i):
+        s = torch.cuda.current_stream()
+        L.check(L.lib().icua_gemv(fmt, n, k, C.c_void_p(base + (i % copies) * nbytes), C.c_void_p(x.data_ptr()),
+                                  x_dtype, C.c_void_p(y.data_ptr()), C.c_void_p(s.cuda_stream)))
 
-    for _ in range(5):
-        run()
-    reps = 50
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        for i in range(max(5, copies)):
+            run(i)
     torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(reps):
+            run(i)
+    g.replay()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(s)
-    for _ in range(reps):
-        run()
+    for _ in range(5):
+        g.replay()
     b.record(s)
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / reps
-    alg = nbytes + k * 4 + n * 4
+    ms = a.elapsed_time(b) / (5 * reps)
+    alg = nbytes + k * x.element_size() + n * 4
+    return ms, alg, copies
+
+
+def profile_traffic(name):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) recorded in a committed
+    ncu summary under profiles/, or None when that summary is absent."""
+    import re
+
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", open(p).read())
+    return int(m.group(1)) if m else None
+
+
+def lm_head_roofline(torch, L, peak):
+    n, k = V, 2048
+    ms, alg, _ = time_gemv(torch, L, 1, n, k)
     ach = alg / (ms / 1e3) / 1e9
     return {"kernel": "gemv_kernel<q8,store> lm_head 151936x2048", "bound": "hbm", "achieved": round(ach, 1),
-            "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "traffic": None,
+            "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+            "traffic": profile_traffic("gemv_q8_lm_head_151936x2048.md"),
             "algorithmic_bytes": alg, "ms_per_launch": round(ms, 5)}
+
+
+MICRO_SHAPES = (("q/o 2048x2048", 3, 2048, 2048), ("k/v 2048x1024", 3, 1024, 2048),
+                ("gate+up 2048x12288", 3, 12288, 2048), ("down 6144x2048", 3, 2048, 6144),
+                ("lm_head q8 2048x151936", 1, V, 2048))
+
+
+def run_micro(args):
+    """Config 1: isolated batch-1 dequant-GEMV per decoder shape (K x N), bf16 activations N(0,1),
+    weights rotated over copies totalling more than twice the 126 MB L2."""
+    import torch
+
+    from instantcua_b200 import _lib as L
+
+    peak, peak_kind = peaks()
+    rows = []
+    for name, fmt, n, k in MICRO_SHAPES:
+        if args.micro_shape and args.micro_shape not in name:
+            continue
+        ms, alg, copies = time_gemv(torch, L, fmt, n, k, x_dtype=1, reps=max(args.steps, 20), min_bytes=256 << 20)
+        gbs = alg / (ms / 1e3) / 1e9
+        rows.append({"shape": name, "fmt": "q8" if fmt == 1 else "q4s", "n_rows": n, "k": k, "us": round(ms * 1e3, 2),
+                     "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4), "algorithmic_bytes": alg,
+                     "copies_rotated": copies})
+    tot_b = sum(r["algorithmic_bytes"] for r in rows)
+    tot_us = sum(r["us"] for r in rows)
+    print(json.dumps({"metric": "q4/q8 dequant-GEMV GB/s (batch 1, config 1)", "value": round(tot_b / tot_us / 1e3, 1),
+                      "unit": "GB/s", "n_gpus": 1, "steps": max(args.steps, 20), "higher_is_better": True,
+                      "dtype": "q4s/q8 weights, bf16 x, fp32 accumulate", "data": "synthetic random codes",
+                      "config": {"workload": "config 1: GEMV microbench", "l2": "weights rotated over > 256 MB"},
+                      "peak": peak, "peak_kind": peak_kind, "shapes": rows}))
 
 
 def cpu_baseline(path, steps: int = 3):
@@ -293,6 +360,89 @@ def oracle_model_from_file(path):
     return w, O.TextModel(w)
 
 
+N_VIS, LLM_H, LLM_W, N_TEXT, PREFILL_DECODE = 1000, 25, 40, 256, 32
+LAYER_PARAMS = {"qkv": 4096 * 2048, "o": 2048 * 2048, "gu": 12288 * 2048, "d": 2048 * 6144}
+
+
+def prefill_flops(n: int) -> int:
+    """Linear-layer FLOPs of the tensor-core prefill of an n-token prompt: rows 0..n-2 through all
+    layers, except that the last layer only projects K/V (QKV GEMM); the last row runs as a
+    decode step and is not counted."""
+    rows = n - 1
+    per_row = NL * LAYER_PARAMS["qkv"] + (NL - 1) * (LAYER_PARAMS["o"] + LAYER_PARAMS["gu"] + LAYER_PARAMS["d"])
+    return 2 * rows * per_row
+
+
+def config3_inputs(seed: int = 3):
+    """1000 visual rows (pooler + 3 DeepStack tensors, N(0,1) rounded to bf16 values) on a 25 x 40
+    merged grid at the start of the prompt, then 256 uniform text ids."""
+    import numpy as np
+    import torch
+
+    rng = np.random.default_rng(seed)
+
+    def bf16(a):
+        return torch.from_numpy(a).to(torch.bfloat16).float().numpy()
+
+    pooler = bf16(rng.standard_normal((N_VIS, H), dtype=np.float32))
+    ds = [bf16(rng.standard_normal((N_VIS, H), dtype=np.float32)) for _ in range(3)]
+    tokens = np.concatenate([np.full(N_VIS, 151655, np.int32), rng.integers(0, 151643, N_TEXT).astype(np.int32)])
+    return tokens, pooler, ds
+
+
+def run_prefill(args):
+    """Config 3: multimodal prefill (1000 visual + 256 text rows, DeepStack at layers 0-2) through
+    the tcgen05 dequant-GEMM path, then 32 greedy decode steps.  value = prefill tokens/s (device
+    time of the prefill call); roofline = linear-layer TFLOP/s against the measured bf16 GEMM peak."""
+    import torch
+
+    from instantcua_b200 import Engine
+
+    torch.cuda.set_device(0)
+    path = model_file(0, None, 0)
+    tokens, pooler, ds = config3_inputs()
+    n = len(tokens)
+    eng = Engine(path, max_context=n + PREFILL_DECODE + 64, max_pass=n, max_steps=PREFILL_DECODE + 8,
+                 kv_dtype="bf16", steps_per_graph=8)
+    eng.stop_on_eos = False
+    K, W = args.steps, args.warmup
+    for _ in range(W):
+        eng.generate_vision(tokens, PREFILL_DECODE, pooler=pooler, deepstack=ds, grid=(LLM_H, LLM_W))
+    pre_ms, dec_ms, wall_ms = [], [], []
+    with Clocks(0) as clk:
+        for _ in range(K):
+            t0 = time.perf_counter()
+            out = eng.generate_vision(tokens, PREFILL_DECODE, pooler=pooler, deepstack=ds, grid=(LLM_H, LLM_W))
+            wall_ms.append((time.perf_counter() - t0) * 1e3)
+            t = eng.last_timing
+            pre_ms.append(t.prefill_ms)
+            dec_ms.append(t.decode_ms)
+    eng.close()
+    pm = statistics.median(pre_ms)
+    fl = prefill_flops(n)
+    peaks_d = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    tpk = float(peaks_d.get("bf16_tflops_sustained", 1400.0))
+    ach = fl / (pm / 1e3) / 1e12
+    print(json.dumps({
+        "metric": "multimodal prefill tokens/s (config 3)", "value": round(n / (pm / 1e3), 1), "unit": "tokens/s",
+        "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": round(pm, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 operands (q4s weights dequantised), fp32 accumulate",
+        "data": "synthetic (seeded weights; N(0,1) bf16-valued visual rows)",
+        "config": {"workload": f"config 3: {N_VIS} visual ({LLM_H}x{LLM_W}) + {N_TEXT} text rows, DeepStack, then "
+                               f"{PREFILL_DECODE} greedy steps", "prompt_tokens": n},
+        "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": tpk, "unit": "TFLOP/s",
+                     "frac": round(ach / tpk, 4), "traffic": None,
+                     "note": f"{fl / 1e12:.3f} TFLOP of linear layers per prefill over the whole prefill call "
+                             "(GEMMs, attention, norms, and the last row's decode step); peak: measured sustained bf16"},
+        "decode_ms_per_token": round(statistics.median(dec_ms) / PREFILL_DECODE, 4),
+        "e2e": {"value": round(statistics.median(wall_ms), 2), "unit": "ms per request",
+                "h2d_bytes_per_step": int(4 * N_VIS * H * 4 + n * 4), "d2h_bytes_per_step": 4 * PREFILL_DECODE,
+                "api": "icua_generate (host pooler/DeepStack/tokens in, host tokens out)"},
+        "generated": len(out), "clocks": clk.summary(),
+    }))
+
+
 def run_reference(args):
     """The reference's own CPU path (the numpy port of tools/reference/qwen3vl_ref.py): each step
     decodes one token at 4K context through a 4-of-28-layer sample plus 1/7 of the lm_head rows,
@@ -339,11 +489,18 @@ def main():
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro", action="store_true", help="config 1: per-shape GEMV microbench")
+    ap.add_argument("--micro-shape", default="", help="run only the microbench shapes whose name contains this")
+    ap.add_argument("--prefill", action="store_true", help="config 3: multimodal prefill through the GEMM path")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.micro:
+        run_micro(args)
+    elif args.prefill:
+        run_prefill(args)
     else:
         run_ours(args)
 

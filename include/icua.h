@@ -73,6 +73,9 @@ typedef struct {
     int32_t format;         /* ICUA_FMT_* */
     int32_t kv_dtype;       /* ICUA_KV_* */
     int32_t steps_per_graph;/* decode steps captured per CUDA graph launch (>=1) */
+    int32_t prefill_gemm_min;/* prompts whose rows before the last number at least this many run
+                              * through the tensor-core GEMM path; shorter ones through the decode
+                              * kernels row by row.  0 = always row by row.  Default 64. */
 } icua_config;
 
 /* Mirrors Engine.Timing (Engine.swift:44-51); times are device times from CUDA events. */
@@ -137,6 +140,20 @@ icua_status icua_decode(icua_engine* eng, int32_t session, int32_t max_new, int3
  * The step's logits are kept for icua_get_logits. */
 icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token, int32_t* out_token);
 
+/* Batched greedy decode (the serving counterpart of icua_decode): every step
+ * decodes one token for each of n_sessions sessions together -- tensor-core GEMMs over the session
+ * rows, per-session attention over each session's own cache, the tied lm_head with a per-row
+ * argmax -- for `steps` steps.  in_tokens: n_sessions input tokens, or NULL to continue each session
+ * from its last token (the session must have been prefilled).  out: [n_sessions][steps] tokens; a
+ * session that stops (EOS when stop_on_eos, as icua_decode) has -1 after its EOS token.
+ * n_sessions <= max_pass; sessions distinct.  The arithmetic is the prefill path's (fp16 operands,
+ * fp32 accumulation), so tokens can differ from icua_decode's where two logits nearly tie. */
+icua_status icua_decode_batch(icua_engine* eng, const int32_t* sessions, int32_t n_sessions,
+                              const int32_t* in_tokens, int32_t steps, int32_t* out);
+/* The next icua_decode_batch calls copy the last step's fp32 logits [n_rows][vocab] (rows in the
+ * call's session order) to host_out; NULL / 0 turns it off. */
+icua_status icua_capture_batch_logits(icua_engine* eng, float* host_out, int32_t n_rows);
+
 /* Whole call: reset session, prefill, decode; returns tokens like generateVision. */
 icua_status icua_generate(icua_engine* eng, int32_t session, const int32_t* tokens, int32_t n,
                           const icua_visual* visual, int32_t max_new, int32_t write_first_logits,
@@ -173,6 +190,14 @@ icua_status icua_pack_matrix(int32_t fmt, int32_t n_rows, int32_t k, const void*
  * or NULL.  No scratch memory: every CTA owns whole 16-row tiles. */
 icua_status icua_gemv(int32_t fmt, int32_t n_rows, int32_t k, const void* packed_dev,
                       const void* x_dev, int32_t x_dtype, float* y_dev, void* stream);
+/* y[m_tok, n_rows] (fp32, row-major) = x[m_tok, k] (fp16, row-major, 16-byte aligned) W^T, W a q4s
+ * matrix in the device tile layout: the tensor-core dequant-GEMM of prefill (tcgen05.mma with
+ * TMEM accumulators, TMA-fed activations; weights dequantised as half(q) * half(scale), the rule
+ * of the reference prefill GEMM llm_gemm_tile, Shaders.swift:927-1097) with a plain store
+ * epilogue.  n_rows a multiple of 128, k a multiple of 1024 up to 6144, m_tok >= 1.  err_dev:
+ * optional device int32 OR-ed with error flags when a bounded wait gives up (NULL: not reported). */
+icua_status icua_gemm_q4s(int32_t n_rows, int32_t k, int32_t m_tok, const void* packed_dev, const void* x_dev,
+                          float* y_dev, int32_t* err_dev, void* stream);
 /* Greedy head on the device: token = argmax_v (embed_v . RMSNorm(x) * norm_w), the tied q8 lm_head
  * of the reference (k_lm_head + k_commit, Shaders.swift:1452-1547; lowest index wins ties).
  * packed_embed_dev: q8 [vocab, 2048] in the device layout (icua_pack_matrix); x_dev fp32 [2048];

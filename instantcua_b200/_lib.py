@@ -22,7 +22,8 @@ TENSOR_COUNT = 710
 class IcuaConfig(C.Structure):
     _fields_ = [("device", C.c_int32), ("n_layers", C.c_int32), ("vocab", C.c_int32), ("max_context", C.c_int32),
                 ("max_pass", C.c_int32), ("max_steps", C.c_int32), ("max_sessions", C.c_int32),
-                ("format", C.c_int32), ("kv_dtype", C.c_int32), ("steps_per_graph", C.c_int32)]
+                ("format", C.c_int32), ("kv_dtype", C.c_int32), ("steps_per_graph", C.c_int32),
+                ("prefill_gemm_min", C.c_int32)]
 
 
 class IcuaTiming(C.Structure):
@@ -71,6 +72,9 @@ PROTOTYPES = {
     "icua_packed_bytes": (C.c_uint64, [_I, _I, _I]),
     "icua_pack_matrix": (_I, [_I, _I, _I, _P, _P, _P]),
     "icua_gemv": (_I, [_I, _I, _I, _P, _P, _I, _P, _P]),
+    "icua_decode_batch": (_I, [_P, _IP, _I, _IP, _I, _IP]),
+    "icua_capture_batch_logits": (_I, [_P, _FP, _I]),
+    "icua_gemm_q4s": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),
     "icua_dequant": (_I, [_I, _I, _I, _P, _P, _P]),
     "icua_greedy_head_scratch_bytes": (C.c_uint64, [_I]),
     "icua_greedy_head": (_I, [_I, _P, _P, _P, _P, _P, _P, _P]),

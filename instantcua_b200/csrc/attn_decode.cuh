@@ -42,6 +42,14 @@ struct AttnParams {
     float* part;             // out: [NKV][n_split / cluster][ATT_PART]
     DevState* st;
     L2Plan l2;               // data of later kernels to prefetch into L2
+    // batched decode (blockIdx.y = row): row r uses session rows_sess[r] (state st + session,
+    // cache kc / vc + session * sess_kv_elems, projection qkv + r * qkv_stride) and writes its
+    // normalised output to out16[r][2048] (one part per kv head: n_split == cluster)
+    const int* rows_sess;
+    long long sess_kv_elems;
+    long long sess_rope_elems;  // float2 entries between sessions' RoPE tables
+    int qkv_stride;
+    __half* out16;
 };
 
 template <typename KVT>
@@ -197,6 +205,13 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int NSP = p.n_split;
     const int h = blockIdx.x / NSP, j = blockIdx.x % NSP;
+    const int row = blockIdx.y;
+    const int sess = p.rows_sess != nullptr ? p.rows_sess[row] : 0;
+    DevState* const st = p.st + sess;
+    const float* const qkv = p.qkv + (size_t)row * p.qkv_stride;
+    KVT* const kc = p.kc + sess * p.sess_kv_elems;
+    KVT* const vc = p.vc + sess * p.sess_kv_elems;
+    const float2* const rope = p.rope + sess * p.sess_rope_elems;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bars_off) + warp * ATT_NS;
     uint8_t* ring = smem + S::ring_off + warp * S::ring_warp;
     float* qs = reinterpret_cast<float*>(smem + S::q_off);
@@ -207,13 +222,13 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
 
     // The cache position was written by a kernel at least two launches earlier (the commit or
     // the prompt cursor advance of the previous step), so it can be read before the wait.
-    const int pos = *(volatile int*)&p.st->pos;
+    const int pos = *(volatile int*)&st->pos;
     const long long Ls = pos;
     const int p0 = (int)(Ls * j / NSP), p1 = (int)(Ls * (j + 1) / NSP);
     const int a = p0 + (int)((long long)(p1 - p0) * warp / 8), b = p0 + (int)((long long)(p1 - p0) * (warp + 1) / 8);
     const int n_chunks = (b - a + ATT_SLOT - 1) / ATT_SLOT;
-    const KVT* kbase = p.kc + (long long)h * p.max_ctx * HD;
-    const KVT* vbase = p.vc + (long long)h * p.max_ctx * HD;
+    const KVT* kbase = kc + (long long)h * p.max_ctx * HD;
+    const KVT* vbase = vc + (long long)h * p.max_ctx * HD;
 
     auto issue = [&](int c) {
         const int r0 = a + c * ATT_SLOT;
@@ -238,13 +253,13 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
         const float4 w4 = *reinterpret_cast<const float4*>((warp < 2 ? p.q_norm : p.k_norm) + 4 * lane);
         nw[0] = w4.x; nw[1] = w4.y; nw[2] = w4.z; nw[3] = w4.w;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) cs4[e] = p.rope[(long long)pos * 64 + 4 * (lane & 15) + e];
+        for (int e = 0; e < 4; ++e) cs4[e] = rope[(long long)pos * 64 + 4 * (lane & 15) + e];
     }
     __syncwarp();
 
     pdl_wait();
 
-    if (*(volatile int*)&p.st->done) {  // uniform over the grid: no CTA reaches the cluster barriers
+    if (*(volatile int*)&st->done) {  // uniform over the grid: no CTA reaches the cluster barriers
         pdl_launch_dependents();
         if (lane == 0)
             for (int c = 0; c < min(ATT_NS, n_chunks); ++c) mbar_wait_bounded(&bars[c], 0);
@@ -254,7 +269,7 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
     // ---- q/k norm + RoPE for the new position: warp 0/1 -> q heads 2h, 2h+1, warp 2 -> k, 3 -> v ----
     if (warp < 4) {
         const int base = warp < 2 ? (2 * h + warp) * HD : (warp == 2 ? 2048 + h * HD : 3072 + h * HD);
-        const float4 x4 = *reinterpret_cast<const float4*>(p.qkv + base + 4 * lane);
+        const float4 x4 = *reinterpret_cast<const float4*>(qkv + base + 4 * lane);
         float x[4] = {x4.x, x4.y, x4.z, x4.w};
         if (warp < 3) {
             const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
@@ -284,8 +299,8 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
     __syncthreads();
     pdl_launch_dependents();  // after the latency-bound q/k/v loads
     if (j == 0 && tid < HD) {  // append the new row (already in the swizzled order)
-        p.kc[((long long)h * p.max_ctx + pos) * HD + tid] = knew[tid];
-        p.vc[((long long)h * p.max_ctx + pos) * HD + tid] = vnew[tid];
+        kc[((long long)h * p.max_ctx + pos) * HD + tid] = knew[tid];
+        vc[((long long)h * p.max_ctx + pos) * HD + tid] = vnew[tid];
     }
 
     // ---- per-warp flash-decode over rows [a, b) ------------------------------------------------
@@ -313,7 +328,7 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
     for (int c = 0; c < n_chunks; ++c) {
         const int slot = c % ATT_NS;
         if (!mbar_wait_bounded(&bars[slot], (uint32_t)((c / ATT_NS) & 1))) {
-            if (lane == 0) atomicOr(&p.st->error, ERR_WAIT_ATTN);
+            if (lane == 0) atomicOr(&st->error, ERR_WAIT_ATTN);
             break;  // keep going to the cluster barriers with what we have
         }
         const uint32_t kslot = smem_u32(ring + slot * S::slot_bytes);
@@ -389,10 +404,14 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
                 Lsum = fmaf(ld_dsmem(&cpart[2 + hh], q), f, Lsum);
                 O = fmaf(ld_dsmem(&cpart[4 + hh * HD + d], q), f, O);
             }
-            out[4 + hh * HD + d] = O;
-            if (d == 0) {
-                out[hh] = M;
-                out[2 + hh] = Lsum;
+            if (p.out16 != nullptr) {
+                p.out16[(size_t)row * H + (2 * h + hh) * HD + d] = __float2half_rn(O / Lsum);
+            } else {
+                out[4 + hh * HD + d] = O;
+                if (d == 0) {
+                    out[hh] = M;
+                    out[2 + hh] = Lsum;
+                }
             }
         }
     }

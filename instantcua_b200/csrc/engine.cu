@@ -13,6 +13,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdarg>
@@ -23,11 +24,16 @@
 #include <string>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 #include "../../include/icua.h"
 #include "attn_decode.cuh"
+#include "batch.cuh"
 #include "common.cuh"
+#include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "misc.cuh"
+#include "prefill.cuh"
 
 namespace icua_host {
 uint16_t f32_to_f16_bits(float f);
@@ -103,6 +109,28 @@ struct icua_engine {
     icua_timing timing{};
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     float inv_freq[64];
+    // prefill rows through the tensor-core GEMM (max_pass rows each)
+    float *px = nullptr, *pqkv = nullptr, *pq = nullptr;
+    __half *pxn = nullptr, *pattn = nullptr, *ph = nullptr;
+    CUtensorMap map_xn{}, map_attn{}, map_h{};  // TMA maps of the fp16 GEMM inputs
+    int* gemm_err = nullptr;                     // error flags of the batched kernels
+    // sessions (contiguous arrays; Session holds pointers into them)
+    DevState* st_all = nullptr;
+    int* out_all = nullptr;
+    float2* rope_all = nullptr;
+    void* kc_all = nullptr;
+    void* vc_all = nullptr;
+    size_t kv_elems = 0;  // cache elements of one session (all layers, K or V)
+    int out_stride = 0;
+    // batched decode: row -> session table, lm_head argmax partials, cached graphs
+    int* batch_rows = nullptr;
+    float* batch_best_v = nullptr;
+    int* batch_best_i = nullptr;
+    std::vector<int> batch_key;
+    cudaGraphExec_t g_batch1 = nullptr, g_batchn = nullptr;
+    float* batch_logits = nullptr;  // [rows][vocab] of the last batched step, when requested
+    float* batch_logits_host = nullptr;
+    int batch_logits_rows = 0;
 };
 
 namespace {
@@ -197,6 +225,59 @@ cudaError_t launch_gemv(const Matrix& m, const GemvParams& p, cudaStream_t s, bo
     return launch(gemv_kernel<FMT, EPI, KMAX, STREAM, IN>, m.grid, nt, smem, s, pdl, p);
 }
 
+// ---- tensor-core GEMM launch ------------------------------------------------------------------
+constexpr int TC_BN = 128;  // tokens per CTA tile of the prefill GEMMs
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// TMA map of an fp16 activation matrix [rows, k] (k contiguous): boxes of 64 columns (128 bytes,
+// the swizzle span) x box_rows rows, SWIZZLE_128B, rows past `rows` read as zeros.
+bool make_act_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows) {
+    auto enc = tensor_map_encoder();
+    if (!enc || ((uintptr_t)base & 15) || k % 64 || rows < 1) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+TcGemmParams tc_params(const Matrix& m, int m_tok, int* err) {
+    TcGemmParams p{};
+    p.w = m.dev;
+    p.n_rows = m.n_rows;
+    p.k = m.k;
+    p.n_tiles = m.n_tiles;
+    p.upt = m.k / 64;
+    p.m_tok = m_tok;
+    p.err = err;
+    return p;
+}
+
+template <int EPI, int FMT = FMT_Q4S>
+cudaError_t launch_tc_gemm(const CUtensorMap& map, const TcGemmParams& p, cudaStream_t s) {
+    if (p.n_rows % TC_BM || p.k % TC_BK || p.m_tok < 1) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.n_rows / TC_BM, (p.m_tok + TC_BN - 1) / TC_BN);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = TcSmem<TC_BN, FMT>::alloc;
+    cfg.stream = s;
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<TC_BN, EPI, FMT>, map, p);
+}
+
 cudaError_t set_smem_attrs() {
     static bool done = false;
     if (done) return cudaSuccess;
@@ -227,6 +308,19 @@ cudaError_t set_smem_attrs() {
     SETA(advance_kernel);
     SETA(argmax_parts_kernel);
 #undef SETA
+    for (const void* k : {(const void*)tc_gemm_kernel<TC_BN, TC_STORE>, (const void*)tc_gemm_kernel<TC_BN, TC_RESID>,
+                          (const void*)tc_gemm_kernel<TC_BN, TC_SWIGLU>}) {
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TcSmem<TC_BN>::alloc)) != cudaSuccess)
+            return e;
+    }
+    if ((e = cudaFuncSetAttribute(tc_gemm_kernel<TC_BN, TC_ARGMAX, FMT_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  TcSmem<TC_BN, FMT_Q8>::alloc)) != cudaSuccess)
+        return e;
+    for (const void* k : {(const void*)prefill_attn_kernel<__half>, (const void*)prefill_attn_kernel<__nv_bfloat16>}) {
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      PrefillAttnSmem<__half>::total)) != cudaSuccess)
+            return e;
+    }
     done = true;
     return cudaSuccess;
 }
@@ -562,6 +656,181 @@ icua_status try_finalize(icua_engine* eng) {
     return ICUA_OK;
 }
 
+// Prompt rows [0, n_rows) at cache slots S.pos .. through the tensor-core path (reference
+// encodePrefill, Engine.swift:476-630): embed, then per layer RMSNorm -> QKV GEMM -> QK norm +
+// RoPE + KV append -> causal attention -> o-proj GEMM + residual -> RMSNorm -> gate/up GEMM +
+// SwiGLU -> down GEMM + residual (+ DeepStack rows after layers 0..2).  The last layer only
+// appends K/V: the prompt's final row, whose logits are needed, runs through the decode step
+// afterwards (the reference's last-layer shortcut, Engine.swift:525-528).
+template <typename KVT>
+cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_off, int n_vis) {
+    cudaError_t err;
+    cudaStream_t st = e->stream;
+    const int L = e->cfg.n_layers, pos0 = S.pos;
+    int* errp = &S.st->error;
+    if ((err = launch(prefill_embed_kernel, n_rows, 256, 0, st, false, (const int*)S.prompt, n_rows, vis_off, n_vis,
+                      (const float*)e->pooler, (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->px)) != cudaSuccess)
+        return err;
+    const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
+    for (int l = 0; l < L; ++l) {
+        Layer& ly = e->layers[l];
+        KVT* kc = reinterpret_cast<KVT*>(S.kc) + kv_layer * l;
+        KVT* vc = reinterpret_cast<KVT*>(S.vc) + kv_layer * l;
+        if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
+                          (const float*)ly.attn_norm, n_rows, e->pxn)) != cudaSuccess)
+            return err;
+        TcGemmParams p = tc_params(ly.qkv, n_rows, errp);
+        p.out = e->pqkv;
+        p.ldo = QKV_ROWS;
+        if ((err = launch_tc_gemm<TC_STORE>(e->map_xn, p, st)) != cudaSuccess) return err;
+        if ((err = launch(qk_rope_kv_kernel<KVT>, n_rows, 256, 0, st, false, (const float*)e->pqkv, n_rows,
+                          (const float*)ly.q_norm, (const float*)ly.k_norm, (const float2*)S.rope, pos0, kc, vc,
+                          e->cfg.max_context, e->pq)) != cudaSuccess)
+            return err;
+        if (l == L - 1) break;
+        {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((n_rows + PA_BQ - 1) / PA_BQ, NKV);
+            cfg.blockDim = dim3(256);
+            cfg.dynamicSmemBytes = PrefillAttnSmem<KVT>::total;
+            cfg.stream = st;
+            if ((err = cudaLaunchKernelEx(&cfg, prefill_attn_kernel<KVT>, (const float*)e->pq, (const KVT*)kc,
+                                          (const KVT*)vc, e->cfg.max_context, n_rows, pos0, e->pattn, errp)) != cudaSuccess)
+                return err;
+        }
+        p = tc_params(ly.o, n_rows, errp);
+        p.out = e->px;
+        p.ldo = H;
+        if ((err = launch_tc_gemm<TC_RESID>(e->map_attn, p, st)) != cudaSuccess) return err;
+        if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
+                          (const float*)ly.mlp_norm, n_rows, e->pxn)) != cudaSuccess)
+            return err;
+        p = tc_params(ly.gu, n_rows, errp);
+        p.out_h = e->ph;
+        p.ldh = FF;
+        if ((err = launch_tc_gemm<TC_SWIGLU>(e->map_xn, p, st)) != cudaSuccess) return err;
+        p = tc_params(ly.d, n_rows, errp);
+        p.out = e->px;
+        p.ldo = H;
+        if (l < 3 && vis_off >= 0) {
+            p.deepstack = e->deepstack[l];
+            p.ds_row0 = vis_off;
+            p.ds_rows = n_vis;
+        }
+        if ((err = launch_tc_gemm<TC_RESID>(e->map_h, p, st)) != cudaSuccess) return err;
+    }
+    return cudaSuccess;
+}
+
+// One batched decode step over rows [0, n_rows) (row r -> session eng->batch_rows[r]): embedding
+// of each session's current token, the layers through the tensor-core GEMMs with per-row
+// attention, the tied lm_head GEMM with per-row argmax partials, and the per-session commit.
+template <typename KVT>
+cudaError_t record_batch_step(icua_engine* e, int n_rows) {
+    cudaError_t err;
+    cudaStream_t st = e->stream;
+    const int L = e->cfg.n_layers;
+    if ((err = launch(batch_embed_kernel, n_rows, 256, 0, st, false, (const int*)e->batch_rows,
+                      (const DevState*)e->st_all, (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->px)) != cudaSuccess)
+        return err;
+    const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
+    for (int l = 0; l < L; ++l) {
+        Layer& ly = e->layers[l];
+        if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
+                          (const float*)ly.attn_norm, n_rows, e->pxn)) != cudaSuccess)
+            return err;
+        TcGemmParams p = tc_params(ly.qkv, n_rows, e->gemm_err);
+        p.out = e->pqkv;
+        p.ldo = QKV_ROWS;
+        if ((err = launch_tc_gemm<TC_STORE>(e->map_xn, p, st)) != cudaSuccess) return err;
+        {
+            AttnParams<KVT> a{};
+            a.qkv = e->pqkv;
+            a.qkv_stride = QKV_ROWS;
+            a.q_norm = ly.q_norm;
+            a.k_norm = ly.k_norm;
+            a.rope = e->rope_all;
+            a.sess_rope_elems = (long long)e->cfg.max_context * 64;
+            a.kc = reinterpret_cast<KVT*>(e->kc_all) + kv_layer * l;
+            a.vc = reinterpret_cast<KVT*>(e->vc_all) + kv_layer * l;
+            a.sess_kv_elems = (long long)e->kv_elems;
+            a.max_ctx = e->cfg.max_context;
+            a.n_split = e->att_cluster;  // one cluster per (row, kv head): one part, normalised in place
+            a.cluster = e->att_cluster;
+            a.part = e->att_part;
+            a.st = e->st_all;
+            a.rows_sess = e->batch_rows;
+            a.out16 = e->pattn;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(NKV * a.n_split, n_rows);
+            cfg.blockDim = dim3(256);
+            cfg.dynamicSmemBytes = AttnSmem<KVT>::total;
+            cfg.stream = st;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = a.cluster;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            if ((err = cudaLaunchKernelEx(&cfg, attn_decode_kernel<KVT>, a)) != cudaSuccess) return err;
+        }
+        p = tc_params(ly.o, n_rows, e->gemm_err);
+        p.out = e->px;
+        p.ldo = H;
+        if ((err = launch_tc_gemm<TC_RESID>(e->map_attn, p, st)) != cudaSuccess) return err;
+        if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
+                          (const float*)ly.mlp_norm, n_rows, e->pxn)) != cudaSuccess)
+            return err;
+        p = tc_params(ly.gu, n_rows, e->gemm_err);
+        p.out_h = e->ph;
+        p.ldh = FF;
+        if ((err = launch_tc_gemm<TC_SWIGLU>(e->map_xn, p, st)) != cudaSuccess) return err;
+        p = tc_params(ly.d, n_rows, e->gemm_err);
+        p.out = e->px;
+        p.ldo = H;
+        if ((err = launch_tc_gemm<TC_RESID>(e->map_h, p, st)) != cudaSuccess) return err;
+    }
+    if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
+                      (const float*)e->final_norm, n_rows, e->pxn)) != cudaSuccess)
+        return err;
+    TcGemmParams p = tc_params(e->embed, n_rows, e->gemm_err);
+    p.best_v = e->batch_best_v;
+    p.best_i = e->batch_best_i;
+    p.out = e->batch_logits;  // nullptr unless the logits of the step were requested
+    p.ldo = e->cfg.vocab;
+    if ((err = launch_tc_gemm<TC_ARGMAX, FMT_Q8>(e->map_xn, p, st)) != cudaSuccess) return err;
+    return launch(batch_commit_kernel, n_rows, 256, 0, st, false, (const float*)e->batch_best_v,
+                  (const int*)e->batch_best_i, e->cfg.vocab / TC_BM, n_rows, (const int*)e->batch_rows, e->st_all,
+                  e->out_all, e->out_stride);
+}
+
+void drop_batch_graphs(icua_engine* e) {
+    if (e->g_batch1) cudaGraphExecDestroy(e->g_batch1);
+    if (e->g_batchn) cudaGraphExecDestroy(e->g_batchn);
+    e->g_batch1 = e->g_batchn = nullptr;
+    e->batch_key.clear();
+}
+
+icua_status build_batch_graph(icua_engine* eng, int n_rows, int steps, cudaGraphExec_t* out) {
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(eng->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t err = cudaSuccess;
+    for (int i = 0; i < steps && err == cudaSuccess; ++i)
+        err = eng->cfg.kv_dtype == ICUA_KV_BF16 ? record_batch_step<__nv_bfloat16>(eng, n_rows)
+                                                : record_batch_step<__half>(eng, n_rows);
+    cudaError_t e2 = cudaStreamEndCapture(eng->stream, &g);
+    if (err != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        return fail(eng, ICUA_ERR_CUDA, "batched graph capture: %s", cudaGetErrorString(err));
+    }
+    if (e2 != cudaSuccess) return fail(eng, ICUA_ERR_CUDA, "end capture: %s", cudaGetErrorString(e2));
+    cudaError_t e3 = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e3 != cudaSuccess) return fail(eng, ICUA_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e3));
+    return ICUA_OK;
+}
+
 }  // namespace
 
 // =================================================================================================
@@ -583,6 +852,7 @@ void icua_default_config(icua_config* c) {
     c->format = ICUA_FMT_Q4S;
     c->kv_dtype = ICUA_KV_F16;
     c->steps_per_graph = 8;
+    c->prefill_gemm_min = 64;
 }
 
 icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
@@ -666,16 +936,47 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
     TRY(dalloc_t(eng, &eng->att_part, (size_t)NKV * eng->att_split * ATT_PART));
     TRY(dalloc_t(eng, &eng->cta_best_v, (size_t)eng->n_sm));
     TRY(dalloc_t(eng, &eng->cta_best_i, (size_t)eng->n_sm));
+    {
+        const size_t P = (size_t)cfg->max_pass;
+        TRY(dalloc_t(eng, &eng->px, P * H));
+        TRY(dalloc_t(eng, &eng->pqkv, P * QKV_ROWS));
+        TRY(dalloc_t(eng, &eng->pq, P * NQ * HD));
+        TRY(dalloc_t(eng, &eng->pxn, P * H));
+        TRY(dalloc_t(eng, &eng->pattn, P * H));
+        TRY(dalloc_t(eng, &eng->ph, P * FF));
+        TRY(dalloc_t(eng, &eng->gemm_err, 1));
+        cudaMemset(eng->ph, 0, P * FF * sizeof(__half));
+        cudaMemset(eng->pxn, 0, P * H * sizeof(__half));
+        cudaMemset(eng->pattn, 0, P * H * sizeof(__half));
+        cudaMemset(eng->gemm_err, 0, sizeof(int));
+        if (!make_act_map(&eng->map_xn, eng->pxn, (int)P, H, TC_BN) ||
+            !make_act_map(&eng->map_attn, eng->pattn, (int)P, H, TC_BN) ||
+            !make_act_map(&eng->map_h, eng->ph, (int)P, FF, TC_BN))
+            TRY(fail(eng, ICUA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the prefill activations"));
+    }
+    // Sessions live in contiguous per-engine arrays (state, outputs, RoPE tables, caches), so the
+    // batched decode reaches session s of any row by one stride.
     eng->sessions.resize(cfg->max_sessions);
-    const size_t kv_elems = (size_t)cfg->n_layers * NKV * cfg->max_context * HD;
-    for (auto& S : eng->sessions) {
-        TRY(dalloc_t(eng, &S.st, 1));
+    const size_t NS = (size_t)cfg->max_sessions;
+    eng->kv_elems = (size_t)cfg->n_layers * NKV * cfg->max_context * HD;
+    eng->out_stride = cfg->max_steps + 64;
+    TRY(dalloc_t(eng, &eng->st_all, NS));
+    TRY(dalloc_t(eng, &eng->out_all, NS * eng->out_stride));
+    TRY(dalloc_t(eng, &eng->rope_all, NS * cfg->max_context * 64));
+    TRY(dalloc(eng, &eng->kc_all, NS * eng->kv_elems * 2));
+    TRY(dalloc(eng, &eng->vc_all, NS * eng->kv_elems * 2));
+    TRY(dalloc_t(eng, &eng->batch_rows, (size_t)cfg->max_pass));
+    TRY(dalloc_t(eng, &eng->batch_best_v, (size_t)(cfg->vocab / TC_BM) * cfg->max_pass));
+    TRY(dalloc_t(eng, &eng->batch_best_i, (size_t)(cfg->vocab / TC_BM) * cfg->max_pass));
+    cudaMemset(eng->st_all, 0, NS * sizeof(DevState));
+    for (size_t i = 0; i < NS; ++i) {
+        Session& S = eng->sessions[i];
+        S.st = eng->st_all + i;
         TRY(dalloc_t(eng, &S.prompt, (size_t)cfg->max_pass));
-        TRY(dalloc_t(eng, &S.out_tokens, (size_t)cfg->max_steps + 64));
-        TRY(dalloc_t(eng, &S.rope, (size_t)cfg->max_context * 64));
-        TRY(dalloc(eng, &S.kc, kv_elems * 2));
-        TRY(dalloc(eng, &S.vc, kv_elems * 2));
-        cudaMemset(S.st, 0, sizeof(DevState));
+        S.out_tokens = eng->out_all + i * eng->out_stride;
+        S.rope = eng->rope_all + i * (size_t)cfg->max_context * 64;
+        S.kc = static_cast<uint8_t*>(eng->kc_all) + i * eng->kv_elems * 2;
+        S.vc = static_cast<uint8_t*>(eng->vc_all) + i * eng->kv_elems * 2;
     }
 #undef TRY
     e = cudaDeviceSynchronize();
@@ -695,6 +996,7 @@ void icua_engine_destroy(icua_engine* eng) {
     cudaSetDevice(eng->cfg.device);
     if (eng->stream) cudaStreamSynchronize(eng->stream);
     for (auto& S : eng->sessions) drop_graphs(S);
+    drop_batch_graphs(eng);
     for (void* p : eng->allocations) cudaFree(p);
     for (int i = 0; i < 4; ++i)
         if (eng->ev[i]) cudaEventDestroy(eng->ev[i]);
@@ -877,7 +1179,7 @@ icua_status icua_capture_step_logits(icua_engine* eng, float* host_out, int32_t 
 
 // Writes the prompt, visual rows, RoPE table and loop state; returns via *pos0 the start position.
 static icua_status prepare_prefill(icua_engine* eng, Session& S, int session, const int32_t* tokens, int n,
-                                   const icua_visual* vis, int write_logits) {
+                                   const icua_visual* vis, int write_logits, int* vis_off_out, int* n_vis_out) {
     const int C = eng->cfg.max_context;
     if (n < 1 || n > eng->cfg.max_pass) return fail(eng, ICUA_ERR_CAPACITY, "prompt of %d tokens (max_pass %d)", n, eng->cfg.max_pass);
     if (S.pos + n + 1 > C) return fail(eng, ICUA_ERR_CAPACITY, "context %d + %d exceeds max_context %d", S.pos, n, C);
@@ -930,6 +1232,8 @@ static icua_status prepare_prefill(icua_engine* eng, Session& S, int session, co
     hs.n_vis = n_vis;
     hs.write_logits = write_logits ? 1 : 0;
     hs.session = session;
+    *vis_off_out = vis_off;
+    *n_vis_out = n_vis;
     CK(cudaMemcpyAsync(S.st, &hs, sizeof hs, cudaMemcpyHostToDevice, eng->stream));
     CK(cudaStreamSynchronize(eng->stream));  // host staging buffers go out of scope
     S.step = 0;
@@ -946,9 +1250,21 @@ icua_status icua_prefill(icua_engine* eng, int32_t session, const int32_t* token
     if (!S) return fail(eng, ICUA_ERR_INVALID, "session %d out of range", session);
     CK(cudaSetDevice(eng->cfg.device));
     if ((s = ensure_graphs(eng, *S)) != ICUA_OK) return s;
-    if ((s = prepare_prefill(eng, *S, session, tokens, n, vis, write_logits)) != ICUA_OK) return s;
+    int vis_off = -1, n_vis = 0;
+    if ((s = prepare_prefill(eng, *S, session, tokens, n, vis, write_logits, &vis_off, &n_vis)) != ICUA_OK) return s;
     CK(cudaEventRecord(eng->ev[0], eng->stream));
-    for (int i = 0; i < n - 1; ++i) CK(cudaGraphLaunch(S->g_prefill_tok, eng->stream));
+    const int n_rows = n - 1;  // rows before the last one, which runs as a decode step
+    if (eng->cfg.prefill_gemm_min > 0 && n_rows >= eng->cfg.prefill_gemm_min) {
+        const cudaError_t e2 = eng->cfg.kv_dtype == ICUA_KV_BF16
+                                   ? record_prefill_rows<__nv_bfloat16>(eng, *S, n_rows, vis_off, n_vis)
+                                   : record_prefill_rows<__half>(eng, *S, n_rows, vis_off, n_vis);
+        if (e2 != cudaSuccess) return fail(eng, ICUA_ERR_CUDA, "prefill launch: %s", cudaGetErrorString(e2));
+        const int pos = S->pos + n_rows;
+        CK(cudaMemcpyAsync(&S->st->pos, &pos, 4, cudaMemcpyHostToDevice, eng->stream));
+        CK(cudaMemcpyAsync(&S->st->prompt_idx, &n_rows, 4, cudaMemcpyHostToDevice, eng->stream));
+    } else {
+        for (int i = 0; i < n_rows; ++i) CK(cudaGraphLaunch(S->g_prefill_tok, eng->stream));
+    }
     CK(cudaGraphLaunch(S->g_step1, eng->stream));
     CK(cudaEventRecord(eng->ev[1], eng->stream));
     if ((s = sync_and_check(eng, *S)) != ICUA_OK) return s;
@@ -1055,6 +1371,124 @@ icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token
     return ICUA_OK;
 }
 
+icua_status icua_decode_batch(icua_engine* eng, const int32_t* sessions, int32_t n_sessions, const int32_t* in_tokens,
+                              int32_t steps, int32_t* out) {
+    if (!eng || !sessions || !out) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    icua_status s;
+    if ((s = check_ready(eng)) != ICUA_OK) return s;
+    if (n_sessions < 1 || n_sessions > eng->cfg.max_pass)
+        return fail(eng, ICUA_ERR_CAPACITY, "%d sessions per batch (1 .. max_pass %d)", n_sessions, eng->cfg.max_pass);
+    if (eng->cfg.vocab % TC_BM) return fail(eng, ICUA_ERR_UNSUPPORTED, "batched decode needs vocab %% 128 == 0");
+    if (steps <= 0) return ICUA_OK;
+    std::vector<int> key(sessions, sessions + n_sessions);
+    {
+        std::vector<int> sorted = key;
+        std::sort(sorted.begin(), sorted.end());
+        if (std::adjacent_find(sorted.begin(), sorted.end()) != sorted.end())
+            return fail(eng, ICUA_ERR_INVALID, "a session appears twice in the batch");
+    }
+    for (int i = 0; i < n_sessions; ++i) {
+        Session* S = get_session(eng, key[i]);
+        if (!S) return fail(eng, ICUA_ERR_INVALID, "session %d out of range", key[i]);
+        if (in_tokens && (in_tokens[i] < 0 || in_tokens[i] >= eng->cfg.vocab))
+            return fail(eng, ICUA_ERR_INVALID, "token %d out of range", in_tokens[i]);
+        if (!in_tokens && S->step < 1) return fail(eng, ICUA_ERR_STATE, "session %d has no token to continue from", key[i]);
+        if (S->pos + steps + eng->cfg.steps_per_graph >= eng->cfg.max_context)
+            return fail(eng, ICUA_ERR_CAPACITY, "session %d: context %d + %d exceeds max_context", key[i], S->pos, steps);
+    }
+    CK(cudaSetDevice(eng->cfg.device));
+    const int spg = eng->cfg.steps_per_graph;
+    if (key != eng->batch_key) {
+        drop_batch_graphs(eng);
+        CK(cudaMemcpy(eng->batch_rows, key.data(), (size_t)n_sessions * 4, cudaMemcpyHostToDevice));
+        if (eng->batch_logits_rows > 0 && eng->batch_logits_rows < n_sessions)
+            return fail(eng, ICUA_ERR_CAPACITY, "batch logits capture holds %d rows", eng->batch_logits_rows);
+        if ((s = build_batch_graph(eng, n_sessions, 1, &eng->g_batch1)) != ICUA_OK) return s;
+        if (steps >= spg && (s = build_batch_graph(eng, n_sessions, spg, &eng->g_batchn)) != ICUA_OK) return s;
+        eng->batch_key = key;
+    } else if (steps >= spg && !eng->g_batchn) {
+        if ((s = build_batch_graph(eng, n_sessions, spg, &eng->g_batchn)) != ICUA_OK) return s;
+    }
+    // per-session step budget: each session runs until it has `steps` more tokens (or stops)
+    std::vector<int> base(n_sessions);
+    for (int i = 0; i < n_sessions; ++i) {
+        Session* S = get_session(eng, key[i]);
+        if (S->step + steps > eng->cfg.max_steps) S->step = 0;  // wrap the output slots, as icua_decode_step
+        base[i] = S->step;
+        struct {
+            int step, done, max_steps, eos0, eos1, stop_on_eos;
+        } head = {S->step, 0, S->step + steps, eng->eos0, eng->eos1, eng->stop_on_eos};
+        CK(cudaMemcpy(&S->st->step, &head, sizeof head, cudaMemcpyHostToDevice));
+        if (in_tokens) CK(cudaMemcpyAsync(&S->st->cur_token, &in_tokens[i], 4, cudaMemcpyHostToDevice, eng->stream));
+    }
+    const int zero = 0;
+    CK(cudaMemcpyAsync(eng->gemm_err, &zero, 4, cudaMemcpyHostToDevice, eng->stream));
+    const auto t0 = std::chrono::steady_clock::now();
+    CK(cudaEventRecord(eng->ev[2], eng->stream));
+    int launched = 0;
+    while (launched + spg <= steps) {
+        CK(cudaGraphLaunch(eng->g_batchn, eng->stream));
+        launched += spg;
+    }
+    while (launched < steps) {
+        CK(cudaGraphLaunch(eng->g_batch1, eng->stream));
+        launched += 1;
+    }
+    CK(cudaEventRecord(eng->ev[3], eng->stream));
+    CK(cudaStreamSynchronize(eng->stream));
+    int gerr = 0;
+    CK(cudaMemcpy(&gerr, eng->gemm_err, 4, cudaMemcpyDeviceToHost));
+    if (gerr) {
+        eng->failed = true;
+        return fail(eng, ICUA_ERR_TIMEOUT, "a bounded device wait gave up in the batched step (flags 0x%x)", gerr);
+    }
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, eng->ev[2], eng->ev[3]);
+    int total = 0;
+    for (int i = 0; i < n_sessions; ++i) {
+        Session* S = get_session(eng, key[i]);
+        if ((s = sync_and_check(eng, *S)) != ICUA_OK) return s;
+        const int got = S->step - base[i];
+        std::vector<int32_t> toks(steps, -1);
+        if (got > 0) CK(cudaMemcpy(toks.data(), S->out_tokens + base[i], (size_t)got * 4, cudaMemcpyDeviceToHost));
+        bool stopped = false;
+        for (int t = 0; t < steps; ++t) {
+            if (stopped || t >= got) {
+                out[(size_t)i * steps + t] = -1;
+                continue;
+            }
+            out[(size_t)i * steps + t] = toks[t];
+            if (eng->stop_on_eos && (toks[t] == eng->eos0 || toks[t] == eng->eos1)) stopped = true;
+            else ++total;
+        }
+    }
+    if (eng->batch_logits_host && eng->batch_logits)
+        CK(cudaMemcpy(eng->batch_logits_host, eng->batch_logits, (size_t)n_sessions * eng->cfg.vocab * 4,
+                      cudaMemcpyDeviceToHost));
+    eng->timing.decode_ms = ms;
+    eng->timing.generated_tokens = total;
+    eng->timing.total_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return ICUA_OK;
+}
+
+icua_status icua_capture_batch_logits(icua_engine* eng, float* host_out, int32_t n_rows) {
+    if (!eng) return fail(nullptr, ICUA_ERR_INVALID, "null engine");
+    CK(cudaSetDevice(eng->cfg.device));
+    drop_batch_graphs(eng);  // the graphs bake the logits pointer
+    if (!host_out || n_rows <= 0) {
+        eng->batch_logits_host = nullptr;
+        eng->batch_logits_rows = 0;
+        eng->batch_logits = nullptr;  // the allocation stays with the engine
+        return ICUA_OK;
+    }
+    if (n_rows > eng->cfg.max_pass) return fail(eng, ICUA_ERR_CAPACITY, "%d rows (max_pass %d)", n_rows, eng->cfg.max_pass);
+    icua_status s;
+    if ((s = dalloc_t(eng, &eng->batch_logits, (size_t)n_rows * eng->cfg.vocab)) != ICUA_OK) return s;
+    eng->batch_logits_host = host_out;
+    eng->batch_logits_rows = n_rows;
+    return ICUA_OK;
+}
+
 icua_status icua_generate(icua_engine* eng, int32_t session, const int32_t* tokens, int32_t n, const icua_visual* vis,
                           int32_t max_new, int32_t write_first_logits, int32_t* out, int32_t* n_out) {
     if (!eng || !tokens || !out || !n_out) return fail(eng, ICUA_ERR_INVALID, "null argument");
@@ -1141,6 +1575,33 @@ icua_status icua_gemv(int32_t fmt, int32_t n_rows, int32_t k, const void* packed
                   : launch_gemv<FMT_Q8, EPI_STORE, 2048, true, IN_BF16>(m, p, s, false);
     }
     CK(err);
+    return ICUA_OK;
+}
+
+// Error flags of standalone GEMM calls made without a caller flag (never read back).
+static __device__ int g_tc_gemm_err_sink;
+
+icua_status icua_gemm_q4s(int32_t n_rows, int32_t k, int32_t m_tok, const void* packed, const void* x, float* y,
+                          int32_t* err_dev, void* stream) {
+    icua_engine* eng = nullptr;
+    if (!packed || !x || !y) return fail(nullptr, ICUA_ERR_INVALID, "null argument");
+    if (n_rows < TC_BM || n_rows % TC_BM || k < 1024 || k % 1024 || k > 6144 || m_tok < 1 || ((uintptr_t)x & 15))
+        return fail(nullptr, ICUA_ERR_INVALID, "unsupported gemm shape (rows %% 128, k %% 1024, k <= 6144, m >= 1, x 16-byte aligned)");
+    CK(set_smem_attrs());
+    CUtensorMap map;
+    if (!make_act_map(&map, x, m_tok, k, TC_BN)) return fail(nullptr, ICUA_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+    int* errp = err_dev;
+    if (!errp) CK(cudaGetSymbolAddress(reinterpret_cast<void**>(&errp), g_tc_gemm_err_sink));
+    Matrix m;
+    m.dev = (uint8_t*)packed;
+    m.fmt = FMT_Q4S;
+    m.n_rows = n_rows;
+    m.k = k;
+    m.n_tiles = n_rows / 16;
+    TcGemmParams p = tc_params(m, m_tok, errp);
+    p.out = y;
+    p.ldo = n_rows;
+    CK(launch_tc_gemm<TC_STORE>(map, p, (cudaStream_t)stream));
     return ICUA_OK;
 }
 

@@ -1,0 +1,396 @@
+// Tensor-core dequant-GEMM for the dense cases (prefill rows, batched decode): tcgen05.mma with
+// the accumulator in tensor memory, weights dequantised from the q4s device tile layout into
+// shared memory by CUDA cores, activations brought in by TMA.
+//
+// Replaces the reference prefill GEMM (llm_gemm_tile + k_g3_*, Shaders.swift:927-1097): fp16
+// activations X [m_tok, K], weights dequantised to fp16 as half(q) * half(scale) (one fp16
+// rounding, the rule of Shaders.swift:958-959 applied to the symmetric int4 codes), fp32
+// accumulation, fused epilogues (store, residual add, SwiGLU into fp16).
+//
+// Design (B200): one CTA computes D[128 weight rows][BN tokens] = W[128, K] X[BN, K]^T as
+// UMMA M=128, N=BN, K=16 steps (kind::f16, both operands K-major with the 128-byte swizzle).
+//   warp 0      producer: 1-D bulk copies of the eight 16-row q4s units of each 64-column
+//               k-block, and a 2-D TMA tile load (box 64 x BN, SWIZZLE_128B) of the activations
+//   warp 1      allocates tensor memory (BN columns) and issues the MMAs (one thread); each
+//               stage is released with tcgen05.commit onto the stage's "empty" barrier
+//   warps 2..5  dequantise each staged unit into the swizzled A tile, then run the epilogue:
+//               tcgen05.ld 32x32b (warp w reads TMEM lanes 32 (w % 4) ..), one weight row per
+//               thread, tokens along the registers
+// Every wait is bounded; a wait that gives up records an error flag, and the kernel still drains
+// its copies and frees its tensor memory before it exits.
+#pragma once
+#include <cuda.h>
+
+#include "common.cuh"
+#include "layout.h"
+
+namespace icua {
+
+constexpr int TC_BM = 128;      // weight rows per CTA (UMMA M)
+constexpr int TC_BK = 64;       // columns per stage: one 128-byte swizzle row of fp16
+constexpr int TC_THREADS = 192;
+
+enum TcEpi { TC_STORE = 0, TC_RESID = 1, TC_SWIGLU = 2, TC_ARGMAX = 3 };
+
+struct TcGemmParams {
+    const uint8_t* w;          // q4s device tile layout [n_rows, k]
+    int n_rows, k, n_tiles, upt;
+    int m_tok;                 // activation rows (tokens)
+    float* out;                // TC_STORE: out[tok * ldo + row] = y; TC_RESID: out[...] += y
+    int ldo;
+    __half* out_h;             // TC_SWIGLU: out_h[tok * ldh + j] = silu(gate_j) * up_j
+    int ldh;
+    const float* deepstack;    // TC_RESID: optional rows added after the residual, [ds_rows][ldo]
+    int ds_row0, ds_rows;      // token range [ds_row0, ds_row0 + ds_rows) that receives them
+    float* best_v;             // TC_ARGMAX: per (row tile, token) maximum [gridDim.x][m_tok] and the
+    int* best_i;               //   row of it (lowest row on ties); out, when set, also gets the values
+    int* err;                  // error flags (bounded waits that gave up)
+};
+
+template <int BN, int FMT = FMT_Q4S>
+struct TcSmem {
+    static constexpr int a_bytes = TC_BM * 128;                // fp16 [128][64], swizzled
+    static constexpr int b_bytes = BN * 128;                   // fp16 [BN][64], swizzled by TMA
+    static constexpr int raw_bytes = 8 * unit_bytes(FMT);      // eight 16-row units
+    static constexpr int stage_bytes = a_bytes + b_bytes + raw_bytes;
+    // pipeline stages: as many as fit (at most 6) next to the argmax scratch and barriers
+    static constexpr int S_fit = (225 * 1024 - 4 * BN * 8 - 1024 - 256) / stage_bytes;
+    static constexpr int S = S_fit < 6 ? S_fit : 6;
+    static constexpr int a_off = 0;
+    static constexpr int b_off = a_off + S * a_bytes;
+    static constexpr int raw_off = b_off + S * b_bytes;
+    static constexpr int bar_off = raw_off + S * raw_bytes;    // rawfull, bfull, afull, empty [S]; accfull
+    static constexpr int tmem_off = bar_off + (4 * S + 1) * 8;
+    static constexpr int red_off = tmem_off + 16;               // TC_ARGMAX: [4 warps][BN] (value, row)
+    static constexpr int total = red_off + 4 * BN * 8;
+    static constexpr int alloc = total + 1024;                 // room to align the tiles to 1024 B
+    static constexpr uint32_t tmem_cols = BN < 32 ? 32 : BN;
+    static_assert(S >= 2 && alloc <= 227 * 1024, "GEMM shared memory");
+};
+
+// ---- tcgen05 / TMA helpers ------------------------------------------------------------------
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart
+// (stride byte offset), descriptor version 1, layout type 2 (SWIZZLE_128B).  The leading byte
+// offset is unused for swizzled K-major layouts and set to 1.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulator, fp16 A and B, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrives on `bar` once every tcgen05.mma issued so far by this thread has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes: lane i of the warp gets lane
+// (base lane + i), columns col .. col + 31.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 2-D TMA tile load (no multicast).  x (the contiguous dimension) is a multiple of 64 elements.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Byte offset of element (row, k) of a [rows][64] fp16 tile in the 128-byte swizzle: row r at
+// r * 128, its 16-byte chunk c at position c ^ (r & 7) (the TMA SWIZZLE_128B pattern).
+__device__ __forceinline__ int sw128_off(int row, int k) {
+    return row * 128 + ((((k >> 3) ^ (row & 7))) << 4) + ((k & 7) << 1);
+}
+
+// Dequantises lane l's 16 bytes of one q4s unit (rows row0 .. row0 + 15, 64 columns) into the
+// swizzled A tile.  The lane holds rows g = l / 4 and g + 8 at columns 16 s + 2t (+1, +8, +9)
+// for s = 0..3; codes u in 0..15 mean q = u - 8.  fp16(1024 + u) is built by OR-ing u into the
+// mantissa of 1024, 1032 is subtracted exactly and the scale applied with one fp16 rounding.
+__device__ __forceinline__ void dequant_q4s_lane(const uint8_t* unit, int l, uint8_t* A, int row0) {
+    const uint4 nib = *reinterpret_cast<const uint4*>(unit + l * 16);
+    const int g = l >> 2, t = l & 3;
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(unit + 512 + g * 8);  // ra g0, rb g0, ra g1, rb g1
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032
+    const int ra = row0 + g, rb = ra + 8;
+    const uint32_t w[4] = {nib.x, nib.y, nib.z, nib.w};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const __half sa1 = __ushort_as_half(sc[(s >> 1) * 2]), sb1 = __ushort_as_half(sc[(s >> 1) * 2 + 1]);
+        const __half2 sa = __halves2half2(sa1, sa1), sb = __halves2half2(sb1, sb1);
+        const int k0 = 16 * s + 2 * t;
+        const uint32_t v = w[s];
+        uint32_t h[4];
+        h[0] = (v & 0x000F000Fu) | 0x64006400u;          // row a, k0 / k0+1
+        h[1] = ((v >> 4) & 0x000F000Fu) | 0x64006400u;   // row b, k0 / k0+1
+        h[2] = ((v >> 8) & 0x000F000Fu) | 0x64006400u;   // row a, k0+8 / k0+9
+        h[3] = ((v >> 12) & 0x000F000Fu) | 0x64006400u;  // row b, k0+8 / k0+9
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            __half2 x = *reinterpret_cast<__half2*>(&h[i]);
+            x = __hmul2(__hsub2(x, bias), (i & 1) ? sb : sa);
+            h[i] = *reinterpret_cast<uint32_t*>(&x);
+        }
+        *reinterpret_cast<uint32_t*>(A + sw128_off(ra, k0)) = h[0];
+        *reinterpret_cast<uint32_t*>(A + sw128_off(rb, k0)) = h[1];
+        *reinterpret_cast<uint32_t*>(A + sw128_off(ra, k0 + 8)) = h[2];
+        *reinterpret_cast<uint32_t*>(A + sw128_off(rb, k0 + 8)) = h[3];
+    }
+}
+
+// q8 counterpart: lane l's bytes of one q8 unit (offset-binary codes u = q + 128).  For k16 step
+// s the lane's 8 bytes sit at (s / 2) * 512 + l * 16 + (s % 2) * 8: rows a/b interleaved at
+// columns k0, k0+1, then k0+8, k0+9.  fp16(1024 + u) - 1152 = q exactly, then one fp16 rounding
+// of q * scale (the reference prefill rule half4(char4) * s, Shaders.swift:958-959).
+__device__ __forceinline__ void dequant_q8_lane(const uint8_t* unit, int l, uint8_t* A, int row0) {
+    const int g = l >> 2, t = l & 3;
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(unit + 1024 + g * 8);
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+    const int ra = row0 + g, rb = ra + 8;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const __half sa1 = __ushort_as_half(sc[(s >> 1) * 2]), sb1 = __ushort_as_half(sc[(s >> 1) * 2 + 1]);
+        const __half2 sa = __halves2half2(sa1, sa1), sb = __halves2half2(sb1, sb1);
+        const int k0 = 16 * s + 2 * t;
+        const uint2 w = *reinterpret_cast<const uint2*>(unit + (s >> 1) * 512 + l * 16 + (s & 1) * 8);
+        uint32_t h[4];
+        h[0] = __byte_perm(w.x, 0x6464u, 0x5240);  // row a, k0 / k0+1
+        h[1] = __byte_perm(w.x, 0x6464u, 0x5341);  // row b, k0 / k0+1
+        h[2] = __byte_perm(w.y, 0x6464u, 0x5240);  // row a, k0+8 / k0+9
+        h[3] = __byte_perm(w.y, 0x6464u, 0x5341);  // row b, k0+8 / k0+9
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            __half2 x = *reinterpret_cast<__half2*>(&h[i]);
+            x = __hmul2(__hsub2(x, bias), (i & 1) ? sb : sa);
+            h[i] = *reinterpret_cast<uint32_t*>(&x);
+        }
+        *reinterpret_cast<uint32_t*>(A + sw128_off(ra, k0)) = h[0];
+        *reinterpret_cast<uint32_t*>(A + sw128_off(rb, k0)) = h[1];
+        *reinterpret_cast<uint32_t*>(A + sw128_off(ra, k0 + 8)) = h[2];
+        *reinterpret_cast<uint32_t*>(A + sw128_off(rb, k0 + 8)) = h[3];
+    }
+}
+
+template <int BN, int EPI, int FMT = FMT_Q4S>
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                const TcGemmParams p) {
+    using SM = TcSmem<BN, FMT>;
+    constexpr int S = SM::S;
+    constexpr int UB = unit_bytes(FMT);
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t base_u = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((base_u + 1023u) & ~1023u) - base_u);
+    uint64_t* rawfull = reinterpret_cast<uint64_t*>(smem + SM::bar_off);
+    uint64_t* bfull = rawfull + S;
+    uint64_t* afull = bfull + S;
+    uint64_t* empty = afull + S;
+    uint64_t* accfull = empty + S;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::tmem_off);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile0 = blockIdx.x * (TC_BM / 16);
+    const int tok0 = blockIdx.y * BN;
+    const int nk = p.k / TC_BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&rawfull[s], 1);
+            mbar_init(&bfull[s], 1);
+            mbar_init(&afull[s], 4);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accfull, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, SM::tmem_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
+            int kc = 0;
+            for (; kc < nk; ++kc) {
+                const int s = kc % S;
+                if (kc >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((kc / S - 1) & 1))) {
+                    atomicOr(p.err, ERR_WAIT_PREFILL);
+                    break;
+                }
+                uint8_t* raw = smem + SM::raw_off + s * SM::raw_bytes;
+                mbar_expect_tx(&rawfull[s], 8 * UB);
+#pragma unroll 1
+                for (int t = 0; t < 8; ++t)
+                    bulk_g2s(raw + t * UB, p.w + icua_layout::unit_offset(FMT, p.n_tiles, p.upt, tile0 + t, kc), UB,
+                             &rawfull[s]);
+                mbar_expect_tx(&bfull[s], (uint32_t)SM::b_bytes);
+                tma_load_2d(smem + SM::b_off + s * SM::b_bytes, &xmap, kc * TC_BK, tok0, &bfull[s]);
+            }
+            // the copies of the last stages complete before the CTA may exit (at once on success)
+            for (int c = (kc > S ? kc - S : 0); c < kc; ++c) {
+                mbar_wait_bounded(&rawfull[c % S], (uint32_t)((c / S) & 1));
+                mbar_wait_bounded(&bfull[c % S], (uint32_t)((c / S) & 1));
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_f16(TC_BM, BN);
+            for (int kc = 0; kc < nk; ++kc) {
+                const int s = kc % S;
+                const uint32_t ph = (uint32_t)((kc / S) & 1);
+                if (!mbar_wait_bounded(&afull[s], ph) || !mbar_wait_bounded(&bfull[s], ph)) {
+                    atomicOr(p.err, ERR_WAIT_PREFILL);
+                    break;
+                }
+                tc_fence_after();
+                const uint64_t ad = umma_desc_sw128(smem_u32(smem + SM::a_off + s * SM::a_bytes));
+                const uint64_t bd = umma_desc_sw128(smem_u32(smem + SM::b_off + s * SM::b_bytes));
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks)  // K = 16 per MMA: 32 bytes along the swizzled row
+                    tc_mma_f16(tmem, ad + 2 * ks, bd + 2 * ks, idesc, (kc | ks) != 0);
+                tc_commit(&empty[s]);
+            }
+            tc_commit(accfull);  // also on the error path: tracks the MMAs already issued
+        }
+    } else {
+        // ---- dequantisation: 8 units x 32 lanes per stage over 128 threads ----
+        const int d = threadIdx.x - 64;
+        for (int kc = 0; kc < nk; ++kc) {
+            const int s = kc % S;
+            const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(&rawfull[s], (uint32_t)((kc / S) & 1)));
+            if (!got) {
+                if (lane == 0) atomicOr(p.err, ERR_WAIT_PREFILL);
+                break;
+            }
+            const uint8_t* raw = smem + SM::raw_off + s * SM::raw_bytes;
+            uint8_t* A = smem + SM::a_off + s * SM::a_bytes;
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int pi = d + 128 * i, t = pi >> 5;
+                if (FMT == FMT_Q4S)
+                    dequant_q4s_lane(raw + t * UB, pi & 31, A, t * 16);
+                else
+                    dequant_q8_lane(raw + t * UB, pi & 31, A, t * 16);
+            }
+            fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&afull[s]);
+        }
+        // ---- epilogue ----
+        const bool done = __all_sync(0xffffffffu, mbar_wait_bounded(accfull, 0));
+        tc_fence_after();
+        if (!done) {
+            if (lane == 0) atomicOr(p.err, ERR_WAIT_PREFILL);
+        } else {
+            const int q = warp & 3;
+            const int row = blockIdx.x * TC_BM + q * 32 + lane;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                if (tok0 + c * 32 >= p.m_tok) break;
+                float v[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int tok = tok0 + c * 32 + j;
+                    if (tok >= p.m_tok) break;
+                    if (EPI == TC_STORE) {
+                        p.out[(size_t)tok * p.ldo + row] = v[j];
+                    } else if (EPI == TC_RESID) {
+                        float* o = p.out + (size_t)tok * p.ldo + row;
+                        float nv = *o + v[j];
+                        if (p.deepstack != nullptr && tok >= p.ds_row0 && tok < p.ds_row0 + p.ds_rows)
+                            nv += p.deepstack[(size_t)(tok - p.ds_row0) * p.ldo + row];
+                        *o = nv;
+                    } else if (EPI == TC_ARGMAX) {
+                        if (p.out != nullptr) p.out[(size_t)tok * p.ldo + row] = v[j];
+                        float bv = v[j];
+                        int bi = row;
+                        warp_argmax(bv, bi);
+                        if (lane == 0) {
+                            float2* red = reinterpret_cast<float2*>(smem + SM::red_off);
+                            red[q * BN + c * 32 + j] = make_float2(bv, __int_as_float(bi));
+                        }
+                    } else {
+                        // rows of a 16-row tile: 0..7 gate j, 8..15 up j (tile * 8 + r)
+                        const float u = __shfl_xor_sync(0xffffffffu, v[j], 8);
+                        if (!(lane & 8)) {
+                            const float gv = v[j];
+                            const float hv = (gv / (1.0f + expf(-gv))) * u;
+                            p.out_h[(size_t)tok * p.ldh + (row >> 4) * 8 + (lane & 7)] = __float2half_rn(hv);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (EPI == TC_ARGMAX && threadIdx.x < BN && tok0 + (int)threadIdx.x < p.m_tok) {
+        // combine the four row quarters of this tile for token threadIdx.x (lower row on ties)
+        const float2* red = reinterpret_cast<const float2*>(smem + SM::red_off);
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float2 e = red[q * BN + threadIdx.x];
+            argmax_merge(bv, bi, e.x, __float_as_int(e.y));
+        }
+        p.best_v[(size_t)blockIdx.x * p.m_tok + tok0 + threadIdx.x] = bv;
+        p.best_i[(size_t)blockIdx.x * p.m_tok + tok0 + threadIdx.x] = bi;
+    }
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, SM::tmem_cols);
+    }
+}
+
+}  // namespace icua

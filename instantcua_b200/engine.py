@@ -33,7 +33,8 @@ class Engine:
 
     def __init__(self, model_path: str | None = None, tensors: dict | None = None, *, max_context: int = 2048,
                  max_pass: int = 512, max_steps: int = 256, n_layers: int = 28, vocab: int = 151936,
-                 max_sessions: int = 1, kv_dtype: str = "f16", steps_per_graph: int = 8, device: int = 0):
+                 max_sessions: int = 1, kv_dtype: str = "f16", steps_per_graph: int = 8, device: int = 0,
+                 prefill_gemm_min: int | None = None):
         self._lib = L.lib()
         cfg = L.IcuaConfig()
         self._lib.icua_default_config(C.byref(cfg))
@@ -47,6 +48,8 @@ class Engine:
         cfg.format = L.FMT_Q4S
         cfg.kv_dtype = {"f16": L.KV_F16, "bf16": L.KV_BF16}[kv_dtype]
         cfg.steps_per_graph = steps_per_graph
+        if prefill_gemm_min is not None:
+            cfg.prefill_gemm_min = prefill_gemm_min
         self.cfg = cfg
         h = C.c_void_p()
         L.check(self._lib.icua_engine_create(C.byref(cfg), C.byref(h)))
@@ -143,6 +146,28 @@ class Engine:
         n = C.c_int32()
         L.check(self._lib.icua_decode(self._h, session, max_new, out.ctypes.data_as(L._IP), C.byref(n)), self._h)
         return out[: n.value].tolist()
+
+    def decode_batch(self, sessions, steps: int, in_tokens=None) -> np.ndarray:
+        """Batched greedy decode of several sessions at once; returns int32 [len(sessions), steps]
+        (-1 after a session's EOS)."""
+        ss = np.ascontiguousarray(sessions, np.int32)
+        out = np.zeros((len(ss), max(steps, 1)), np.int32)
+        it = None if in_tokens is None else np.ascontiguousarray(in_tokens, np.int32)
+        L.check(self._lib.icua_decode_batch(self._h, ss.ctypes.data_as(L._IP), len(ss),
+                                            it.ctypes.data_as(L._IP) if it is not None else None, steps,
+                                            out.ctypes.data_as(L._IP)), self._h)
+        return out[:, :steps]
+
+    def capture_batch_logits(self, rows: int | None):
+        """Returns a host array [rows, vocab] that the next decode_batch calls fill with the logits
+        of their last step (or None to stop)."""
+        if not rows:
+            L.check(self._lib.icua_capture_batch_logits(self._h, None, 0), self._h)
+            self._bcap = None
+            return None
+        self._bcap = np.zeros((rows, self.cfg.vocab), np.float32)
+        L.check(self._lib.icua_capture_batch_logits(self._h, self._bcap.ctypes.data_as(L._FP), rows), self._h)
+        return self._bcap
 
     def decode_step(self, in_token: int, session: int = 0) -> int:
         o = C.c_int32()
