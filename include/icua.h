@@ -198,6 +198,14 @@ icua_status icua_gemv(int32_t fmt, int32_t n_rows, int32_t k, const void* packed
  * optional device int32 OR-ed with error flags when a bounded wait gives up (NULL: not reported). */
 icua_status icua_gemm_q4s(int32_t n_rows, int32_t k, int32_t m_tok, const void* packed_dev, const void* x_dev,
                           float* y_dev, int32_t* err_dev, void* stream);
+/* The prefill path's two halves: icua_dequant_q4s_f16 writes the row-major fp16 matrix
+ * [n_rows, k] with values half(q) * half(scale) (one rounding of the exact product); icua_gemm_f16
+ * is the tensor-core GEMM y[m_tok, n_rows] = x w16^T with both operands brought in by TMA (n_rows
+ * a multiple of 128, k of 64; 16-byte aligned pointers).  Same accumulation order as
+ * icua_gemm_q4s, so the two routes give identical results. */
+icua_status icua_dequant_q4s_f16(int32_t n_rows, int32_t k, const void* packed_dev, void* out_dev, void* stream);
+icua_status icua_gemm_f16(int32_t n_rows, int32_t k, int32_t m_tok, const void* w16_dev, const void* x_dev,
+                          float* y_dev, int32_t* err_dev, void* stream);
 /* Greedy head on the device: token = argmax_v (embed_v . RMSNorm(x) * norm_w), the tied q8 lm_head
  * of the reference (k_lm_head + k_commit, Shaders.swift:1452-1547; lowest index wins ties).
  * packed_embed_dev: q8 [vocab, 2048] in the device layout (icua_pack_matrix); x_dev fp32 [2048];

@@ -75,6 +75,8 @@ PROTOTYPES = {
     "icua_decode_batch": (_I, [_P, _IP, _I, _IP, _I, _IP]),
     "icua_capture_batch_logits": (_I, [_P, _FP, _I]),
     "icua_gemm_q4s": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),
+    "icua_dequant_q4s_f16": (_I, [_I, _I, _P, _P, _P]),
+    "icua_gemm_f16": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),
     "icua_dequant": (_I, [_I, _I, _I, _P, _P, _P]),
     "icua_greedy_head_scratch_bytes": (C.c_uint64, [_I]),
     "icua_greedy_head": (_I, [_I, _P, _P, _P, _P, _P, _P, _P]),

@@ -76,11 +76,14 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
     return r;
 }
 
+// Loads a float of cluster peer `rank`'s shared memory.  Ordering against the peer's writes
+// comes from the cluster barrier (release / acquire) around the combine, so the loads carry no
+// memory clobber and a thread's loads can be in flight together.
 __device__ __forceinline__ float ld_dsmem(const float* local_ptr, uint32_t rank) {
     uint32_t a = smem_u32(local_ptr), ra;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
     float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra));
     return v;
 }
 
@@ -395,14 +398,28 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
         float* out = p.part + ((long long)h * (NSP / CL) + j / CL) * ATT_PART;
         if (tid < per) {
             const int idx = rank * per + tid, hh = idx >> 7, d = idx & 127;
+            // all remote loads first (independent, in flight together), then the combine
+            float mq[8], lq[8], oq[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                if (q < CL) {
+                    mq[q] = ld_dsmem(&cpart[hh], q);
+                    lq[q] = ld_dsmem(&cpart[2 + hh], q);
+                    oq[q] = ld_dsmem(&cpart[4 + hh * HD + d], q);
+                }
+            }
             float M = -INFINITY;
-            for (int q = 0; q < CL; ++q) M = fmaxf(M, ld_dsmem(&cpart[hh], q));
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                if (q < CL) M = fmaxf(M, mq[q]);
             float Lsum = 0.f, O = 0.f;
-            for (int q = 0; q < CL; ++q) {
-                const float mq = ld_dsmem(&cpart[hh], q);
-                const float f = (mq == -INFINITY) ? 0.f : expf(mq - M);
-                Lsum = fmaf(ld_dsmem(&cpart[2 + hh], q), f, Lsum);
-                O = fmaf(ld_dsmem(&cpart[4 + hh * HD + d], q), f, O);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                if (q < CL) {
+                    const float f = (mq[q] == -INFINITY) ? 0.f : expf(mq[q] - M);
+                    Lsum = fmaf(lq[q], f, Lsum);
+                    O = fmaf(oq[q], f, O);
+                }
             }
             if (p.out16 != nullptr) {
                 p.out16[(size_t)row * H + (2 * h + hh) * HD + d] = __float2half_rn(O / Lsum);

@@ -112,8 +112,12 @@ struct icua_engine {
     // prefill rows through the tensor-core GEMM (max_pass rows each)
     float *px = nullptr, *pqkv = nullptr, *pq = nullptr;
     __half *pxn = nullptr, *pattn = nullptr, *ph = nullptr;
-    CUtensorMap map_xn{}, map_attn{}, map_h{};  // TMA maps of the fp16 GEMM inputs
     int* gemm_err = nullptr;                     // error flags of the batched kernels
+    // prefill: the layer matrices dequantised to fp16, two layers' sets (layer l in set l % 2),
+    // filled by a side stream one layer ahead of the GEMMs
+    __half* wscr[2][4] = {{nullptr, nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr, nullptr}};
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_ready[2] = {nullptr, nullptr}, ev_free[2] = {nullptr, nullptr};
     // sessions (contiguous arrays; Session holds pointers into them)
     DevState* st_all = nullptr;
     int* out_all = nullptr;
@@ -226,7 +230,6 @@ cudaError_t launch_gemv(const Matrix& m, const GemvParams& p, cudaStream_t s, bo
 }
 
 // ---- tensor-core GEMM launch ------------------------------------------------------------------
-constexpr int TC_BN = 128;  // tokens per CTA tile of the prefill GEMMs
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -267,15 +270,72 @@ TcGemmParams tc_params(const Matrix& m, int m_tok, int* err) {
     return p;
 }
 
+// Tile shape of a GEMM: MH accumulators of 128 weight rows (MH = 2 shares each activation tile
+// between 256 rows) and BN tokens per CTA, chosen so that the CTA count fills whole waves of SMs:
+// cost = waves x (MMA columns per CTA, at least those of 64 tokens per accumulator since below
+// that the weight stream and its dequantisation set the pace, + a fixed per-CTA overhead);
+// MH = 1 is charged 10% for its doubled activation traffic; ties go to the wider tile.
+struct TcTile {
+    int mh, bn;
+};
+
+TcTile choose_tc_tile(int n_rows, int m_tok, int n_sm, bool allow_mh2) {
+    TcTile best{1, 16};
+    double best_cost = 1e30;
+    const int bn_max = std::min(256, (m_tok + 15) / 16 * 16);
+    for (int mh = 2; mh >= 1; --mh) {
+        if ((mh == 2 && !allow_mh2) || n_rows % (TC_BM * mh)) continue;
+        for (int bn = bn_max; bn >= 16; bn -= 16) {
+            const long tiles = (long)(n_rows / (TC_BM * mh)) * ((m_tok + bn - 1) / bn);
+            const long waves = (tiles + n_sm - 1) / n_sm;
+            const double cost = (double)waves * (mh * std::max(bn, 64) + 48) * (mh == 1 ? 1.1 : 1.0);
+            if (cost < best_cost - 1e-9) {
+                best_cost = cost;
+                best = TcTile{mh, bn};
+            }
+        }
+    }
+    return best;
+}
+
+int g_n_sm_cache = 0;
+
+// Launches the GEMM over activations `x` ([rows_alloc, k] fp16) with a TMA map built for the
+// chosen tile height.  FMT_F16: the weights are the row-major fp16 matrix w16 (dequantised by
+// dequant_q4s_f16_kernel), brought in by TMA as well.
 template <int EPI, int FMT = FMT_Q4S>
-cudaError_t launch_tc_gemm(const CUtensorMap& map, const TcGemmParams& p, cudaStream_t s) {
-    if (p.n_rows % TC_BM || p.k % TC_BK || p.m_tok < 1) return cudaErrorInvalidValue;
+cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaStream_t s, const __half* w16 = nullptr) {
+    if (p.n_rows % TC_BM || p.k % TC_BK || p.m_tok < 1 || p.m_tok > rows_alloc) return cudaErrorInvalidValue;
+    if (!g_n_sm_cache) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_n_sm_cache, cudaDevAttrMultiProcessorCount, dev);
+    }
+    const TcTile t = choose_tc_tile(p.n_rows, p.m_tok, g_n_sm_cache, EPI != TC_ARGMAX);
+    p.bn = t.bn;
+    CUtensorMap map, wmap;
+    if (!make_act_map(&map, x, rows_alloc, p.k, t.bn)) return cudaErrorInvalidValue;
+    if (FMT == FMT_F16) {
+        if (!w16 || !make_act_map(&wmap, w16, p.n_rows, p.k, TC_BM)) return cudaErrorInvalidValue;
+    } else {
+        wmap = map;  // unused
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.n_rows / TC_BM, (p.m_tok + TC_BN - 1) / TC_BN);
+    cfg.gridDim = dim3(p.n_rows / (TC_BM * t.mh), (p.m_tok + t.bn - 1) / t.bn);
     cfg.blockDim = dim3(TC_THREADS);
-    cfg.dynamicSmemBytes = TcSmem<TC_BN, FMT>::alloc;
+    cfg.dynamicSmemBytes = TcLayout(t.bn, t.mh, FMT, EPI == TC_ARGMAX).alloc;
     cfg.stream = s;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<TC_BN, EPI, FMT>, map, p);
+    if (t.mh == 2) {
+        if constexpr (EPI != TC_ARGMAX) return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI, FMT, 2>, map, wmap, p);
+        return cudaErrorInvalidValue;
+    }
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI, FMT, 1>, map, wmap, p);
+}
+
+cudaError_t launch_dequant_f16(const Matrix& m, __half* out, int n_sm, cudaStream_t s) {
+    const long long n8 = (long long)m.n_rows * (m.k / 8);
+    const int grid = (int)std::min<long long>((n8 + 255) / 256, 8LL * n_sm);
+    return launch(dequant_q4s_f16_kernel, grid, 256, 0, s, false, (const uint8_t*)m.dev, m.n_rows, m.k, out);
 }
 
 cudaError_t set_smem_attrs() {
@@ -308,14 +368,17 @@ cudaError_t set_smem_attrs() {
     SETA(advance_kernel);
     SETA(argmax_parts_kernel);
 #undef SETA
-    for (const void* k : {(const void*)tc_gemm_kernel<TC_BN, TC_STORE>, (const void*)tc_gemm_kernel<TC_BN, TC_RESID>,
-                          (const void*)tc_gemm_kernel<TC_BN, TC_SWIGLU>}) {
-        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TcSmem<TC_BN>::alloc)) != cudaSuccess)
+    for (const void* k :
+         {(const void*)tc_gemm_kernel<TC_STORE, FMT_Q4S, 1>, (const void*)tc_gemm_kernel<TC_RESID, FMT_Q4S, 1>,
+          (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q4S, 1>, (const void*)tc_gemm_kernel<TC_STORE, FMT_Q4S, 2>,
+          (const void*)tc_gemm_kernel<TC_RESID, FMT_Q4S, 2>, (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q4S, 2>,
+          (const void*)tc_gemm_kernel<TC_ARGMAX, FMT_Q8, 1>, (const void*)tc_gemm_kernel<TC_STORE, FMT_F16, 1>,
+          (const void*)tc_gemm_kernel<TC_RESID, FMT_F16, 1>, (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_F16, 1>,
+          (const void*)tc_gemm_kernel<TC_STORE, FMT_F16, 2>, (const void*)tc_gemm_kernel<TC_RESID, FMT_F16, 2>,
+          (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_F16, 2>}) {
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)) != cudaSuccess)
             return e;
     }
-    if ((e = cudaFuncSetAttribute(tc_gemm_kernel<TC_BN, TC_ARGMAX, FMT_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  TcSmem<TC_BN, FMT_Q8>::alloc)) != cudaSuccess)
-        return e;
     for (const void* k : {(const void*)prefill_attn_kernel<__half>, (const void*)prefill_attn_kernel<__nv_bfloat16>}) {
         if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       PrefillAttnSmem<__half>::total)) != cudaSuccess)
@@ -672,17 +735,35 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
                       (const float*)e->pooler, (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->px)) != cudaSuccess)
         return err;
     const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
+    // dequantisation of layer l's matrices into set l % 2 on the side stream, one layer ahead;
+    // a set is rewritten only after the GEMMs of the layer two back have been issued behind it
+    auto dequant_layer = [&](int l) -> cudaError_t {
+        const int set = l & 1;
+        cudaError_t er;
+        if ((er = cudaStreamWaitEvent(e->side, e->ev_free[set], 0)) != cudaSuccess) return er;
+        const Layer& ly = e->layers[l];
+        const Matrix* ms[4] = {&ly.qkv, &ly.o, &ly.gu, &ly.d};
+        for (int i = 0; i < (l == L - 1 ? 1 : 4); ++i)
+            if ((er = launch_dequant_f16(*ms[i], e->wscr[set][i], e->n_sm, e->side)) != cudaSuccess) return er;
+        return cudaEventRecord(e->ev_ready[set], e->side);
+    };
+    for (int set = 0; set < 2; ++set)
+        if ((err = cudaEventRecord(e->ev_free[set], st)) != cudaSuccess) return err;
+    if ((err = dequant_layer(0)) != cudaSuccess) return err;
+    if (L > 1 && (err = dequant_layer(1)) != cudaSuccess) return err;
     for (int l = 0; l < L; ++l) {
         Layer& ly = e->layers[l];
         KVT* kc = reinterpret_cast<KVT*>(S.kc) + kv_layer * l;
         KVT* vc = reinterpret_cast<KVT*>(S.vc) + kv_layer * l;
+        __half* const* w16 = e->wscr[l & 1];
+        if ((err = cudaStreamWaitEvent(st, e->ev_ready[l & 1], 0)) != cudaSuccess) return err;
         if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
                           (const float*)ly.attn_norm, n_rows, e->pxn)) != cudaSuccess)
             return err;
         TcGemmParams p = tc_params(ly.qkv, n_rows, errp);
         p.out = e->pqkv;
         p.ldo = QKV_ROWS;
-        if ((err = launch_tc_gemm<TC_STORE>(e->map_xn, p, st)) != cudaSuccess) return err;
+        if ((err = launch_tc_gemm<TC_STORE, FMT_F16>(e->pxn, e->cfg.max_pass, p, st, w16[0])) != cudaSuccess) return err;
         if ((err = launch(qk_rope_kv_kernel<KVT>, n_rows, 256, 0, st, false, (const float*)e->pqkv, n_rows,
                           (const float*)ly.q_norm, (const float*)ly.k_norm, (const float2*)S.rope, pos0, kc, vc,
                           e->cfg.max_context, e->pq)) != cudaSuccess)
@@ -701,14 +782,14 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
         p = tc_params(ly.o, n_rows, errp);
         p.out = e->px;
         p.ldo = H;
-        if ((err = launch_tc_gemm<TC_RESID>(e->map_attn, p, st)) != cudaSuccess) return err;
+        if ((err = launch_tc_gemm<TC_RESID, FMT_F16>(e->pattn, e->cfg.max_pass, p, st, w16[1])) != cudaSuccess) return err;
         if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
                           (const float*)ly.mlp_norm, n_rows, e->pxn)) != cudaSuccess)
             return err;
         p = tc_params(ly.gu, n_rows, errp);
         p.out_h = e->ph;
         p.ldh = FF;
-        if ((err = launch_tc_gemm<TC_SWIGLU>(e->map_xn, p, st)) != cudaSuccess) return err;
+        if ((err = launch_tc_gemm<TC_SWIGLU, FMT_F16>(e->pxn, e->cfg.max_pass, p, st, w16[2])) != cudaSuccess) return err;
         p = tc_params(ly.d, n_rows, errp);
         p.out = e->px;
         p.ldo = H;
@@ -717,7 +798,9 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
             p.ds_row0 = vis_off;
             p.ds_rows = n_vis;
         }
-        if ((err = launch_tc_gemm<TC_RESID>(e->map_h, p, st)) != cudaSuccess) return err;
+        if ((err = launch_tc_gemm<TC_RESID, FMT_F16>(e->ph, e->cfg.max_pass, p, st, w16[3])) != cudaSuccess) return err;
+        if ((err = cudaEventRecord(e->ev_free[l & 1], st)) != cudaSuccess) return err;
+        if (l + 2 < L && (err = dequant_layer(l + 2)) != cudaSuccess) return err;
     }
     return cudaSuccess;
 }
@@ -742,7 +825,7 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
         TcGemmParams p = tc_params(ly.qkv, n_rows, e->gemm_err);
         p.out = e->pqkv;
         p.ldo = QKV_ROWS;
-        if ((err = launch_tc_gemm<TC_STORE>(e->map_xn, p, st)) != cudaSuccess) return err;
+        if ((err = launch_tc_gemm<TC_STORE>(e->pxn, e->cfg.max_pass, p, st)) != cudaSuccess) return err;
         {
             AttnParams<KVT> a{};
             a.qkv = e->pqkv;
@@ -755,8 +838,10 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
             a.vc = reinterpret_cast<KVT*>(e->vc_all) + kv_layer * l;
             a.sess_kv_elems = (long long)e->kv_elems;
             a.max_ctx = e->cfg.max_context;
-            a.n_split = e->att_cluster;  // one cluster per (row, kv head): one part, normalised in place
-            a.cluster = e->att_cluster;
+            // one cluster per (row, kv head): one part, normalised in place.  With enough rows to
+            // fill the GPU twice over, one CTA per (row, kv head) streams the whole context.
+            a.n_split = (n_rows * NKV >= 2 * e->n_sm) ? 1 : e->att_cluster;
+            a.cluster = a.n_split;
             a.part = e->att_part;
             a.st = e->st_all;
             a.rows_sess = e->batch_rows;
@@ -778,18 +863,18 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
         p = tc_params(ly.o, n_rows, e->gemm_err);
         p.out = e->px;
         p.ldo = H;
-        if ((err = launch_tc_gemm<TC_RESID>(e->map_attn, p, st)) != cudaSuccess) return err;
+        if ((err = launch_tc_gemm<TC_RESID>(e->pattn, e->cfg.max_pass, p, st)) != cudaSuccess) return err;
         if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
                           (const float*)ly.mlp_norm, n_rows, e->pxn)) != cudaSuccess)
             return err;
         p = tc_params(ly.gu, n_rows, e->gemm_err);
         p.out_h = e->ph;
         p.ldh = FF;
-        if ((err = launch_tc_gemm<TC_SWIGLU>(e->map_xn, p, st)) != cudaSuccess) return err;
+        if ((err = launch_tc_gemm<TC_SWIGLU>(e->pxn, e->cfg.max_pass, p, st)) != cudaSuccess) return err;
         p = tc_params(ly.d, n_rows, e->gemm_err);
         p.out = e->px;
         p.ldo = H;
-        if ((err = launch_tc_gemm<TC_RESID>(e->map_h, p, st)) != cudaSuccess) return err;
+        if ((err = launch_tc_gemm<TC_RESID>(e->ph, e->cfg.max_pass, p, st)) != cudaSuccess) return err;
     }
     if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
                       (const float*)e->final_norm, n_rows, e->pxn)) != cudaSuccess)
@@ -799,7 +884,7 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
     p.best_i = e->batch_best_i;
     p.out = e->batch_logits;  // nullptr unless the logits of the step were requested
     p.ldo = e->cfg.vocab;
-    if ((err = launch_tc_gemm<TC_ARGMAX, FMT_Q8>(e->map_xn, p, st)) != cudaSuccess) return err;
+    if ((err = launch_tc_gemm<TC_ARGMAX, FMT_Q8>(e->pxn, e->cfg.max_pass, p, st)) != cudaSuccess) return err;
     return launch(batch_commit_kernel, n_rows, 256, 0, st, false, (const float*)e->batch_best_v,
                   (const int*)e->batch_best_i, e->cfg.vocab / TC_BM, n_rows, (const int*)e->batch_rows, e->st_all,
                   e->out_all, e->out_stride);
@@ -945,14 +1030,22 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
         TRY(dalloc_t(eng, &eng->pattn, P * H));
         TRY(dalloc_t(eng, &eng->ph, P * FF));
         TRY(dalloc_t(eng, &eng->gemm_err, 1));
+        for (int set = 0; set < 2; ++set) {
+            TRY(dalloc_t(eng, &eng->wscr[set][0], (size_t)QKV_ROWS * H));
+            TRY(dalloc_t(eng, &eng->wscr[set][1], (size_t)H * H));
+            TRY(dalloc_t(eng, &eng->wscr[set][2], (size_t)GU_ROWS * H));
+            TRY(dalloc_t(eng, &eng->wscr[set][3], (size_t)H * FF));
+            cudaEventCreateWithFlags(&eng->ev_ready[set], cudaEventDisableTiming);
+            cudaEventCreateWithFlags(&eng->ev_free[set], cudaEventDisableTiming);
+        }
+        cudaStreamCreateWithFlags(&eng->side, cudaStreamNonBlocking);
         cudaMemset(eng->ph, 0, P * FF * sizeof(__half));
         cudaMemset(eng->pxn, 0, P * H * sizeof(__half));
         cudaMemset(eng->pattn, 0, P * H * sizeof(__half));
         cudaMemset(eng->gemm_err, 0, sizeof(int));
-        if (!make_act_map(&eng->map_xn, eng->pxn, (int)P, H, TC_BN) ||
-            !make_act_map(&eng->map_attn, eng->pattn, (int)P, H, TC_BN) ||
-            !make_act_map(&eng->map_h, eng->ph, (int)P, FF, TC_BN))
-            TRY(fail(eng, ICUA_ERR_CUDA, "cuTensorMapEncodeTiled failed for the prefill activations"));
+        CUtensorMap probe;
+        if (!make_act_map(&probe, eng->pxn, (int)P, H, 16))
+            TRY(fail(eng, ICUA_ERR_CUDA, "cuTensorMapEncodeTiled is not available"));
     }
     // Sessions live in contiguous per-engine arrays (state, outputs, RoPE tables, caches), so the
     // batched decode reaches session s of any row by one stride.
@@ -1000,6 +1093,14 @@ void icua_engine_destroy(icua_engine* eng) {
     for (void* p : eng->allocations) cudaFree(p);
     for (int i = 0; i < 4; ++i)
         if (eng->ev[i]) cudaEventDestroy(eng->ev[i]);
+    for (int i = 0; i < 2; ++i) {
+        if (eng->ev_ready[i]) cudaEventDestroy(eng->ev_ready[i]);
+        if (eng->ev_free[i]) cudaEventDestroy(eng->ev_free[i]);
+    }
+    if (eng->side) {
+        cudaStreamSynchronize(eng->side);
+        cudaStreamDestroy(eng->side);
+    }
     if (eng->stream) cudaStreamDestroy(eng->stream);
     delete eng;
 }
@@ -1588,8 +1689,6 @@ icua_status icua_gemm_q4s(int32_t n_rows, int32_t k, int32_t m_tok, const void* 
     if (n_rows < TC_BM || n_rows % TC_BM || k < 1024 || k % 1024 || k > 6144 || m_tok < 1 || ((uintptr_t)x & 15))
         return fail(nullptr, ICUA_ERR_INVALID, "unsupported gemm shape (rows %% 128, k %% 1024, k <= 6144, m >= 1, x 16-byte aligned)");
     CK(set_smem_attrs());
-    CUtensorMap map;
-    if (!make_act_map(&map, x, m_tok, k, TC_BN)) return fail(nullptr, ICUA_ERR_CUDA, "cuTensorMapEncodeTiled failed");
     int* errp = err_dev;
     if (!errp) CK(cudaGetSymbolAddress(reinterpret_cast<void**>(&errp), g_tc_gemm_err_sink));
     Matrix m;
@@ -1601,7 +1700,40 @@ icua_status icua_gemm_q4s(int32_t n_rows, int32_t k, int32_t m_tok, const void* 
     TcGemmParams p = tc_params(m, m_tok, errp);
     p.out = y;
     p.ldo = n_rows;
-    CK(launch_tc_gemm<TC_STORE>(map, p, (cudaStream_t)stream));
+    CK(launch_tc_gemm<TC_STORE>(x, m_tok, p, (cudaStream_t)stream));
+    return ICUA_OK;
+}
+
+icua_status icua_dequant_q4s_f16(int32_t n_rows, int32_t k, const void* packed, void* out, void* stream) {
+    icua_engine* eng = nullptr;
+    if (!packed || !out) return fail(nullptr, ICUA_ERR_INVALID, "null argument");
+    if (n_rows < 16 || n_rows % 16 || k < 1024 || k % 1024 || ((uintptr_t)out & 15))
+        return fail(nullptr, ICUA_ERR_INVALID, "unsupported shape (rows %% 16, k %% 1024, out 16-byte aligned)");
+    const long long n8 = (long long)n_rows * (k / 8);
+    CK(launch(dequant_q4s_f16_kernel, (int)std::min<long long>((n8 + 255) / 256, 4096), 256, 0, (cudaStream_t)stream,
+              false, (const uint8_t*)packed, (int)n_rows, (int)k, (__half*)out));
+    return ICUA_OK;
+}
+
+icua_status icua_gemm_f16(int32_t n_rows, int32_t k, int32_t m_tok, const void* w16, const void* x, float* y,
+                          int32_t* err_dev, void* stream) {
+    icua_engine* eng = nullptr;
+    if (!w16 || !x || !y) return fail(nullptr, ICUA_ERR_INVALID, "null argument");
+    if (n_rows < TC_BM || n_rows % TC_BM || k < 64 || k % 64 || m_tok < 1 || ((uintptr_t)x & 15) || ((uintptr_t)w16 & 15))
+        return fail(nullptr, ICUA_ERR_INVALID, "unsupported gemm shape (rows %% 128, k %% 64, m >= 1, 16-byte aligned)");
+    CK(set_smem_attrs());
+    int* errp = err_dev;
+    if (!errp) CK(cudaGetSymbolAddress(reinterpret_cast<void**>(&errp), g_tc_gemm_err_sink));
+    Matrix m;
+    m.fmt = FMT_F16;
+    m.n_rows = n_rows;
+    m.k = k;
+    m.n_tiles = n_rows / 16;
+    TcGemmParams p = tc_params(m, m_tok, errp);
+    p.out = y;
+    p.ldo = n_rows;
+    const cudaError_t err = launch_tc_gemm<TC_STORE, FMT_F16>(x, m_tok, p, (cudaStream_t)stream, (const __half*)w16);
+    CK(err);
     return ICUA_OK;
 }
 

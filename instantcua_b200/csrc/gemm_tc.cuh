@@ -1,21 +1,24 @@
 // Tensor-core dequant-GEMM for the dense cases (prefill rows, batched decode): tcgen05.mma with
-// the accumulator in tensor memory, weights dequantised from the q4s device tile layout into
+// the accumulator in tensor memory, weights dequantised from the q4s / q8 device tile layout into
 // shared memory by CUDA cores, activations brought in by TMA.
 //
 // Replaces the reference prefill GEMM (llm_gemm_tile + k_g3_*, Shaders.swift:927-1097): fp16
 // activations X [m_tok, K], weights dequantised to fp16 as half(q) * half(scale) (one fp16
 // rounding, the rule of Shaders.swift:958-959 applied to the symmetric int4 codes), fp32
-// accumulation, fused epilogues (store, residual add, SwiGLU into fp16).
+// accumulation, fused epilogues (store, residual add, SwiGLU into fp16, argmax partials).
 //
-// Design (B200): one CTA computes D[128 weight rows][BN tokens] = W[128, K] X[BN, K]^T as
-// UMMA M=128, N=BN, K=16 steps (kind::f16, both operands K-major with the 128-byte swizzle).
-//   warp 0      producer: 1-D bulk copies of the eight 16-row q4s units of each 64-column
+// Design (B200): one CTA computes D[MH x 128 weight rows][BN tokens] = W X^T as UMMA M=128,
+// N=BN, K=16 steps (kind::f16, both operands K-major with the 128-byte swizzle), MH = 1 or 2
+// accumulators of BN columns in tensor memory sharing every activation tile (MH = 2 halves the
+// L2 traffic per FLOP).  BN (a multiple of 16 up to 256) is chosen per GEMM by the host so that
+// the tile count fills whole waves of SMs.
+//   warp 0      producer: 1-D bulk copies of the 8 x MH 16-row weight units of each 64-column
 //               k-block, and a 2-D TMA tile load (box 64 x BN, SWIZZLE_128B) of the activations
-//   warp 1      allocates tensor memory (BN columns) and issues the MMAs (one thread); each
-//               stage is released with tcgen05.commit onto the stage's "empty" barrier
-//   warps 2..5  dequantise each staged unit into the swizzled A tile, then run the epilogue:
-//               tcgen05.ld 32x32b (warp w reads TMEM lanes 32 (w % 4) ..), one weight row per
-//               thread, tokens along the registers
+//   warp 1      allocates tensor memory and issues the MMAs (one thread); each stage is released
+//               with tcgen05.commit onto the stage's "empty" barrier
+//   warps 2..9  dequantise each staged unit into the swizzled A tile (two warps per scheduler),
+//               then run the epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes 32 (w % 4) ..),
+//               one weight row per thread, tokens along the registers
 // Every wait is bounded; a wait that gives up records an error flag, and the kernel still drains
 // its copies and frees its tensor memory before it exits.
 #pragma once
@@ -26,16 +29,18 @@
 
 namespace icua {
 
-constexpr int TC_BM = 128;      // weight rows per CTA (UMMA M)
+constexpr int TC_BM = 128;      // weight rows per accumulator (UMMA M)
 constexpr int TC_BK = 64;       // columns per stage: one 128-byte swizzle row of fp16
-constexpr int TC_THREADS = 192;
+constexpr int TC_THREADS = 320; // producer warp, MMA warp, 8 dequant / epilogue warps
+constexpr int TC_SMEM_BUDGET = 225 * 1024;
 
 enum TcEpi { TC_STORE = 0, TC_RESID = 1, TC_SWIGLU = 2, TC_ARGMAX = 3 };
 
 struct TcGemmParams {
-    const uint8_t* w;          // q4s device tile layout [n_rows, k]
+    const uint8_t* w;          // weights in the device tile layout [n_rows, k] (q4s or q8)
     int n_rows, k, n_tiles, upt;
     int m_tok;                 // activation rows (tokens)
+    int bn;                    // tokens per CTA tile (multiple of 16, <= 256; the TMA box height)
     float* out;                // TC_STORE: out[tok * ldo + row] = y; TC_RESID: out[...] += y
     int ldo;
     __half* out_h;             // TC_SWIGLU: out_h[tok * ldh + j] = silu(gate_j) * up_j
@@ -47,25 +52,29 @@ struct TcGemmParams {
     int* err;                  // error flags (bounded waits that gave up)
 };
 
-template <int BN, int FMT = FMT_Q4S>
-struct TcSmem {
-    static constexpr int a_bytes = TC_BM * 128;                // fp16 [128][64], swizzled
-    static constexpr int b_bytes = BN * 128;                   // fp16 [BN][64], swizzled by TMA
-    static constexpr int raw_bytes = 8 * unit_bytes(FMT);      // eight 16-row units
-    static constexpr int stage_bytes = a_bytes + b_bytes + raw_bytes;
-    // pipeline stages: as many as fit (at most 6) next to the argmax scratch and barriers
-    static constexpr int S_fit = (225 * 1024 - 4 * BN * 8 - 1024 - 256) / stage_bytes;
-    static constexpr int S = S_fit < 6 ? S_fit : 6;
-    static constexpr int a_off = 0;
-    static constexpr int b_off = a_off + S * a_bytes;
-    static constexpr int raw_off = b_off + S * b_bytes;
-    static constexpr int bar_off = raw_off + S * raw_bytes;    // rawfull, bfull, afull, empty [S]; accfull
-    static constexpr int tmem_off = bar_off + (4 * S + 1) * 8;
-    static constexpr int red_off = tmem_off + 16;               // TC_ARGMAX: [4 warps][BN] (value, row)
-    static constexpr int total = red_off + 4 * BN * 8;
-    static constexpr int alloc = total + 1024;                 // room to align the tiles to 1024 B
-    static constexpr uint32_t tmem_cols = BN < 32 ? 32 : BN;
-    static_assert(S >= 2 && alloc <= 227 * 1024, "GEMM shared memory");
+// Shared-memory layout of one CTA for a (BN, MH, format) choice; the same arithmetic runs on the
+// host (launch size) and the device (offsets).
+struct TcLayout {
+    int S;                                   // pipeline stages
+    int a_bytes, b_bytes, raw_bytes, stage_bytes;
+    int a_off, b_off, raw_off, bar_off, tmem_off, red_off, total, alloc;
+    __host__ __device__ TcLayout(int bn, int mh, int fmt, bool argmax) {
+        a_bytes = mh * TC_BM * 128;          // fp16 [mh * 128][64], swizzled
+        b_bytes = bn * 128;                  // fp16 [bn][64], swizzled by TMA
+        raw_bytes = mh * 8 * unit_bytes(fmt);
+        stage_bytes = a_bytes + b_bytes + raw_bytes;
+        const int red = argmax ? 4 * mh * bn * 8 : 0;
+        S = (TC_SMEM_BUDGET - red - 1024 - 512) / stage_bytes;
+        if (S > 8) S = 8;
+        a_off = 0;
+        b_off = a_off + S * a_bytes;
+        raw_off = b_off + S * b_bytes;
+        bar_off = raw_off + S * raw_bytes;   // rawfull, bfull, afull, empty [S]; accfull
+        tmem_off = bar_off + (4 * S + 1) * 8;
+        red_off = (tmem_off + 16 + 15) & ~15;
+        total = red_off + red;
+        alloc = total + 1024;                // room to align the tiles to 1024 B
+    }
 };
 
 // ---- tcgen05 / TMA helpers ------------------------------------------------------------------
@@ -131,6 +140,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // 2-D TMA tile load (no multicast).  x (the contiguous dimension) is a multiple of 64 elements.
@@ -216,38 +238,44 @@ __device__ __forceinline__ void dequant_q8_lane(const uint8_t* unit, int l, uint
     }
 }
 
-template <int BN, int EPI, int FMT = FMT_Q4S>
+template <int EPI, int FMT, int MH>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                const __grid_constant__ CUtensorMap wmap,
                                                                 const TcGemmParams p) {
-    using SM = TcSmem<BN, FMT>;
-    constexpr int S = SM::S;
     constexpr int UB = unit_bytes(FMT);
+    constexpr int NU = 8 * MH;  // 16-row units per stage
+    const int BN = p.bn;
+    const TcLayout SM(BN, MH, FMT, EPI == TC_ARGMAX);
+    const int S = SM.S;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base_u = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((base_u + 1023u) & ~1023u) - base_u);
-    uint64_t* rawfull = reinterpret_cast<uint64_t*>(smem + SM::bar_off);
+    uint64_t* rawfull = reinterpret_cast<uint64_t*>(smem + SM.bar_off);
     uint64_t* bfull = rawfull + S;
     uint64_t* afull = bfull + S;
     uint64_t* empty = afull + S;
     uint64_t* accfull = empty + S;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::tmem_off);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM.tmem_off);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile0 = blockIdx.x * (TC_BM / 16);
+    const int tile0 = blockIdx.x * (MH * TC_BM / 16);
+    const int row0 = blockIdx.x * (MH * TC_BM);
     const int tok0 = blockIdx.y * BN;
     const int nk = p.k / TC_BK;
+    constexpr uint32_t tmem_cols = MH == 2 ? 512 : 256;
+    constexpr int half_cols = 256;  // column offset of the second accumulator
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&rawfull[s], 1);
             mbar_init(&bfull[s], 1);
-            mbar_init(&afull[s], 4);
+            mbar_init(&afull[s], 8);
             mbar_init(&empty[s], 1);
         }
         mbar_init(accfull, 1);
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, SM::tmem_cols);
+        tmem_alloc(tmem_slot, tmem_cols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -258,6 +286,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     if (warp == 0) {
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
+            if (FMT == FMT_F16) asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
             int kc = 0;
             for (; kc < nk; ++kc) {
                 const int s = kc % S;
@@ -265,98 +294,133 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                     atomicOr(p.err, ERR_WAIT_PREFILL);
                     break;
                 }
-                uint8_t* raw = smem + SM::raw_off + s * SM::raw_bytes;
-                mbar_expect_tx(&rawfull[s], 8 * UB);
+                if constexpr (FMT == FMT_F16) {
+                    // dequantised weights: MH boxes of 128 rows x 64 columns by TMA, same barrier as X
+                    mbar_expect_tx(&bfull[s], (uint32_t)(SM.a_bytes + SM.b_bytes));
+#pragma unroll
+                    for (int h = 0; h < MH; ++h)
+                        tma_load_2d(smem + SM.a_off + s * SM.a_bytes + h * TC_BM * 128, &wmap, kc * TC_BK,
+                                    row0 + h * TC_BM, &bfull[s]);
+                } else {
+                    uint8_t* raw = smem + SM.raw_off + s * SM.raw_bytes;
+                    mbar_expect_tx(&rawfull[s], NU * UB);
 #pragma unroll 1
-                for (int t = 0; t < 8; ++t)
-                    bulk_g2s(raw + t * UB, p.w + icua_layout::unit_offset(FMT, p.n_tiles, p.upt, tile0 + t, kc), UB,
-                             &rawfull[s]);
-                mbar_expect_tx(&bfull[s], (uint32_t)SM::b_bytes);
-                tma_load_2d(smem + SM::b_off + s * SM::b_bytes, &xmap, kc * TC_BK, tok0, &bfull[s]);
+                    for (int t = 0; t < NU; ++t)
+                        bulk_g2s(raw + t * UB, p.w + icua_layout::unit_offset(FMT, p.n_tiles, p.upt, tile0 + t, kc),
+                                 UB, &rawfull[s]);
+                    mbar_expect_tx(&bfull[s], (uint32_t)SM.b_bytes);
+                }
+                tma_load_2d(smem + SM.b_off + s * SM.b_bytes, &xmap, kc * TC_BK, tok0, &bfull[s]);
             }
             // the copies of the last stages complete before the CTA may exit (at once on success)
             for (int c = (kc > S ? kc - S : 0); c < kc; ++c) {
-                mbar_wait_bounded(&rawfull[c % S], (uint32_t)((c / S) & 1));
+                if (FMT != FMT_F16) mbar_wait_bounded(&rawfull[c % S], (uint32_t)((c / S) & 1));
                 mbar_wait_bounded(&bfull[c % S], (uint32_t)((c / S) & 1));
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_f16(TC_BM, BN);
+            const uint32_t idesc = umma_idesc_f16(TC_BM, BN);
             for (int kc = 0; kc < nk; ++kc) {
                 const int s = kc % S;
                 const uint32_t ph = (uint32_t)((kc / S) & 1);
-                if (!mbar_wait_bounded(&afull[s], ph) || !mbar_wait_bounded(&bfull[s], ph)) {
+                if ((FMT != FMT_F16 && !mbar_wait_bounded(&afull[s], ph)) || !mbar_wait_bounded(&bfull[s], ph)) {
                     atomicOr(p.err, ERR_WAIT_PREFILL);
                     break;
                 }
                 tc_fence_after();
-                const uint64_t ad = umma_desc_sw128(smem_u32(smem + SM::a_off + s * SM::a_bytes));
-                const uint64_t bd = umma_desc_sw128(smem_u32(smem + SM::b_off + s * SM::b_bytes));
+                const uint64_t bd = umma_desc_sw128(smem_u32(smem + SM.b_off + s * SM.b_bytes));
 #pragma unroll
-                for (int ks = 0; ks < 4; ++ks)  // K = 16 per MMA: 32 bytes along the swizzled row
-                    tc_mma_f16(tmem, ad + 2 * ks, bd + 2 * ks, idesc, (kc | ks) != 0);
+                for (int h = 0; h < MH; ++h) {
+                    const uint64_t ad = umma_desc_sw128(smem_u32(smem + SM.a_off + s * SM.a_bytes + h * TC_BM * 128));
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)  // K = 16 per MMA: 32 bytes along the swizzled row
+                        tc_mma_f16(tmem + h * half_cols, ad + 2 * ks, bd + 2 * ks, idesc, (kc | ks) != 0);
+                }
                 tc_commit(&empty[s]);
             }
             tc_commit(accfull);  // also on the error path: tracks the MMAs already issued
         }
     } else {
-        // ---- dequantisation: 8 units x 32 lanes per stage over 128 threads ----
+        // ---- dequantisation: NU units x 32 lanes per stage over 256 threads ----
         const int d = threadIdx.x - 64;
-        for (int kc = 0; kc < nk; ++kc) {
+        for (int kc = 0; kc < (FMT == FMT_F16 ? 0 : nk); ++kc) {
             const int s = kc % S;
             const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(&rawfull[s], (uint32_t)((kc / S) & 1)));
             if (!got) {
                 if (lane == 0) atomicOr(p.err, ERR_WAIT_PREFILL);
                 break;
             }
-            const uint8_t* raw = smem + SM::raw_off + s * SM::raw_bytes;
-            uint8_t* A = smem + SM::a_off + s * SM::a_bytes;
+            const uint8_t* raw = smem + SM.raw_off + s * SM.raw_bytes;
+            uint8_t* A = smem + SM.a_off + s * SM.a_bytes;
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int pi = d + 128 * i, t = pi >> 5;
-                if (FMT == FMT_Q4S)
+            for (int i = 0; i < MH; ++i) {
+                const int pi = d + 256 * i, t = pi >> 5;
+                if constexpr (FMT == FMT_Q4S)
                     dequant_q4s_lane(raw + t * UB, pi & 31, A, t * 16);
-                else
+                else if constexpr (FMT == FMT_Q8)
                     dequant_q8_lane(raw + t * UB, pi & 31, A, t * 16);
             }
             fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
             __syncwarp();
             if (lane == 0) mbar_arrive(&afull[s]);
         }
-        // ---- epilogue ----
+        // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) ..; wg = 0 / 1 picks the accumulator
+        // (MH == 2) or every other 32-column chunk (MH == 1) ----
         const bool done = __all_sync(0xffffffffu, mbar_wait_bounded(accfull, 0));
         tc_fence_after();
         if (!done) {
             if (lane == 0) atomicOr(p.err, ERR_WAIT_PREFILL);
         } else {
-            const int q = warp & 3;
-            const int row = blockIdx.x * TC_BM + q * 32 + lane;
+            const int q = warp & 3, wg = (warp - 2) >> 2;
+            const int h = MH == 2 ? wg : 0;
+            const int row = blockIdx.x * (MH * TC_BM) + h * TC_BM + q * 32 + lane;
+            const int cstep = MH == 2 ? 1 : 2;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int c = (MH == 2 ? 0 : wg); c * 32 < BN; c += cstep) {
                 if (tok0 + c * 32 >= p.m_tok) break;
                 float v[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * half_cols + c * 32);
+                const int ncol = min(32, BN - c * 32);  // 32 or 16
+                if (ncol == 32)
+                    tmem_ld32(taddr, v);
+                else
+                    tmem_ld16(taddr, v);
+                if (EPI == TC_RESID) {
+                    // residual rows: the chunk's loads first (independent, in flight together),
+                    // then the adds and stores; DeepStack rows (three layers of a visual prefill)
+                    // are added after the residual, as the reference does
+                    const int nj = min(ncol, p.m_tok - (tok0 + c * 32));
+                    float old[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        old[j] = j < nj ? p.out[(size_t)(tok0 + c * 32 + j) * p.ldo + row] : 0.f;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int tok = tok0 + c * 32 + j;
+                        if (j < nj) {
+                            float nv = old[j] + v[j];
+                            if (p.deepstack != nullptr && tok >= p.ds_row0 && tok < p.ds_row0 + p.ds_rows)
+                                nv += p.deepstack[(size_t)(tok - p.ds_row0) * p.ldo + row];
+                            p.out[(size_t)tok * p.ldo + row] = nv;
+                        }
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int tok = tok0 + c * 32 + j;
-                    if (tok >= p.m_tok) break;
+                    if (j >= ncol || tok >= p.m_tok) break;
                     if (EPI == TC_STORE) {
                         p.out[(size_t)tok * p.ldo + row] = v[j];
-                    } else if (EPI == TC_RESID) {
-                        float* o = p.out + (size_t)tok * p.ldo + row;
-                        float nv = *o + v[j];
-                        if (p.deepstack != nullptr && tok >= p.ds_row0 && tok < p.ds_row0 + p.ds_rows)
-                            nv += p.deepstack[(size_t)(tok - p.ds_row0) * p.ldo + row];
-                        *o = nv;
                     } else if (EPI == TC_ARGMAX) {
                         if (p.out != nullptr) p.out[(size_t)tok * p.ldo + row] = v[j];
                         float bv = v[j];
                         int bi = row;
                         warp_argmax(bv, bi);
                         if (lane == 0) {
-                            float2* red = reinterpret_cast<float2*>(smem + SM::red_off);
-                            red[q * BN + c * 32 + j] = make_float2(bv, __int_as_float(bi));
+                            float2* red = reinterpret_cast<float2*>(smem + SM.red_off);
+                            red[(h * 4 + q) * BN + c * 32 + j] = make_float2(bv, __int_as_float(bi));
                         }
                     } else {
                         // rows of a 16-row tile: 0..7 gate j, 8..15 up j (tile * 8 + r)
@@ -373,23 +437,52 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     }
     tc_fence_before();
     __syncthreads();
-    if (EPI == TC_ARGMAX && threadIdx.x < BN && tok0 + (int)threadIdx.x < p.m_tok) {
-        // combine the four row quarters of this tile for token threadIdx.x (lower row on ties)
-        const float2* red = reinterpret_cast<const float2*>(smem + SM::red_off);
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float2 e = red[q * BN + threadIdx.x];
-            argmax_merge(bv, bi, e.x, __float_as_int(e.y));
+    if (EPI == TC_ARGMAX) {
+        // combine the 4 x MH row quarters of this tile per token (lower row on ties)
+        const float2* red = reinterpret_cast<const float2*>(smem + SM.red_off);
+        for (int t = threadIdx.x; t < BN && tok0 + t < p.m_tok; t += blockDim.x) {
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            for (int q = 0; q < 4 * MH; ++q) {
+                const float2 e = red[q * BN + t];
+                argmax_merge(bv, bi, e.x, __float_as_int(e.y));
+            }
+            p.best_v[(size_t)blockIdx.x * p.m_tok + tok0 + t] = bv;
+            p.best_i[(size_t)blockIdx.x * p.m_tok + tok0 + t] = bi;
         }
-        p.best_v[(size_t)blockIdx.x * p.m_tok + tok0 + threadIdx.x] = bv;
-        p.best_i[(size_t)blockIdx.x * p.m_tok + tok0 + threadIdx.x] = bi;
     }
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem, SM::tmem_cols);
+        tmem_dealloc(tmem, tmem_cols);
+    }
+}
+
+// Dequantises a q4s matrix of the device tile layout into row-major fp16 [n_rows][k] with the
+// GEMM's rule half(q) * half(scale) (computed as one rounding of the exact fp32 product, which
+// is the same value): the operand of the prefill GEMMs, whose tiles then come in by TMA.  One
+// thread per (row, 8 consecutive columns): four words of the unit, one 16-byte store.
+__global__ void __launch_bounds__(256) dequant_q4s_f16_kernel(const uint8_t* tiles, int n_rows, int K, __half* out) {
+    const long long n8 = (long long)n_rows * (K / 8);
+    const int n_tiles = n_rows / 16, upt = K / 64;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+        const int row = (int)(i / (K / 8)), j8 = (int)(i % (K / 8));
+        const uint8_t* ub = tiles + icua_layout::unit_offset(FMT_Q4S, n_tiles, upt, row >> 4, j8 >> 3);
+        const int rt = row & 15, g = rt & 7, up = rt >> 3;
+        const int j = j8 & 7, step = j >> 1, hi8 = j & 1;
+        const __half s = *reinterpret_cast<const __half*>(ub + 512 + g * 8 + (step >> 1) * 4 + up * 2);
+        const float sf = __half2float(s);
+        uint32_t o[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(ub + (g * 4 + t) * 16 + step * 4);
+            const int sh = hi8 * 8 + up * 4;
+            const float a = sf * (float)((int)((w >> sh) & 0xF) - 8);
+            const float b = sf * (float)((int)((w >> (16 + sh)) & 0xF) - 8);
+            const __half2 hv = __floats2half2_rn(a, b);
+            o[t] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+        *reinterpret_cast<uint4*>(out + (size_t)row * K + (size_t)j8 * 8) = make_uint4(o[0], o[1], o[2], o[3]);
     }
 }
 

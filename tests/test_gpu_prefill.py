@@ -70,6 +70,43 @@ def test_gemm_matches_fp64(torch_cuda, n, k, m):
     assert np.array_equal(y, y2)  # deterministic
 
 
+@pytest.mark.parametrize("n,k", [(4096, 2048), (2048, 6144)])
+def test_dequant_f16_bit_exact(torch_cuda, n, k):
+    """The prefill path's dequantised operand equals fp16(float(scale) * q) element for element."""
+    torch = torch_cuda
+    buf, w16 = _packed_q4s(n, k, seed=5)
+    dev_w = torch.from_numpy(buf).cuda()
+    out = torch.empty((n, k), dtype=torch.float16, device="cuda")
+    L.check(L.lib().icua_dequant_q4s_f16(n, k, C.c_void_p(dev_w.data_ptr()), C.c_void_p(out.data_ptr()), None))
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), w16.view(np.uint16))
+
+
+@pytest.mark.parametrize("n,k,m", [(4096, 2048, 1255), (2048, 6144, 300), (12288, 2048, 64)])
+def test_gemm_f16_route_matches(torch_cuda, n, k, m):
+    """Dequantise-then-TMA GEMM (the prefill route) against the fused-dequant GEMM and float64."""
+    torch = torch_cuda
+    buf, w16 = _packed_q4s(n, k, seed=n + m)
+    dev_w = torch.from_numpy(buf).cuda()
+    x = np.random.default_rng(m).standard_normal((m, k), dtype=np.float32).astype(np.float16)
+    x16 = torch.from_numpy(x).cuda()
+    wd = torch.empty((n, k), dtype=torch.float16, device="cuda")
+    L.check(L.lib().icua_dequant_q4s_f16(n, k, C.c_void_p(dev_w.data_ptr()), C.c_void_p(wd.data_ptr()), None))
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    L.check(L.lib().icua_gemm_f16(n, k, m, C.c_void_p(wd.data_ptr()), C.c_void_p(x16.data_ptr()),
+                                  C.c_void_p(y.data_ptr()), C.c_void_p(err.data_ptr()), None))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    y = y.cpu().numpy()
+    want = x.astype(np.float64) @ w16.astype(np.float64).T
+    rel = np.abs(y - want).max() / np.abs(want).max()
+    fused = _gemm(torch, n, k, m, dev_w, x16).cpu().numpy()
+    print(f"gemm_f16 {m}x{n}x{k}: max rel err {rel:.2e}, max |f16 route - fused| {np.abs(y - fused).max():.2e}")
+    assert rel <= GEMM_TOL
+    assert np.array_equal(y, fused)
+
+
 def test_gemm_one_hot_rows_exact(torch_cuda):
     """Activation row t = e_j gives output row t = fp16 weight column j, exactly."""
     torch = torch_cuda
