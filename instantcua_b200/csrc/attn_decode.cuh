@@ -61,19 +61,32 @@ struct AttnSmem {
     static constexpr int new_off = 8 * ring_warp;                 // K, V rows of the new position
     static constexpr int q_off = new_off + 2 * row_bytes;         // float q[2][128] (scaled)
     static constexpr int wpart_off = q_off + 2 * HD * 4;          // float [8][ATT_PART]
-    static constexpr int cpart_off = wpart_off + 8 * ATT_PART * 4;  // float [ATT_PART]
-    static constexpr int bars_off = cpart_off + ATT_PART * 4;
+    static constexpr int cpart_off = wpart_off + 8 * ATT_PART * 4;  // float [8 cluster ranks][ATT_PART]
+    static constexpr int bars_off = cpart_off + 8 * ATT_PART * 4;
     static constexpr int total = bars_off + 8 * ATT_NS * 8;
 };
 
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Split cluster barrier: arrive early, wait where it is needed (here: before the first access to a
+// peer's shared memory, which requires every CTA of the cluster to have started).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
     return r;
+}
+
+// Stores a float into cluster peer `rank`'s shared memory at the address `local_ptr` has here.
+__device__ __forceinline__ void st_dsmem(float* local_ptr, uint32_t rank, float v) {
+    uint32_t a = smem_u32(local_ptr), ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
 }
 
 // Loads a float of cluster peer `rank`'s shared memory.  Ordering against the peer's writes
@@ -269,6 +282,8 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
         return;
     }
 
+    cluster_arrive_relaxed();  // every CTA of the cluster has started (waited on before the push)
+
     // ---- q/k norm + RoPE for the new position: warp 0/1 -> q heads 2h, 2h+1, warp 2 -> k, 3 -> v ----
     if (warp < 4) {
         const int base = warp < 2 ? (2 * h + warp) * HD : (warp == 2 ? 2048 + h * HD : 3072 + h * HD);
@@ -383,56 +398,48 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
             Lsum = fmaf(wpart[w2 * ATT_PART + 2 + hh], f, Lsum);
             O = fmaf(wpart[w2 * ATT_PART + 4 + hh * HD + d], f, O);
         }
-        cpart[4 + hh * HD + d] = O;
+        // push this CTA's part into slot `rank` of the cluster leader's (rank 0) shared memory
+        cluster_wait();
+        const uint32_t rank = cluster_ctarank();
+        float* slot = cpart + rank * ATT_PART;
+        st_dsmem(&slot[4 + hh * HD + d], 0, O);
         if (d == 0) {
-            cpart[hh] = M;
-            cpart[2 + hh] = Lsum;
+            st_dsmem(&slot[hh], 0, M);
+            st_dsmem(&slot[2 + hh], 0, Lsum);
         }
     }
-    // cluster combine through distributed shared memory; every CTA reaches both barriers
+    // one cluster barrier: the pushes (release) are visible to the leader (acquire); the other
+    // CTAs are done, since nobody reads their shared memory
     cluster_sync_all();
+    if (cluster_ctarank() != 0) return;
     {
         const int CL = p.cluster;
-        const uint32_t rank = cluster_ctarank();
-        const int per = (2 * HD) / CL;  // outputs combined by this CTA
-        float* out = p.part + ((long long)h * (NSP / CL) + j / CL) * ATT_PART;
-        if (tid < per) {
-            const int idx = rank * per + tid, hh = idx >> 7, d = idx & 127;
-            // all remote loads first (independent, in flight together), then the combine
-            float mq[8], lq[8], oq[8];
+        const int hh = tid >> 7, d = tid & 127;
+        float M = -INFINITY;
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                if (q < CL) {
-                    mq[q] = ld_dsmem(&cpart[hh], q);
-                    lq[q] = ld_dsmem(&cpart[2 + hh], q);
-                    oq[q] = ld_dsmem(&cpart[4 + hh * HD + d], q);
-                }
+        for (int q = 0; q < 8; ++q)
+            if (q < CL) M = fmaxf(M, cpart[q * ATT_PART + hh]);
+        float Lsum = 0.f, O = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            if (q < CL) {
+                const float mq = cpart[q * ATT_PART + hh];
+                const float f = (mq == -INFINITY) ? 0.f : expf(mq - M);
+                Lsum = fmaf(cpart[q * ATT_PART + 2 + hh], f, Lsum);
+                O = fmaf(cpart[q * ATT_PART + 4 + hh * HD + d], f, O);
             }
-            float M = -INFINITY;
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-                if (q < CL) M = fmaxf(M, mq[q]);
-            float Lsum = 0.f, O = 0.f;
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                if (q < CL) {
-                    const float f = (mq[q] == -INFINITY) ? 0.f : expf(mq[q] - M);
-                    Lsum = fmaf(lq[q], f, Lsum);
-                    O = fmaf(oq[q], f, O);
-                }
-            }
-            if (p.out16 != nullptr) {
-                p.out16[(size_t)row * H + (2 * h + hh) * HD + d] = __float2half_rn(O / Lsum);
-            } else {
-                out[4 + hh * HD + d] = O;
-                if (d == 0) {
-                    out[hh] = M;
-                    out[2 + hh] = Lsum;
-                }
+        }
+        if (p.out16 != nullptr) {
+            p.out16[(size_t)row * H + (2 * h + hh) * HD + d] = __float2half_rn(O / Lsum);
+        } else {
+            float* out = p.part + ((long long)h * (NSP / CL) + j / CL) * ATT_PART;
+            out[4 + hh * HD + d] = O;
+            if (d == 0) {
+                out[hh] = M;
+                out[2 + hh] = Lsum;
             }
         }
     }
-    cluster_sync_all();  // peers may still be reading this CTA's shared memory
 }
 
 }  // namespace icua

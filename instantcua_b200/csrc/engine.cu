@@ -113,6 +113,7 @@ struct icua_engine {
     float *px = nullptr, *pqkv = nullptr, *pq = nullptr;
     __half *pxn = nullptr, *pattn = nullptr, *ph = nullptr;
     int* gemm_err = nullptr;                     // error flags of the batched kernels
+    float* splitk_part = nullptr;                // split-K partial products of the batched GEMMs
     // prefill: the layer matrices dequantised to fp16, two layers' sets (layer l in set l % 2),
     // filled by a side stream one layer ahead of the GEMMs
     __half* wscr[2][4] = {{nullptr, nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr, nullptr}};
@@ -304,7 +305,8 @@ int g_n_sm_cache = 0;
 // chosen tile height.  FMT_F16: the weights are the row-major fp16 matrix w16 (dequantised by
 // dequant_q4s_f16_kernel), brought in by TMA as well.
 template <int EPI, int FMT = FMT_Q4S>
-cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaStream_t s, const __half* w16 = nullptr) {
+cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaStream_t s, const __half* w16 = nullptr,
+                           int ksplit = 1) {
     if (p.n_rows % TC_BM || p.k % TC_BK || p.m_tok < 1 || p.m_tok > rows_alloc) return cudaErrorInvalidValue;
     if (!g_n_sm_cache) {
         int dev = 0;
@@ -321,7 +323,8 @@ cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaSt
         wmap = map;  // unused
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.n_rows / (TC_BM * t.mh), (p.m_tok + t.bn - 1) / t.bn);
+    if (ksplit > 1 && (EPI != TC_STORE || ksplit > p.k / TC_BK)) return cudaErrorInvalidValue;
+    cfg.gridDim = dim3(p.n_rows / (TC_BM * t.mh), (p.m_tok + t.bn - 1) / t.bn, ksplit);
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = TcLayout(t.bn, t.mh, FMT, EPI == TC_ARGMAX).alloc;
     cfg.stream = s;
@@ -330,6 +333,31 @@ cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaSt
         return cudaErrorInvalidValue;
     }
     return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI, FMT, 1>, map, wmap, p);
+}
+
+constexpr int SPLITK_MAX = 8;      // K slices of the batched GEMMs
+constexpr int SPLITK_MAX_ROWS = 128;  // split K only for batches of up to this many rows
+
+// Batched-decode GEMM over few rows: when the weight-row tiles alone cannot fill the GPU, K is
+// split over up to 8 CTA slices whose partial products a finish kernel sums in slice order
+// (deterministic) before the epilogue.
+template <int EPI>
+cudaError_t batch_gemm(icua_engine* e, const void* x, TcGemmParams p, cudaStream_t s) {
+    const TcTile t = choose_tc_tile(p.n_rows, p.m_tok, e->n_sm, true);
+    const int tiles = (p.n_rows / (TC_BM * t.mh)) * ((p.m_tok + t.bn - 1) / t.bn);
+    int ks = std::min(SPLITK_MAX, e->n_sm / std::max(tiles, 1));
+    ks = std::min(ks, p.k / TC_BK / 4);  // at least four k-blocks per slice
+    if (ks < 2 || p.m_tok > SPLITK_MAX_ROWS) return launch_tc_gemm<EPI>(x, e->cfg.max_pass, p, s);
+    TcGemmParams q = p;
+    q.out = e->splitk_part;
+    q.ldo = p.n_rows;
+    q.out_zstride = (long long)p.m_tok * p.n_rows;
+    cudaError_t err = launch_tc_gemm<TC_STORE>(x, e->cfg.max_pass, q, s, nullptr, ks);
+    if (err != cudaSuccess) return err;
+    const long long total = (long long)p.m_tok * p.n_rows;
+    const int grid = (int)std::min<long long>((total + 255) / 256, 4LL * e->n_sm);
+    return launch(splitk_finish_kernel<EPI>, grid, 256, 0, s, false, (const float*)e->splitk_part, ks, p.m_tok,
+                  p.n_rows, p.out, p.out_h);
 }
 
 cudaError_t launch_dequant_f16(const Matrix& m, __half* out, int n_sm, cudaStream_t s) {
@@ -772,7 +800,7 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
         {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3((n_rows + PA_BQ - 1) / PA_BQ, NKV);
-            cfg.blockDim = dim3(256);
+            cfg.blockDim = dim3(PA_THREADS);
             cfg.dynamicSmemBytes = PrefillAttnSmem<KVT>::total;
             cfg.stream = st;
             if ((err = cudaLaunchKernelEx(&cfg, prefill_attn_kernel<KVT>, (const float*)e->pq, (const KVT*)kc,
@@ -825,7 +853,7 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
         TcGemmParams p = tc_params(ly.qkv, n_rows, e->gemm_err);
         p.out = e->pqkv;
         p.ldo = QKV_ROWS;
-        if ((err = launch_tc_gemm<TC_STORE>(e->pxn, e->cfg.max_pass, p, st)) != cudaSuccess) return err;
+        if ((err = batch_gemm<TC_STORE>(e, e->pxn, p, st)) != cudaSuccess) return err;
         {
             AttnParams<KVT> a{};
             a.qkv = e->pqkv;
@@ -863,18 +891,18 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
         p = tc_params(ly.o, n_rows, e->gemm_err);
         p.out = e->px;
         p.ldo = H;
-        if ((err = launch_tc_gemm<TC_RESID>(e->pattn, e->cfg.max_pass, p, st)) != cudaSuccess) return err;
+        if ((err = batch_gemm<TC_RESID>(e, e->pattn, p, st)) != cudaSuccess) return err;
         if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
                           (const float*)ly.mlp_norm, n_rows, e->pxn)) != cudaSuccess)
             return err;
         p = tc_params(ly.gu, n_rows, e->gemm_err);
         p.out_h = e->ph;
         p.ldh = FF;
-        if ((err = launch_tc_gemm<TC_SWIGLU>(e->pxn, e->cfg.max_pass, p, st)) != cudaSuccess) return err;
+        if ((err = batch_gemm<TC_SWIGLU>(e, e->pxn, p, st)) != cudaSuccess) return err;
         p = tc_params(ly.d, n_rows, e->gemm_err);
         p.out = e->px;
         p.ldo = H;
-        if ((err = launch_tc_gemm<TC_RESID>(e->ph, e->cfg.max_pass, p, st)) != cudaSuccess) return err;
+        if ((err = batch_gemm<TC_RESID>(e, e->ph, p, st)) != cudaSuccess) return err;
     }
     if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
                       (const float*)e->final_norm, n_rows, e->pxn)) != cudaSuccess)
@@ -1030,6 +1058,7 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
         TRY(dalloc_t(eng, &eng->pattn, P * H));
         TRY(dalloc_t(eng, &eng->ph, P * FF));
         TRY(dalloc_t(eng, &eng->gemm_err, 1));
+        TRY(dalloc_t(eng, &eng->splitk_part, (size_t)SPLITK_MAX * SPLITK_MAX_ROWS * GU_ROWS));
         for (int set = 0; set < 2; ++set) {
             TRY(dalloc_t(eng, &eng->wscr[set][0], (size_t)QKV_ROWS * H));
             TRY(dalloc_t(eng, &eng->wscr[set][1], (size_t)H * H));

@@ -50,6 +50,8 @@ struct TcGemmParams {
     float* best_v;             // TC_ARGMAX: per (row tile, token) maximum [gridDim.x][m_tok] and the
     int* best_i;               //   row of it (lowest row on ties); out, when set, also gets the values
     int* err;                  // error flags (bounded waits that gave up)
+    long long out_zstride;     // split K (gridDim.z > 1, TC_STORE only): slice z covers k-blocks
+                               //   [z nk / Z, (z+1) nk / Z) and stores to out + z * out_zstride
 };
 
 // Shared-memory layout of one CTA for a (BN, MH, format) choice; the same arithmetic runs on the
@@ -260,7 +262,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     const int tile0 = blockIdx.x * (MH * TC_BM / 16);
     const int row0 = blockIdx.x * (MH * TC_BM);
     const int tok0 = blockIdx.y * BN;
-    const int nk = p.k / TC_BK;
+    const int nk_all = p.k / TC_BK;
+    const int kb0 = (int)((long long)nk_all * blockIdx.z / gridDim.z);
+    const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb0;
     constexpr uint32_t tmem_cols = MH == 2 ? 512 : 256;
     constexpr int half_cols = 256;  // column offset of the second accumulator
 
@@ -299,18 +303,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                     mbar_expect_tx(&bfull[s], (uint32_t)(SM.a_bytes + SM.b_bytes));
 #pragma unroll
                     for (int h = 0; h < MH; ++h)
-                        tma_load_2d(smem + SM.a_off + s * SM.a_bytes + h * TC_BM * 128, &wmap, kc * TC_BK,
+                        tma_load_2d(smem + SM.a_off + s * SM.a_bytes + h * TC_BM * 128, &wmap, (kb0 + kc) * TC_BK,
                                     row0 + h * TC_BM, &bfull[s]);
                 } else {
                     uint8_t* raw = smem + SM.raw_off + s * SM.raw_bytes;
                     mbar_expect_tx(&rawfull[s], NU * UB);
 #pragma unroll 1
                     for (int t = 0; t < NU; ++t)
-                        bulk_g2s(raw + t * UB, p.w + icua_layout::unit_offset(FMT, p.n_tiles, p.upt, tile0 + t, kc),
+                        bulk_g2s(raw + t * UB, p.w + icua_layout::unit_offset(FMT, p.n_tiles, p.upt, tile0 + t, kb0 + kc),
                                  UB, &rawfull[s]);
                     mbar_expect_tx(&bfull[s], (uint32_t)SM.b_bytes);
                 }
-                tma_load_2d(smem + SM.b_off + s * SM.b_bytes, &xmap, kc * TC_BK, tok0, &bfull[s]);
+                tma_load_2d(smem + SM.b_off + s * SM.b_bytes, &xmap, (kb0 + kc) * TC_BK, tok0, &bfull[s]);
             }
             // the copies of the last stages complete before the CTA may exit (at once on success)
             for (int c = (kc > S ? kc - S : 0); c < kc; ++c) {
@@ -412,7 +416,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                     const int tok = tok0 + c * 32 + j;
                     if (j >= ncol || tok >= p.m_tok) break;
                     if (EPI == TC_STORE) {
-                        p.out[(size_t)tok * p.ldo + row] = v[j];
+                        p.out[blockIdx.z * p.out_zstride + (size_t)tok * p.ldo + row] = v[j];
                     } else if (EPI == TC_ARGMAX) {
                         if (p.out != nullptr) p.out[(size_t)tok * p.ldo + row] = v[j];
                         float bv = v[j];
@@ -483,6 +487,32 @@ __global__ void __launch_bounds__(256) dequant_q4s_f16_kernel(const uint8_t* til
             o[t] = *reinterpret_cast<const uint32_t*>(&hv);
         }
         *reinterpret_cast<uint4*>(out + (size_t)row * K + (size_t)j8 * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// Split-K finish: sums the Z partial products [Z][m][n] in slice order (deterministic) and applies
+// the epilogue of the GEMM that was split: store, residual add, or SwiGLU (gate rows 0..7 and up
+// rows 8..15 of each 16-row tile) into fp16.
+template <int EPI>
+__global__ void __launch_bounds__(256) splitk_finish_kernel(const float* part, int Z, int m, int n, float* out,
+                                                            __half* out_h) {
+    const long long total = (long long)m * n;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        float acc = part[i];
+        for (int z = 1; z < Z; ++z) acc += part[(long long)z * total + i];
+        if (EPI == TC_STORE) {
+            out[i] = acc;
+        } else if (EPI == TC_RESID) {
+            out[i] = out[i] + acc;
+        } else {
+            const int row = (int)(i % n), r = row & 15;
+            if (r < 8) {
+                float up = part[i + 8];
+                for (int z = 1; z < Z; ++z) up += part[(long long)z * total + i + 8];
+                const long long tok = i / n;
+                out_h[tok * (n / 2) + (row >> 4) * 8 + r] = __float2half_rn((acc / (1.0f + expf(-acc))) * up);
+            }
+        }
     }
 }
 

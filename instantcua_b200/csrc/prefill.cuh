@@ -111,9 +111,10 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(const float* qkv, int n
 }
 
 // ---- causal GQA prefill attention ------------------------------------------------------------
-constexpr int PA_BQ = 64;   // query rows per CTA and q head (4 warps x 16 rows)
+constexpr int PA_BQ = 32;   // query rows per CTA and q head (2 warps x 16 rows)
 constexpr int PA_BK = 64;   // cache rows per stage
 constexpr int PA_NS = 2;    // stages
+constexpr int PA_THREADS = 128;
 
 template <typename KVT>
 struct PrefillAttnSmem {
@@ -123,14 +124,16 @@ struct PrefillAttnSmem {
     static constexpr int total = bars_off + PA_NS * 8;
 };
 
-// One CTA per (block of 64 prompt rows, kv head); warps 0-3 take q head 2h, warps 4-7 q head
+// One CTA per (block of 32 prompt rows, kv head); warps 0-1 take q head 2h, warps 2-3 q head
 // 2h+1, 16 rows each, so every K/V tile in shared memory serves both heads of the GQA group.
 // Query row i sits at cache slot pos0 + i and attends slots [0, pos0 + i].  Scores and the
-// softmax stay in registers (m16n8k16 accumulators); q and the probabilities enter the MMAs as
-// hi + lo pairs in the cache type, so the only rounding beyond fp32 is that of the cache.
+// softmax stay in registers (m16n8k16 accumulators, fp32); q and the probabilities enter the
+// MMAs in the cache type, the precision of the reference prefill (fp16 operands, fp32
+// accumulation).  Small row blocks keep the causal critical path (the last block reads every
+// slot) short; blocks are scheduled longest first.
 template <typename KVT>
-__global__ void __launch_bounds__(256, 1) prefill_attn_kernel(const float* q, const KVT* kc, const KVT* vc, int max_ctx,
-                                                              int n, int pos0, __half* out, int* err) {
+__global__ void __launch_bounds__(PA_THREADS) prefill_attn_kernel(const float* q, const KVT* kc, const KVT* vc,
+                                                                  int max_ctx, int n, int pos0, __half* out, int* err) {
     extern __shared__ __align__(128) uint8_t smem[];
     using S = PrefillAttnSmem<KVT>;
     constexpr int RB = S::row_bytes;
@@ -139,8 +142,8 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(const float* q, co
     const int h = blockIdx.y;
     const int qb = gridDim.x - 1 - blockIdx.x;   // longest blocks first
     const int r0 = qb * PA_BQ;
-    const int hh = warp >> 2, qh = 2 * h + hh;
-    const int wr0 = r0 + 16 * (warp & 3);        // first row of this warp
+    const int hh = warp >> 1, qh = 2 * h + hh;
+    const int wr0 = r0 + 16 * (warp & 1);        // first row of this warp
     const int kend = pos0 + min(r0 + PA_BQ, n);   // cache slots [0, kend) are read
     const int nblk = (kend + PA_BK - 1) / PA_BK;
     const KVT* kbase = kc + (size_t)h * max_ctx * HD;
@@ -160,8 +163,10 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(const float* q, co
         for (int b = 0; b < min(PA_NS, nblk); ++b) issue(b);
     }
 
-    // q fragments (A operand, rows g / g+8, dims 16 kk + 2t (+1, +8, +9)), hi and lo parts
-    uint32_t qa[8][2][4];
+    // q fragments (A operand, rows g / g+8, dims 16 kk + 2t (+1, +8, +9)), scaled by log2(e) so
+    // that the softmax runs on exp2
+    constexpr float LOG2E = 1.4426950408889634f;
+    uint32_t qa[8][4];
     {
         const int ra = min(wr0 + g, n - 1), rb = min(wr0 + g + 8, n - 1);
         const float* qra = q + ((size_t)ra * NQ + qh) * HD;
@@ -173,13 +178,10 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(const float* q, co
             const float2 a1 = *reinterpret_cast<const float2*>(qrb + d0);
             const float2 a2 = *reinterpret_cast<const float2*>(qra + d0 + 8);
             const float2 a3 = *reinterpret_cast<const float2*>(qrb + d0 + 8);
-#pragma unroll
-            for (int part = 0; part < 2; ++part) {
-                qa[kk][part][0] = pack2<KVT>(split_part<KVT>(a0.x, part), split_part<KVT>(a0.y, part));
-                qa[kk][part][1] = pack2<KVT>(split_part<KVT>(a1.x, part), split_part<KVT>(a1.y, part));
-                qa[kk][part][2] = pack2<KVT>(split_part<KVT>(a2.x, part), split_part<KVT>(a2.y, part));
-                qa[kk][part][3] = pack2<KVT>(split_part<KVT>(a3.x, part), split_part<KVT>(a3.y, part));
-            }
+            qa[kk][0] = pack2<KVT>(float_to_kv<KVT>(a0.x * LOG2E), float_to_kv<KVT>(a0.y * LOG2E));
+            qa[kk][1] = pack2<KVT>(float_to_kv<KVT>(a1.x * LOG2E), float_to_kv<KVT>(a1.y * LOG2E));
+            qa[kk][2] = pack2<KVT>(float_to_kv<KVT>(a2.x * LOG2E), float_to_kv<KVT>(a2.y * LOG2E));
+            qa[kk][3] = pack2<KVT>(float_to_kv<KVT>(a3.x * LOG2E), float_to_kv<KVT>(a3.y * LOG2E));
         }
     }
     float o[16][4];
@@ -204,7 +206,7 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(const float* q, co
         const int s0 = b * PA_BK, cnt = min(PA_BK, kend - s0);
         if (s0 <= warp_last) {
             const uint32_t kst = smem_u32(smem + st * S::stage_bytes), vst = kst + PA_BK * RB;
-            // ---- S = Q K^T over 64 slots: 8 n-tiles of 8 slots ----
+            // ---- S = Q K^T over 64 slots: 8 n-tiles of 8 slots (log2 units) ----
             float s[8][4];
 #pragma unroll
             for (int nt = 0; nt < 8; ++nt)
@@ -218,10 +220,8 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(const float* q, co
                     const int chunk = 2 * kk + ((lane >> 3) & 1);
                     uint32_t bf[4];
                     ldsm_x4(bf, kst + row * RB + ((chunk ^ (row & 7)) << 4));
-                    mma_kv<KVT>(s[2 * np], qa[kk][0], bf[0], bf[1]);
-                    mma_kv<KVT>(s[2 * np], qa[kk][1], bf[0], bf[1]);
-                    mma_kv<KVT>(s[2 * np + 1], qa[kk][0], bf[2], bf[3]);
-                    mma_kv<KVT>(s[2 * np + 1], qa[kk][1], bf[2], bf[3]);
+                    mma_kv<KVT>(s[2 * np], qa[kk], bf[0], bf[1]);
+                    mma_kv<KVT>(s[2 * np + 1], qa[kk], bf[2], bf[3]);
                 }
             }
             // ---- causal mask + online softmax (rows g: e 0,1; g+8: e 2,3) ----
@@ -244,17 +244,17 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(const float* q, co
             mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
             mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
             const float mna = fmaxf(m_a, mxa), mnb = fmaxf(m_b, mxb);
-            const float ca = (mna == -INFINITY) ? 1.f : expf(m_a - mna);
-            const float cb = (mnb == -INFINITY) ? 1.f : expf(m_b - mnb);
+            const float ca = (mna == -INFINITY) ? 1.f : exp2f(m_a - mna);
+            const float cb = (mnb == -INFINITY) ? 1.f : exp2f(m_b - mnb);
             m_a = mna;
             m_b = mnb;
             float suma = 0.f, sumb = 0.f;
 #pragma unroll
             for (int nt = 0; nt < 8; ++nt) {
-                s[nt][0] = (s[nt][0] == -INFINITY) ? 0.f : expf(s[nt][0] - mna);
-                s[nt][1] = (s[nt][1] == -INFINITY) ? 0.f : expf(s[nt][1] - mna);
-                s[nt][2] = (s[nt][2] == -INFINITY) ? 0.f : expf(s[nt][2] - mnb);
-                s[nt][3] = (s[nt][3] == -INFINITY) ? 0.f : expf(s[nt][3] - mnb);
+                s[nt][0] = (s[nt][0] == -INFINITY) ? 0.f : exp2f(s[nt][0] - mna);
+                s[nt][1] = (s[nt][1] == -INFINITY) ? 0.f : exp2f(s[nt][1] - mna);
+                s[nt][2] = (s[nt][2] == -INFINITY) ? 0.f : exp2f(s[nt][2] - mnb);
+                s[nt][3] = (s[nt][3] == -INFINITY) ? 0.f : exp2f(s[nt][3] - mnb);
                 suma += s[nt][0] + s[nt][1];
                 sumb += s[nt][2] + s[nt][3];
             }
@@ -270,26 +270,19 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(const float* q, co
             // ---- O += P V: P from the score registers (A operand), V^T by ldmatrix.trans ----
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {  // 16 slots per step
-                uint32_t pa[2][4];
-#pragma unroll
-                for (int part = 0; part < 2; ++part) {
-                    pa[part][0] = pack2<KVT>(split_part<KVT>(s[2 * kk][0], part), split_part<KVT>(s[2 * kk][1], part));
-                    pa[part][1] = pack2<KVT>(split_part<KVT>(s[2 * kk][2], part), split_part<KVT>(s[2 * kk][3], part));
-                    pa[part][2] =
-                        pack2<KVT>(split_part<KVT>(s[2 * kk + 1][0], part), split_part<KVT>(s[2 * kk + 1][1], part));
-                    pa[part][3] =
-                        pack2<KVT>(split_part<KVT>(s[2 * kk + 1][2], part), split_part<KVT>(s[2 * kk + 1][3], part));
-                }
+                uint32_t pa[4];
+                pa[0] = pack2<KVT>(float_to_kv<KVT>(s[2 * kk][0]), float_to_kv<KVT>(s[2 * kk][1]));
+                pa[1] = pack2<KVT>(float_to_kv<KVT>(s[2 * kk][2]), float_to_kv<KVT>(s[2 * kk][3]));
+                pa[2] = pack2<KVT>(float_to_kv<KVT>(s[2 * kk + 1][0]), float_to_kv<KVT>(s[2 * kk + 1][1]));
+                pa[3] = pack2<KVT>(float_to_kv<KVT>(s[2 * kk + 1][2]), float_to_kv<KVT>(s[2 * kk + 1][3]));
                 const int row = min(16 * kk + (lane & 7) + (((lane >> 3) & 1) << 3), cnt - 1);
 #pragma unroll
                 for (int dp = 0; dp < 8; ++dp) {  // 16 dims per ldmatrix.x4.trans
                     const int chunk = 2 * dp + (lane >> 4);
                     uint32_t vf[4];
                     ldsm_x4_trans(vf, vst + row * RB + ((chunk ^ (row & 7)) << 4));
-                    mma_kv<KVT>(o[2 * dp], pa[0], vf[0], vf[1]);
-                    mma_kv<KVT>(o[2 * dp], pa[1], vf[0], vf[1]);
-                    mma_kv<KVT>(o[2 * dp + 1], pa[0], vf[2], vf[3]);
-                    mma_kv<KVT>(o[2 * dp + 1], pa[1], vf[2], vf[3]);
+                    mma_kv<KVT>(o[2 * dp], pa, vf[0], vf[1]);
+                    mma_kv<KVT>(o[2 * dp + 1], pa, vf[2], vf[3]);
                 }
             }
         }
