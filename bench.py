@@ -4,6 +4,10 @@ the CPU baseline.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
+Side modes (one GPU, one JSON line each): --micro (config 1, per-shape dequant-GEMV GB/s),
+--prefill (config 3, multimodal prefill through the tensor-core path, TFLOP/s against the
+measured GEMM peak), --batched (config 4, 64 sessions decoded together, HBM roofline).
+
 A step is one greedy decode token (28 layers + lm_head + on-device argmax) of a session whose KV
 cache was pre-filled with 4096 positions of N(0,1) bf16 values; the context grows by one per step.
 Weights are seeded N(0,0.02) (torch CUDA generator), q4s decoder matrices and q8 lm_head.  The
@@ -104,22 +108,49 @@ def model_file(rank_local: int, dist, device: int) -> str:
     return path
 
 
-def run_ours(args):
-    import numpy as np
-    import torch
+def init_replicas(backend: str = "nccl"):
+    """One process per GPU (torchrun env).  Returns (dist or None, world, rank, local rank).  The
+    process group carries only the barriers and the max-over-ranks timing: every replica owns its
+    weights and caches, nothing crosses GPUs on the decode path."""
+    import datetime
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import datetime
+    if world == 1:
+        return None, 1, 0, local
+    import torch
+    import torch.distributed as tdist
 
-        import torch.distributed as tdist
-
+    kw = {}
+    if backend == "nccl":
         torch.cuda.set_device(local)
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
-        dist = tdist
+        kw["device_id"] = torch.device("cuda", local)
+    tdist.init_process_group(backend, timeout=datetime.timedelta(seconds=600), **kw)
+    return tdist, world, rank, local
+
+
+def max_over_ranks(dist, value: float, device: str = "cuda") -> float:
+    """Max of a per-rank time over all ranks (the slowest replica sets the job time)."""
+    if dist is None:
+        return value
+    import torch
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def aggregate_rate(units_per_rank: int, world: int, max_time_s: float) -> float:
+    """Whole-job rate: the units all ranks processed over the slowest rank's time."""
+    return world * units_per_rank / max_time_s
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    dist, world, rank, local = init_replicas("nccl")
     torch.cuda.set_device(local)
     from instantcua_b200 import Engine
     from instantcua_b200 import _lib as L
@@ -142,13 +173,11 @@ def run_ours(args):
         eng.decode(K)
         ms = eng.last_timing.decode_ms
     torch.cuda.synchronize()
+    ms = max_over_ranks(dist, ms)
     if dist is not None:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
         dist.barrier()
     ms_step = ms / K
-    value = world * K / (ms / 1e3)
+    value = aggregate_rate(K, world, ms / 1e3)
 
     # e2e through the public host API: one decode step per call, token in from host, token out
     # to host, synchronised each call (inputs and results cross PCIe every step).
@@ -159,12 +188,8 @@ def run_ours(args):
     t0 = time.perf_counter()
     for _ in range(KE):
         cur = eng.decode_step(cur)
-    e2e_s = time.perf_counter() - t0
-    if dist is not None:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = world * KE / e2e_s
+    e2e_s = max_over_ranks(dist, time.perf_counter() - t0)
+    e2e = aggregate_rate(KE, world, e2e_s)
 
     # roofline of the dominant kernel: the q8 lm_head dequant-GEMV (largest single stream, 330.6 MB),
     # timed alone with CUDA events on the launching stream; and the whole step for context.

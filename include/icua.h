@@ -154,7 +154,14 @@ icua_status icua_decode_batch(icua_engine* eng, const int32_t* sessions, int32_t
  * call's session order) to host_out; NULL / 0 turns it off. */
 icua_status icua_capture_batch_logits(icua_engine* eng, float* host_out, int32_t n_rows);
 
-/* Whole call: reset session, prefill, decode; returns tokens like generateVision. */
+/* System-prompt KV prefix cache (reference Engine.usePrefixCache, Engine.swift:40, 719-738; on
+ * by default): icua_generate keeps the K/V rows of the tokens before the visual block when they
+ * equal the previous call's on that session, and prefills from the visual block on.  Any other
+ * write to the session's cache (icua_reset_session, icua_inject_kv*) forgets the prefix. */
+icua_status icua_set_prefix_cache(icua_engine* eng, int32_t enable);
+
+/* Whole call: reset session (keeping a cached prefix), prefill, decode; returns tokens like
+ * generateVision. */
 icua_status icua_generate(icua_engine* eng, int32_t session, const int32_t* tokens, int32_t n,
                           const icua_visual* visual, int32_t max_new, int32_t write_first_logits,
                           int32_t* out_tokens, int32_t* n_out);

@@ -73,6 +73,7 @@ PROTOTYPES = {
     "icua_pack_matrix": (_I, [_I, _I, _I, _P, _P, _P]),
     "icua_gemv": (_I, [_I, _I, _I, _P, _P, _I, _P, _P]),
     "icua_decode_batch": (_I, [_P, _IP, _I, _IP, _I, _IP]),
+    "icua_set_prefix_cache": (_I, [_P, _I]),
     "icua_capture_batch_logits": (_I, [_P, _FP, _I]),
     "icua_gemm_q4s": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),
     "icua_dequant_q4s_f16": (_I, [_I, _I, _P, _P, _P]),

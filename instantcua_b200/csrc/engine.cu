@@ -75,6 +75,10 @@ struct Session {
     int done = 0;
     int rope_delta = 0;
     cudaGraphExec_t g_prefill_tok = nullptr, g_step1 = nullptr, g_stepn = nullptr;
+    // system-prompt prefix cache: the tokens before the visual block of the last icua_generate,
+    // whose K/V rows [0, prefix.size()) are still in the cache
+    std::vector<int> prefix;
+    bool prefix_valid = false;
 };
 
 }  // namespace
@@ -106,6 +110,7 @@ struct icua_engine {
     std::vector<Session> sessions;
     std::vector<void*> allocations;
     int eos0 = 151645, eos1 = 151643, stop_on_eos = 1;
+    int prefix_cache = 1;  // reference Engine.usePrefixCache (Engine.swift:40), on by default
     icua_timing timing{};
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     float inv_freq[64];
@@ -115,10 +120,10 @@ struct icua_engine {
     int* gemm_err = nullptr;                     // error flags of the batched kernels
     float* splitk_part = nullptr;                // split-K partial products of the batched GEMMs
     // prefill: the layer matrices dequantised to fp16, two layers' sets (layer l in set l % 2),
-    // filled by a side stream one layer ahead of the GEMMs
+    // filled by a side stream one matrix ahead of the GEMMs
     __half* wscr[2][4] = {{nullptr, nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr, nullptr}};
     cudaStream_t side = nullptr;
-    cudaEvent_t ev_ready[2] = {nullptr, nullptr}, ev_free[2] = {nullptr, nullptr};
+    cudaEvent_t ev_ready[8] = {}, ev_done[8] = {};  // per GEMM of the sequence, mod 8
     // sessions (contiguous arrays; Session holds pointers into them)
     DevState* st_all = nullptr;
     int* out_all = nullptr;
@@ -183,7 +188,9 @@ void setup_matrix(Matrix& m, int fmt, int n_rows, int k, int n_sm) {
     const int nw = fmt_slices(fmt), ku = k / 64 / nw;
     m.stream = fmt == FMT_Q8 || tpc > SMALL_MAX_TILES;  // q8 kernels are built for the streaming path only
     m.chunk = m.stream ? 1 : tpc;
-    m.n_slots = m.stream ? 2 : 1;
+    // streaming ring depth: the q8 lm_head (330 MB, one launch) keeps 4 tiles per warp in flight,
+    // ~140 KB per SM, enough to cover HBM latency at full bandwidth
+    m.n_slots = !m.stream ? 1 : (fmt == FMT_Q8 ? 4 : 2);
     GemvSmem L{k, nw, m.n_slots, m.chunk, unit_bytes(fmt), ku, tpc, 0};
     m.smem = (size_t)L.total();  // without the RMSNorm weight copy; launch_gemv adds it
 }
@@ -324,7 +331,7 @@ cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaSt
     }
     cudaLaunchConfig_t cfg = {};
     if (ksplit > 1 && (EPI != TC_STORE || ksplit > p.k / TC_BK)) return cudaErrorInvalidValue;
-    cfg.gridDim = dim3(p.n_rows / (TC_BM * t.mh), (p.m_tok + t.bn - 1) / t.bn, ksplit);
+    cfg.gridDim = dim3((p.m_tok + t.bn - 1) / t.bn, p.n_rows / (TC_BM * t.mh), ksplit);
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = TcLayout(t.bn, t.mh, FMT, EPI == TC_ARGMAX).alloc;
     cfg.stream = s;
@@ -763,35 +770,52 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
                       (const float*)e->pooler, (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->px)) != cudaSuccess)
         return err;
     const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
-    // dequantisation of layer l's matrices into set l % 2 on the side stream, one layer ahead;
-    // a set is rewritten only after the GEMMs of the layer two back have been issued behind it
-    auto dequant_layer = [&](int l) -> cudaError_t {
-        const int set = l & 1;
-        cudaError_t er;
-        if ((er = cudaStreamWaitEvent(e->side, e->ev_free[set], 0)) != cudaSuccess) return er;
-        const Layer& ly = e->layers[l];
-        const Matrix* ms[4] = {&ly.qkv, &ly.o, &ly.gu, &ly.d};
-        for (int i = 0; i < (l == L - 1 ? 1 : 4); ++i)
-            if ((er = launch_dequant_f16(*ms[i], e->wscr[set][i], e->n_sm, e->side)) != cudaSuccess) return er;
-        return cudaEventRecord(e->ev_ready[set], e->side);
+    // The layer matrices in GEMM order (the last layer only projects K/V).  Matrix i is
+    // dequantised to fp16 on the side stream while GEMM i-1 runs (after GEMM i-2 has finished), so
+    // its tiles are still in L2 when GEMM i reads them; set (layer % 2, kind) holds it.
+    std::vector<std::pair<int, int>> seq;  // (layer, kind: 0 QKV, 1 O, 2 gate/up, 3 down)
+    for (int l = 0; l < L; ++l)
+        for (int kind = 0; kind < (l == L - 1 ? 1 : 4); ++kind) seq.emplace_back(l, kind);
+    auto matrix_of = [&](int i) -> const Matrix& {
+        const Layer& ly = e->layers[seq[i].first];
+        const int kind = seq[i].second;
+        return kind == 0 ? ly.qkv : kind == 1 ? ly.o : kind == 2 ? ly.gu : ly.d;
     };
-    for (int set = 0; set < 2; ++set)
-        if ((err = cudaEventRecord(e->ev_free[set], st)) != cudaSuccess) return err;
-    if ((err = dequant_layer(0)) != cudaSuccess) return err;
-    if (L > 1 && (err = dequant_layer(1)) != cudaSuccess) return err;
+    auto dequant = [&](int i) -> cudaError_t {
+        if (i >= (int)seq.size()) return cudaSuccess;
+        cudaError_t er;
+        if (i >= 2 && (er = cudaStreamWaitEvent(e->side, e->ev_done[(i - 2) % 8], 0)) != cudaSuccess) return er;
+        if ((er = launch_dequant_f16(matrix_of(i), e->wscr[seq[i].first & 1][seq[i].second], e->n_sm, e->side)) !=
+            cudaSuccess)
+            return er;
+        return cudaEventRecord(e->ev_ready[i % 8], e->side);
+    };
+    int gi = 0;  // next GEMM of the sequence
+    auto gemm_ready = [&]() { return cudaStreamWaitEvent(st, e->ev_ready[gi % 8], 0); };
+    auto gemm_issued = [&]() -> cudaError_t {
+        cudaError_t er = cudaEventRecord(e->ev_done[gi % 8], st);
+        if (er != cudaSuccess) return er;
+        ++gi;
+        return dequant(gi + 1);
+    };
+    // the side stream starts behind everything already queued on the main stream
+    if ((err = cudaEventRecord(e->ev_done[7], st)) != cudaSuccess) return err;
+    if ((err = cudaStreamWaitEvent(e->side, e->ev_done[7], 0)) != cudaSuccess) return err;
+    if ((err = dequant(0)) != cudaSuccess || (err = dequant(1)) != cudaSuccess) return err;
     for (int l = 0; l < L; ++l) {
         Layer& ly = e->layers[l];
         KVT* kc = reinterpret_cast<KVT*>(S.kc) + kv_layer * l;
         KVT* vc = reinterpret_cast<KVT*>(S.vc) + kv_layer * l;
         __half* const* w16 = e->wscr[l & 1];
-        if ((err = cudaStreamWaitEvent(st, e->ev_ready[l & 1], 0)) != cudaSuccess) return err;
         if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
                           (const float*)ly.attn_norm, n_rows, e->pxn)) != cudaSuccess)
             return err;
         TcGemmParams p = tc_params(ly.qkv, n_rows, errp);
         p.out = e->pqkv;
         p.ldo = QKV_ROWS;
+        if ((err = gemm_ready()) != cudaSuccess) return err;
         if ((err = launch_tc_gemm<TC_STORE, FMT_F16>(e->pxn, e->cfg.max_pass, p, st, w16[0])) != cudaSuccess) return err;
+        if ((err = gemm_issued()) != cudaSuccess) return err;
         if ((err = launch(qk_rope_kv_kernel<KVT>, n_rows, 256, 0, st, false, (const float*)e->pqkv, n_rows,
                           (const float*)ly.q_norm, (const float*)ly.k_norm, (const float2*)S.rope, pos0, kc, vc,
                           e->cfg.max_context, e->pq)) != cudaSuccess)
@@ -810,14 +834,18 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
         p = tc_params(ly.o, n_rows, errp);
         p.out = e->px;
         p.ldo = H;
+        if ((err = gemm_ready()) != cudaSuccess) return err;
         if ((err = launch_tc_gemm<TC_RESID, FMT_F16>(e->pattn, e->cfg.max_pass, p, st, w16[1])) != cudaSuccess) return err;
+        if ((err = gemm_issued()) != cudaSuccess) return err;
         if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
                           (const float*)ly.mlp_norm, n_rows, e->pxn)) != cudaSuccess)
             return err;
         p = tc_params(ly.gu, n_rows, errp);
         p.out_h = e->ph;
         p.ldh = FF;
+        if ((err = gemm_ready()) != cudaSuccess) return err;
         if ((err = launch_tc_gemm<TC_SWIGLU, FMT_F16>(e->pxn, e->cfg.max_pass, p, st, w16[2])) != cudaSuccess) return err;
+        if ((err = gemm_issued()) != cudaSuccess) return err;
         p = tc_params(ly.d, n_rows, errp);
         p.out = e->px;
         p.ldo = H;
@@ -826,9 +854,9 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
             p.ds_row0 = vis_off;
             p.ds_rows = n_vis;
         }
+        if ((err = gemm_ready()) != cudaSuccess) return err;
         if ((err = launch_tc_gemm<TC_RESID, FMT_F16>(e->ph, e->cfg.max_pass, p, st, w16[3])) != cudaSuccess) return err;
-        if ((err = cudaEventRecord(e->ev_free[l & 1], st)) != cudaSuccess) return err;
-        if (l + 2 < L && (err = dequant_layer(l + 2)) != cudaSuccess) return err;
+        if ((err = gemm_issued()) != cudaSuccess) return err;
     }
     return cudaSuccess;
 }
@@ -1064,8 +1092,10 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
             TRY(dalloc_t(eng, &eng->wscr[set][1], (size_t)H * H));
             TRY(dalloc_t(eng, &eng->wscr[set][2], (size_t)GU_ROWS * H));
             TRY(dalloc_t(eng, &eng->wscr[set][3], (size_t)H * FF));
-            cudaEventCreateWithFlags(&eng->ev_ready[set], cudaEventDisableTiming);
-            cudaEventCreateWithFlags(&eng->ev_free[set], cudaEventDisableTiming);
+        }
+        for (int i = 0; i < 8; ++i) {
+            cudaEventCreateWithFlags(&eng->ev_ready[i], cudaEventDisableTiming);
+            cudaEventCreateWithFlags(&eng->ev_done[i], cudaEventDisableTiming);
         }
         cudaStreamCreateWithFlags(&eng->side, cudaStreamNonBlocking);
         cudaMemset(eng->ph, 0, P * FF * sizeof(__half));
@@ -1122,9 +1152,9 @@ void icua_engine_destroy(icua_engine* eng) {
     for (void* p : eng->allocations) cudaFree(p);
     for (int i = 0; i < 4; ++i)
         if (eng->ev[i]) cudaEventDestroy(eng->ev[i]);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 8; ++i) {
         if (eng->ev_ready[i]) cudaEventDestroy(eng->ev_ready[i]);
-        if (eng->ev_free[i]) cudaEventDestroy(eng->ev_free[i]);
+        if (eng->ev_done[i]) cudaEventDestroy(eng->ev_done[i]);
     }
     if (eng->side) {
         cudaStreamSynchronize(eng->side);
@@ -1204,10 +1234,23 @@ icua_status icua_set_eos(icua_engine* eng, int32_t eos0, int32_t eos1, int32_t s
     return ICUA_OK;
 }
 
-icua_status icua_reset_session(icua_engine* eng, int32_t session) {
+static icua_status reset_session_impl(icua_engine* eng, int32_t session, bool keep_prefix);
+
+icua_status icua_reset_session(icua_engine* eng, int32_t session) { return reset_session_impl(eng, session, false); }
+
+icua_status icua_set_prefix_cache(icua_engine* eng, int32_t enable) {
+    if (!eng) return fail(nullptr, ICUA_ERR_INVALID, "null engine");
+    eng->prefix_cache = enable ? 1 : 0;
+    if (!enable)
+        for (auto& S : eng->sessions) S.prefix_valid = false;
+    return ICUA_OK;
+}
+
+static icua_status reset_session_impl(icua_engine* eng, int32_t session, bool keep_prefix) {
     if (!eng) return fail(nullptr, ICUA_ERR_INVALID, "null engine");
     Session* S = get_session(eng, session);
     if (!S) return fail(eng, ICUA_ERR_INVALID, "session %d out of range", session);
+    if (!keep_prefix) S->prefix_valid = false;
     CK(cudaSetDevice(eng->cfg.device));
     S->pos = 0;
     S->step = 0;
@@ -1234,6 +1277,7 @@ icua_status icua_inject_kv(icua_engine* eng, int32_t session, const float* k, co
     Session* S = eng ? get_session(eng, session) : nullptr;
     if (!S || !k || !v || n_pos < 0) return fail(eng, ICUA_ERR_INVALID, "bad argument");
     if (n_pos >= eng->cfg.max_context) return fail(eng, ICUA_ERR_CAPACITY, "%d positions exceed max_context", n_pos);
+    S->prefix_valid = false;
     CK(cudaSetDevice(eng->cfg.device));
     const int L = eng->cfg.n_layers, C = eng->cfg.max_context;
     std::vector<uint16_t> kb((size_t)NKV * n_pos * HD), vb((size_t)NKV * n_pos * HD);
@@ -1274,6 +1318,7 @@ icua_status icua_inject_kv_random(icua_engine* eng, int32_t session, int32_t n_p
     Session* S = eng ? get_session(eng, session) : nullptr;
     if (!S || n_pos < 0) return fail(eng, ICUA_ERR_INVALID, "bad argument");
     if (n_pos >= eng->cfg.max_context) return fail(eng, ICUA_ERR_CAPACITY, "%d positions exceed max_context", n_pos);
+    S->prefix_valid = false;
     CK(cudaSetDevice(eng->cfg.device));
     if (eng->cfg.kv_dtype == ICUA_KV_F16)
         kv_fill_random_kernel<__half><<<eng->n_sm * 8, 256, 0, eng->stream>>>(
@@ -1378,6 +1423,7 @@ icua_status icua_prefill(icua_engine* eng, int32_t session, const int32_t* token
     if ((s = check_ready(eng)) != ICUA_OK) return s;
     Session* S = get_session(eng, session);
     if (!S) return fail(eng, ICUA_ERR_INVALID, "session %d out of range", session);
+    if (S->pos < (int)S->prefix.size()) S->prefix_valid = false;  // this prefill overwrites prefix rows
     CK(cudaSetDevice(eng->cfg.device));
     if ((s = ensure_graphs(eng, *S)) != ICUA_OK) return s;
     int vis_off = -1, n_vis = 0;
@@ -1623,10 +1669,35 @@ icua_status icua_generate(icua_engine* eng, int32_t session, const int32_t* toke
                           int32_t max_new, int32_t write_first_logits, int32_t* out, int32_t* n_out) {
     if (!eng || !tokens || !out || !n_out) return fail(eng, ICUA_ERR_INVALID, "null argument");
     const auto t0 = std::chrono::steady_clock::now();
-    icua_status s = icua_reset_session(eng, session);
+    Session* S = get_session(eng, session);
+    if (!S) return fail(eng, ICUA_ERR_INVALID, "session %d out of range", session);
+    // System-prompt prefix cache (reference Engine.swift:719-738): when the tokens before the
+    // visual block equal those of this session's previous call, their K/V rows are still valid
+    // and the prefill starts at the visual block.
+    int vis_off = -1;
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] == IMAGE_PAD_ID) {
+            vis_off = i;
+            break;
+        }
+    const bool use_cache = eng->prefix_cache && vis_off > 0 && vis != nullptr;
+    const bool hit = use_cache && S->prefix_valid && (int)S->prefix.size() == vis_off &&
+                     std::equal(S->prefix.begin(), S->prefix.end(), tokens);
+    icua_status s = reset_session_impl(eng, session, hit);
     if (s != ICUA_OK) return s;
     int first = 0;
-    if ((s = icua_prefill(eng, session, tokens, n, vis, write_first_logits, &first)) != ICUA_OK) return s;
+    if (hit) {
+        S->pos = vis_off;  // rows [0, vis_off) of the cache are the prefix's
+        if ((s = icua_prefill(eng, session, tokens + vis_off, n - vis_off, vis, write_first_logits, &first)) != ICUA_OK)
+            return s;
+    } else {
+        S->prefix_valid = false;
+        if ((s = icua_prefill(eng, session, tokens, n, vis, write_first_logits, &first)) != ICUA_OK) return s;
+        if (use_cache) {
+            S->prefix.assign(tokens, tokens + vis_off);
+            S->prefix_valid = true;
+        }
+    }
     *n_out = 0;
     if (max_new <= 0) return ICUA_OK;
     if (eng->stop_on_eos && (first == eng->eos0 || first == eng->eos1)) {

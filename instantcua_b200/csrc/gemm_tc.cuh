@@ -47,7 +47,7 @@ struct TcGemmParams {
     int ldh;
     const float* deepstack;    // TC_RESID: optional rows added after the residual, [ds_rows][ldo]
     int ds_row0, ds_rows;      // token range [ds_row0, ds_row0 + ds_rows) that receives them
-    float* best_v;             // TC_ARGMAX: per (row tile, token) maximum [gridDim.x][m_tok] and the
+    float* best_v;             // TC_ARGMAX: per (row tile, token) maximum [row tiles][m_tok] and the
     int* best_i;               //   row of it (lowest row on ties); out, when set, also gets the values
     int* err;                  // error flags (bounded waits that gave up)
     long long out_zstride;     // split K (gridDim.z > 1, TC_STORE only): slice z covers k-blocks
@@ -259,9 +259,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     uint64_t* accfull = empty + S;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM.tmem_off);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile0 = blockIdx.x * (MH * TC_BM / 16);
-    const int row0 = blockIdx.x * (MH * TC_BM);
-    const int tok0 = blockIdx.y * BN;
+    // grid: x = token tile (fastest), y = weight-row tile, z = K slice; CTAs that share a weight
+    // tile are launched together, so it comes from DRAM once and from L2 for the others
+    const int rtile = blockIdx.y;
+    const int tile0 = rtile * (MH * TC_BM / 16);
+    const int row0 = rtile * (MH * TC_BM);
+    const int tok0 = blockIdx.x * BN;
     const int nk_all = p.k / TC_BK;
     const int kb0 = (int)((long long)nk_all * blockIdx.z / gridDim.z);
     const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb0;
@@ -378,7 +381,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         } else {
             const int q = warp & 3, wg = (warp - 2) >> 2;
             const int h = MH == 2 ? wg : 0;
-            const int row = blockIdx.x * (MH * TC_BM) + h * TC_BM + q * 32 + lane;
+            const int row = row0 + h * TC_BM + q * 32 + lane;
             const int cstep = MH == 2 ? 1 : 2;
 #pragma unroll 1
             for (int c = (MH == 2 ? 0 : wg); c * 32 < BN; c += cstep) {
@@ -451,8 +454,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 const float2 e = red[q * BN + t];
                 argmax_merge(bv, bi, e.x, __float_as_int(e.y));
             }
-            p.best_v[(size_t)blockIdx.x * p.m_tok + tok0 + t] = bv;
-            p.best_i[(size_t)blockIdx.x * p.m_tok + tok0 + t] = bi;
+            p.best_v[(size_t)rtile * p.m_tok + tok0 + t] = bv;
+            p.best_i[(size_t)rtile * p.m_tok + tok0 + t] = bi;
         }
     }
     if (warp == 1) {

@@ -147,6 +147,16 @@ class Engine:
         L.check(self._lib.icua_decode(self._h, session, max_new, out.ctypes.data_as(L._IP), C.byref(n)), self._h)
         return out[: n.value].tolist()
 
+    @property
+    def use_prefix_cache(self) -> bool:
+        return getattr(self, "_prefix_cache", True)
+
+    @use_prefix_cache.setter
+    def use_prefix_cache(self, on: bool) -> None:
+        """Engine.usePrefixCache: reuse the K/V of an unchanged system prompt before the image."""
+        L.check(self._lib.icua_set_prefix_cache(self._h, int(bool(on))), self._h)
+        self._prefix_cache = bool(on)
+
     def decode_batch(self, sessions, steps: int, in_tokens=None) -> np.ndarray:
         """Batched greedy decode of several sessions at once; returns int32 [len(sessions), steps]
         (-1 after a session's EOS)."""

@@ -152,3 +152,30 @@ def test_model_file_roundtrip(require_gpu, golden, tensors, tmp_path):
     with pytest.raises(IcuaError) as ex:
         Engine(str(bad), n_layers=2, vocab=1024, max_context=64, max_pass=16, max_steps=8)
     assert ex.value.status == L.ERR_FORMAT
+
+
+def test_prefix_cache_reuses_system_prompt(require_gpu, golden, tensors):
+    """Engine.usePrefixCache (Engine.swift:719-738): a second generate with the same tokens before
+    the image prefills only from the visual block on, with the same tokens and first logits."""
+    args = dict(pooler=golden["mm_pooler"], deepstack=list(golden["mm_deepstack"]),
+                grid=tuple(golden["mm_grid"].tolist()), write_first_logits=True)
+    toks = golden["mm_tokens"]
+    n_prefix = int(np.argmax(toks == 151655))
+    e = make_engine(tensors)
+    a = e.generate_vision(toks, max_new_tokens=4, **args)
+    la = e.logits()
+    assert e.last_timing.prefill_tokens == len(toks)
+    b = e.generate_vision(toks, max_new_tokens=4, **args)
+    lb = e.logits()
+    assert e.last_timing.prefill_tokens == len(toks) - n_prefix  # prefix rows reused
+    assert a == b == golden["mm_gen"].tolist()
+    assert float(np.abs(la - lb).max()) <= 1e-4
+    # a different prefix misses; turning the cache off prefills everything
+    other = toks.copy()
+    other[0] = (int(other[0]) + 1) % 1024
+    e.generate_vision(other, max_new_tokens=2, **args)
+    assert e.last_timing.prefill_tokens == len(toks)
+    e.use_prefix_cache = False
+    e.generate_vision(other, max_new_tokens=2, **args)
+    assert e.last_timing.prefill_tokens == len(toks)
+    e.close()
