@@ -385,6 +385,66 @@ def oracle_model_from_file(path):
     return w, O.TextModel(w)
 
 
+GEMM_SHAPES = (("qkv", 4096, 2048), ("o", 2048, 2048), ("gate+up", 12288, 2048), ("down", 2048, 6144))
+
+
+def run_gemm(args):
+    """The prefill GEMMs alone (config 3 shapes, 1255 prompt rows): icua_gemm_f16 (the prefill
+    route: fp16 weights by TMA) per layer matrix, back to back in a CUDA graph; TFLOP/s against
+    the measured bf16 GEMM peak."""
+    import ctypes as C
+
+    import torch
+
+    from instantcua_b200 import _lib as L
+
+    torch.cuda.set_device(0)
+    m = N_VIS + N_TEXT - 1
+    peaks_d = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    tpk = float(peaks_d.get("bf16_tflops", 1590.0))
+    rows = []
+    reps = max(args.steps, 10)
+    for name, n, k in GEMM_SHAPES:
+        w = (torch.randn(n, k, device="cuda") * 0.02).half()
+        x = torch.randn(m, k, device="cuda").half()
+        y = torch.empty(m, n, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+        def run():
+            s = torch.cuda.current_stream()
+            L.check(L.lib().icua_gemm_f16(n, k, m, C.c_void_p(w.data_ptr()), C.c_void_p(x.data_ptr()),
+                                          C.c_void_p(y.data_ptr()), C.c_void_p(err.data_ptr()),
+                                          C.c_void_p(s.cuda_stream)))
+
+        side = torch.cuda.Stream()
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                run()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(reps):
+                run()
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / reps
+        tf = 2.0 * m * n * k / (us * 1e-6) / 1e12
+        assert int(err.item()) == 0
+        rows.append({"gemm": name, "m": m, "n": n, "k": k, "us": round(us, 2), "TFLOP/s": round(tf, 1),
+                     "frac": round(tf / tpk, 4)})
+    tot_f = sum(2.0 * r["m"] * r["n"] * r["k"] for r in rows)
+    tot_us = sum(r["us"] for r in rows)
+    print(json.dumps({"metric": "prefill GEMM TFLOP/s (config 3 shapes, fp16 operands)",
+                      "value": round(tot_f / (tot_us * 1e-6) / 1e12, 1), "unit": "TFLOP/s", "n_gpus": 1,
+                      "steps": reps, "peak": tpk, "peak_kind": "measured burst bf16", "shapes": rows}))
+
+
 N_VIS, LLM_H, LLM_W, N_TEXT, PREFILL_DECODE = 1000, 25, 40, 256, 32
 LAYER_PARAMS = {"qkv": 4096 * 2048, "o": 2048 * 2048, "gu": 12288 * 2048, "d": 2048 * 6144}
 
@@ -567,8 +627,9 @@ def main():
     ap.add_argument("--micro-shape", default="", help="run only the microbench shapes whose name contains this")
     ap.add_argument("--prefill", action="store_true", help="config 3: multimodal prefill through the GEMM path")
     ap.add_argument("--batched", action="store_true", help="config 4: 64 sessions decoded together")
+    ap.add_argument("--gemm", action="store_true", help="the prefill GEMMs alone (config 3 shapes)")
     args = ap.parse_args()
-    if args.warmup < 3 and not (args.prefill or args.batched or args.micro):
+    if args.warmup < 3 and not (args.prefill or args.batched or args.micro or args.gemm):
         args.warmup = 3  # the headline bench always warms up; the side modes allow short profiling runs
     if args.impl == "reference":
         run_reference(args)
@@ -578,6 +639,8 @@ def main():
         run_prefill(args)
     elif args.batched:
         run_batched(args)
+    elif args.gemm:
+        run_gemm(args)
     else:
         run_ours(args)
 

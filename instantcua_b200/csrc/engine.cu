@@ -188,9 +188,18 @@ void setup_matrix(Matrix& m, int fmt, int n_rows, int k, int n_sm) {
     const int nw = fmt_slices(fmt), ku = k / 64 / nw;
     m.stream = fmt == FMT_Q8 || tpc > SMALL_MAX_TILES;  // q8 kernels are built for the streaming path only
     m.chunk = m.stream ? 1 : tpc;
-    // streaming ring depth: the q8 lm_head (330 MB, one launch) keeps 4 tiles per warp in flight,
-    // ~140 KB per SM, enough to cover HBM latency at full bandwidth
-    m.n_slots = !m.stream ? 1 : (fmt == FMT_Q8 ? 4 : 2);
+    // streaming ring depth: up to 4 tiles per warp in flight (~140 KB per SM for the q8 lm_head,
+    // enough to cover HBM latency at full bandwidth), as many as fit next to the input vector and
+    // the RMSNorm weights
+    m.n_slots = 1;
+    for (int ns : {4, 2, 1}) {
+        if (!m.stream && ns > 1) continue;
+        GemvSmem L{k, nw, ns, m.chunk, unit_bytes(fmt), ku, tpc, 0};
+        if ((size_t)L.total() + (size_t)k * 4 <= 216 * 1024) {
+            m.n_slots = ns;
+            break;
+        }
+    }
     GemvSmem L{k, nw, m.n_slots, m.chunk, unit_bytes(fmt), ku, tpc, 0};
     m.smem = (size_t)L.total();  // without the RMSNorm weight copy; launch_gemv adds it
 }
@@ -349,17 +358,20 @@ constexpr int SPLITK_MAX_ROWS = 128;  // split K only for batches of up to this 
 // split over up to 8 CTA slices whose partial products a finish kernel sums in slice order
 // (deterministic) before the epilogue.
 template <int EPI>
-cudaError_t batch_gemm(icua_engine* e, const void* x, TcGemmParams p, cudaStream_t s) {
+cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmParams p, cudaStream_t s) {
+    const bool q8 = m.fmt == FMT_Q8;
     const TcTile t = choose_tc_tile(p.n_rows, p.m_tok, e->n_sm, true);
     const int tiles = (p.n_rows / (TC_BM * t.mh)) * ((p.m_tok + t.bn - 1) / t.bn);
     int ks = std::min(SPLITK_MAX, e->n_sm / std::max(tiles, 1));
     ks = std::min(ks, p.k / TC_BK / 4);  // at least four k-blocks per slice
-    if (ks < 2 || p.m_tok > SPLITK_MAX_ROWS) return launch_tc_gemm<EPI>(x, e->cfg.max_pass, p, s);
+    if (ks < 2 || p.m_tok > SPLITK_MAX_ROWS)
+        return q8 ? launch_tc_gemm<EPI, FMT_Q8>(x, e->cfg.max_pass, p, s) : launch_tc_gemm<EPI>(x, e->cfg.max_pass, p, s);
     TcGemmParams q = p;
     q.out = e->splitk_part;
     q.ldo = p.n_rows;
     q.out_zstride = (long long)p.m_tok * p.n_rows;
-    cudaError_t err = launch_tc_gemm<TC_STORE>(x, e->cfg.max_pass, q, s, nullptr, ks);
+    cudaError_t err = q8 ? launch_tc_gemm<TC_STORE, FMT_Q8>(x, e->cfg.max_pass, q, s, nullptr, ks)
+                         : launch_tc_gemm<TC_STORE>(x, e->cfg.max_pass, q, s, nullptr, ks);
     if (err != cudaSuccess) return err;
     const long long total = (long long)p.m_tok * p.n_rows;
     const int grid = (int)std::min<long long>((total + 255) / 256, 4LL * e->n_sm);
@@ -370,6 +382,8 @@ cudaError_t batch_gemm(icua_engine* e, const void* x, TcGemmParams p, cudaStream
 cudaError_t launch_dequant_f16(const Matrix& m, __half* out, int n_sm, cudaStream_t s) {
     const long long n8 = (long long)m.n_rows * (m.k / 8);
     const int grid = (int)std::min<long long>((n8 + 255) / 256, 8LL * n_sm);
+    if (m.fmt == FMT_Q8)
+        return launch(dequant_q8_f16_kernel, grid, 256, 0, s, false, (const uint8_t*)m.dev, m.n_rows, m.k, out);
     return launch(dequant_q4s_f16_kernel, grid, 256, 0, s, false, (const uint8_t*)m.dev, m.n_rows, m.k, out);
 }
 
@@ -397,6 +411,10 @@ cudaError_t set_smem_attrs() {
     SETA((gemv_kernel<FMT_Q4S, EPI_STORE, 6144, false, IN_BF16>));
     SETA((gemv_kernel<FMT_Q8, EPI_STORE, 2048, true, IN_F32>));
     SETA((gemv_kernel<FMT_Q8, EPI_STORE, 2048, true, IN_BF16>));
+    SETA((gemv_kernel<FMT_Q8, EPI_STORE, 2048, true, IN_EMBED>));
+    SETA((gemv_kernel<FMT_Q8, EPI_RESID, 2048, true, IN_ATTN>));
+    SETA((gemv_kernel<FMT_Q8, EPI_SWIGLU, 2048, true, IN_F32>));
+    SETA((gemv_kernel<FMT_Q8, EPI_RESID, 6144, true, IN_F32>));
     SETA((attn_decode_kernel<__half>));
     SETA((attn_decode_kernel<__nv_bfloat16>));
     SETA(commit_kernel);
@@ -410,7 +428,10 @@ cudaError_t set_smem_attrs() {
           (const void*)tc_gemm_kernel<TC_ARGMAX, FMT_Q8, 1>, (const void*)tc_gemm_kernel<TC_STORE, FMT_F16, 1>,
           (const void*)tc_gemm_kernel<TC_RESID, FMT_F16, 1>, (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_F16, 1>,
           (const void*)tc_gemm_kernel<TC_STORE, FMT_F16, 2>, (const void*)tc_gemm_kernel<TC_RESID, FMT_F16, 2>,
-          (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_F16, 2>}) {
+          (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_F16, 2>, (const void*)tc_gemm_kernel<TC_STORE, FMT_Q8, 1>,
+          (const void*)tc_gemm_kernel<TC_RESID, FMT_Q8, 1>, (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q8, 1>,
+          (const void*)tc_gemm_kernel<TC_STORE, FMT_Q8, 2>, (const void*)tc_gemm_kernel<TC_RESID, FMT_Q8, 2>,
+          (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q8, 2>}) {
         if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)) != cudaSuccess)
             return e;
     }
@@ -458,6 +479,14 @@ L2Plan plan_kv(icua_engine* e, Session& S, int layer) {
     return pl;
 }
 
+// Layer GEMV launch for the engine's weight format: q4s matrices run the whole-tile path, q8
+// matrices (reference FMT 1 files) the streaming path.
+template <int EPI, int KMAX, int IN>
+cudaError_t launch_layer_gemv(const icua_engine* e, const Matrix& m, const GemvParams& p, cudaStream_t s) {
+    if (m.fmt == FMT_Q8) return launch_gemv<FMT_Q8, EPI, KMAX, true, IN>(m, p, s);
+    return launch_gemv<FMT_Q4S, EPI, KMAX, false, IN>(m, p, s);
+}
+
 cudaError_t record_layers(icua_engine* e, Session& S) {
     cudaError_t err;
     const int L = e->cfg.n_layers;
@@ -475,8 +504,8 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.out = e->qkv;
         p.st = S.st;
         p.l2 = plan_weights(ly.o);
-        err = (l == 0) ? launch_gemv<FMT_Q4S, EPI_STORE, 2048, false, IN_EMBED>(ly.qkv, p, e->stream)
-                       : launch_gemv<FMT_Q4S, EPI_STORE, 2048, false, IN_F32>(ly.qkv, p, e->stream);
+        err = (l == 0) ? launch_layer_gemv<EPI_STORE, 2048, IN_EMBED>(e, ly.qkv, p, e->stream)
+                       : launch_layer_gemv<EPI_STORE, 2048, IN_F32>(e, ly.qkv, p, e->stream);
         if (err != cudaSuccess) return err;
         // 2. QK norm + RoPE + KV append + split-K attention (clusters combine the splits)
         const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
@@ -522,7 +551,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.x_resid = e->x;
         p.st = S.st;
         p.l2 = plan_weights(ly.d);
-        if ((err = launch_gemv<FMT_Q4S, EPI_RESID, 2048, false, IN_ATTN>(ly.o, p, e->stream)) != cudaSuccess) return err;
+        if ((err = launch_layer_gemv<EPI_RESID, 2048, IN_ATTN>(e, ly.o, p, e->stream)) != cudaSuccess) return err;
         // 4. RMSNorm + gate/up + SwiGLU
         p = base_params(e, ly.gu);
         p.in_mode = IN_F32;
@@ -531,7 +560,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.out = e->h;
         p.st = S.st;
         if (l + 1 < L) p.l2 = plan_weights(e->layers[l + 1].qkv);
-        if ((err = launch_gemv<FMT_Q4S, EPI_SWIGLU, 2048, false, IN_F32>(ly.gu, p, e->stream)) != cudaSuccess) return err;
+        if ((err = launch_layer_gemv<EPI_SWIGLU, 2048, IN_F32>(e, ly.gu, p, e->stream)) != cudaSuccess) return err;
         // 5. down + residual (+ DeepStack rows after layers 0..2 while prefilling visual rows)
         p = base_params(e, ly.d);
         p.in_mode = IN_F32;
@@ -540,7 +569,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.deepstack = (l < 3) ? e->deepstack[l] : nullptr;
         p.st = S.st;
         p.l2 = (l + 1 < L) ? plan_kv(e, S, l + 1) : plan_weights(e->embed);
-        if ((err = launch_gemv<FMT_Q4S, EPI_RESID, 6144, false, IN_F32>(ly.d, p, e->stream)) != cudaSuccess) return err;
+        if ((err = launch_layer_gemv<EPI_RESID, 6144, IN_F32>(e, ly.d, p, e->stream)) != cudaSuccess) return err;
     }
     return cudaSuccess;
 }
@@ -721,7 +750,7 @@ icua_status try_finalize(icua_engine* eng) {
     CK(cudaSetDevice(eng->cfg.device));
     icua_status s;
     auto& st = eng->staged;
-    const int fmt = FMT_Q4S;
+    const int fmt = eng->cfg.format == ICUA_FMT_Q8 ? FMT_Q8 : FMT_Q4S;  // decoder layers; the embedding is q8
     if ((s = upload_matrix(eng, eng->embed, FMT_Q8, eng->cfg.vocab, H, st[ICUA_TID_EMBED], st[ICUA_TID_EMBED_SB],
                            nullptr)) != ICUA_OK)
         return s;
@@ -881,7 +910,7 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
         TcGemmParams p = tc_params(ly.qkv, n_rows, e->gemm_err);
         p.out = e->pqkv;
         p.ldo = QKV_ROWS;
-        if ((err = batch_gemm<TC_STORE>(e, e->pxn, p, st)) != cudaSuccess) return err;
+        if ((err = batch_gemm<TC_STORE>(e, ly.qkv, e->pxn, p, st)) != cudaSuccess) return err;
         {
             AttnParams<KVT> a{};
             a.qkv = e->pqkv;
@@ -919,18 +948,18 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
         p = tc_params(ly.o, n_rows, e->gemm_err);
         p.out = e->px;
         p.ldo = H;
-        if ((err = batch_gemm<TC_RESID>(e, e->pattn, p, st)) != cudaSuccess) return err;
+        if ((err = batch_gemm<TC_RESID>(e, ly.o, e->pattn, p, st)) != cudaSuccess) return err;
         if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
                           (const float*)ly.mlp_norm, n_rows, e->pxn)) != cudaSuccess)
             return err;
         p = tc_params(ly.gu, n_rows, e->gemm_err);
         p.out_h = e->ph;
         p.ldh = FF;
-        if ((err = batch_gemm<TC_SWIGLU>(e, e->pxn, p, st)) != cudaSuccess) return err;
+        if ((err = batch_gemm<TC_SWIGLU>(e, ly.gu, e->pxn, p, st)) != cudaSuccess) return err;
         p = tc_params(ly.d, n_rows, e->gemm_err);
         p.out = e->px;
         p.ldo = H;
-        if ((err = batch_gemm<TC_RESID>(e, e->ph, p, st)) != cudaSuccess) return err;
+        if ((err = batch_gemm<TC_RESID>(e, ly.d, e->ph, p, st)) != cudaSuccess) return err;
     }
     if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
                       (const float*)e->final_norm, n_rows, e->pxn)) != cudaSuccess)
@@ -999,7 +1028,7 @@ void icua_default_config(icua_config* c) {
 icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
     if (!cfg || !out) return fail(nullptr, ICUA_ERR_INVALID, "null argument");
     *out = nullptr;
-    if (cfg->format != ICUA_FMT_Q4S)
+    if (cfg->format != ICUA_FMT_Q4S && cfg->format != ICUA_FMT_Q8)
         return fail(nullptr, ICUA_ERR_UNSUPPORTED, "weight format %d is not implemented by the kernels", cfg->format);
     if (cfg->n_layers < 1 || cfg->n_layers > 28 || cfg->vocab < 16 || cfg->vocab % 16 || cfg->max_context < 2 ||
         cfg->max_pass < 1 || cfg->max_steps < 1 || cfg->max_sessions < 1 || cfg->steps_per_graph < 1 ||

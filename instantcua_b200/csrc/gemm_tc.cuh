@@ -268,6 +268,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     const int nk_all = p.k / TC_BK;
     const int kb0 = (int)((long long)nk_all * blockIdx.z / gridDim.z);
     const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb0;
+    // CTAs that share an operand tile start at different k-blocks (rotation by the token-tile
+    // index), so they do not all request the same rows from L2 at the same moment
+    const int krot = (int)((blockIdx.x * 5u) % (unsigned)nk);
     constexpr uint32_t tmem_cols = MH == 2 ? 512 : 256;
     constexpr int half_cols = 256;  // column offset of the second accumulator
 
@@ -306,18 +309,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                     mbar_expect_tx(&bfull[s], (uint32_t)(SM.a_bytes + SM.b_bytes));
 #pragma unroll
                     for (int h = 0; h < MH; ++h)
-                        tma_load_2d(smem + SM.a_off + s * SM.a_bytes + h * TC_BM * 128, &wmap, (kb0 + kc) * TC_BK,
-                                    row0 + h * TC_BM, &bfull[s]);
+                        tma_load_2d(smem + SM.a_off + s * SM.a_bytes + h * TC_BM * 128, &wmap,
+                                    (kb0 + (kc + krot) % nk) * TC_BK, row0 + h * TC_BM, &bfull[s]);
                 } else {
                     uint8_t* raw = smem + SM.raw_off + s * SM.raw_bytes;
                     mbar_expect_tx(&rawfull[s], NU * UB);
 #pragma unroll 1
                     for (int t = 0; t < NU; ++t)
-                        bulk_g2s(raw + t * UB, p.w + icua_layout::unit_offset(FMT, p.n_tiles, p.upt, tile0 + t, kb0 + kc),
+                        bulk_g2s(raw + t * UB,
+                                 p.w + icua_layout::unit_offset(FMT, p.n_tiles, p.upt, tile0 + t, kb0 + (kc + krot) % nk),
                                  UB, &rawfull[s]);
                     mbar_expect_tx(&bfull[s], (uint32_t)SM.b_bytes);
                 }
-                tma_load_2d(smem + SM.b_off + s * SM.b_bytes, &xmap, (kb0 + kc) * TC_BK, tok0, &bfull[s]);
+                tma_load_2d(smem + SM.b_off + s * SM.b_bytes, &xmap, (kb0 + (kc + krot) % nk) * TC_BK, tok0, &bfull[s]);
             }
             // the copies of the last stages complete before the CTA may exit (at once on success)
             for (int c = (kc > S ? kc - S : 0); c < kc; ++c) {
@@ -486,6 +490,31 @@ __global__ void __launch_bounds__(256) dequant_q4s_f16_kernel(const uint8_t* til
             const int sh = hi8 * 8 + up * 4;
             const float a = sf * (float)((int)((w >> sh) & 0xF) - 8);
             const float b = sf * (float)((int)((w >> (16 + sh)) & 0xF) - 8);
+            const __half2 hv = __floats2half2_rn(a, b);
+            o[t] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+        *reinterpret_cast<uint4*>(out + (size_t)row * K + (size_t)j8 * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// q8 counterpart of dequant_q4s_f16_kernel (reference FMT 1 weights): one rounding of
+// float(scale) * q, q = u - 128 from the offset-binary byte.
+__global__ void __launch_bounds__(256) dequant_q8_f16_kernel(const uint8_t* tiles, int n_rows, int K, __half* out) {
+    const long long n8 = (long long)n_rows * (K / 8);
+    const int n_tiles = n_rows / 16, upt = K / 64;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+        const int row = (int)(i / (K / 8)), j8 = (int)(i % (K / 8));
+        const uint8_t* ub = tiles + icua_layout::unit_offset(FMT_Q8, n_tiles, upt, row >> 4, j8 >> 3);
+        const int rt = row & 15, g = rt & 7, up = rt >> 3;
+        const int j = j8 & 7, step = j >> 1, hi8 = j & 1;
+        const float sf = __half2float(*reinterpret_cast<const __half*>(ub + 1024 + g * 8 + (step >> 1) * 4 + up * 2));
+        uint32_t o[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(ub + (step >> 1) * 512 + (g * 4 + t) * 16 +
+                                                                  (step & 1) * 8 + hi8 * 4);
+            const float a = sf * (float)((int)((w >> (8 * up)) & 0xFF) - 128);
+            const float b = sf * (float)((int)((w >> (16 + 8 * up)) & 0xFF) - 128);
             const __half2 hv = __floats2half2_rn(a, b);
             o[t] = *reinterpret_cast<const uint32_t*>(&hv);
         }

@@ -422,14 +422,16 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
     }
     int write_logits = (p.logits != nullptr && p.st == nullptr) ? 1 : 0, step = 0;
     float ds = 0.f;
+    int ds_vi = -1;  // DeepStack row of this prompt row (visual rows of layers 0..2), or -1
     if (p.st != nullptr && (EPI == EPI_LOGITS || (EPI == EPI_RESID && p.deepstack != nullptr))) {
         const DevState* st = p.st;
         write_logits = st->write_logits;
         step = st->step;
-        if (EPI == EPI_RESID && !STREAM && (int)threadIdx.x < nt * 16) {
+        if (EPI == EPI_RESID) {
             const int vi = st->prompt_idx - st->vis_offset;
-            if (st->prompt_idx < st->prompt_len && st->vis_offset >= 0 && vi >= 0 && vi < st->n_vis)
-                ds = p.deepstack[(long long)vi * H + t_begin * 16 + threadIdx.x];
+            if (st->prompt_idx < st->prompt_len && st->vis_offset >= 0 && vi >= 0 && vi < st->n_vis) ds_vi = vi;
+            if (!STREAM && ds_vi >= 0 && (int)threadIdx.x < nt * 16)
+                ds = p.deepstack[(long long)ds_vi * H + t_begin * 16 + threadIdx.x];
         }
     }
     store_input<KMAX, NT>(in, p, smem, L, nbar);  // ends with __syncthreads (also publishes cnt[] = 0)
@@ -524,12 +526,22 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
                 prev = __shfl_sync(0xffffffffu, prev, 0);
                 if (prev == NW - 1) {  // this warp completed the tile: reduce the K slices in a fixed order
                     __threadfence_block();
-                    if (lane < 16) {
-                        float v = 0.f;
+                    const int r = lane & 15;
+                    float v = 0.f;
 #pragma unroll
-                        for (int w2 = 0; w2 < NW; ++w2) v += *(volatile float*)&part[(j * NW + w2) * 16 + lane];
-                        gemv_row_epilogue<EPI>(p, (t_begin + j) * 16 + lane, v, 0.f, 0.f, write_logits, step, best_v,
-                                               best_i);
+                    for (int w2 = 0; w2 < NW; ++w2) v += *(volatile float*)&part[(j * NW + w2) * 16 + r];
+                    if (EPI == EPI_SWIGLU) {
+                        // tile rows 0..7 are gate units, rows 8..15 the matching up units
+                        const float uv = __shfl_down_sync(0xffffffffu, v, 8);
+                        if (lane < 8) p.out[(t_begin + j) * 8 + lane] = (v / (1.0f + expf(-v))) * uv;
+                    } else if (lane < 16) {
+                        const int row = (t_begin + j) * 16 + r;
+                        float xo = 0.f, dsv = 0.f;
+                        if (EPI == EPI_RESID) {
+                            xo = p.x_resid[row];
+                            if (ds_vi >= 0) dsv = p.deepstack[(long long)ds_vi * H + row];
+                        }
+                        gemv_row_epilogue<EPI>(p, row, v, xo, dsv, write_logits, step, best_v, best_i);
                     }
                 }
             }

@@ -34,7 +34,7 @@ class Engine:
     def __init__(self, model_path: str | None = None, tensors: dict | None = None, *, max_context: int = 2048,
                  max_pass: int = 512, max_steps: int = 256, n_layers: int = 28, vocab: int = 151936,
                  max_sessions: int = 1, kv_dtype: str = "f16", steps_per_graph: int = 8, device: int = 0,
-                 prefill_gemm_min: int | None = None):
+                 prefill_gemm_min: int | None = None, weight_format: str = "q4s"):
         self._lib = L.lib()
         cfg = L.IcuaConfig()
         self._lib.icua_default_config(C.byref(cfg))
@@ -45,7 +45,7 @@ class Engine:
         cfg.max_pass = max_pass
         cfg.max_steps = max_steps
         cfg.max_sessions = max_sessions
-        cfg.format = L.FMT_Q4S
+        cfg.format = {"q4s": L.FMT_Q4S, "q8": L.FMT_Q8}[weight_format]
         cfg.kv_dtype = {"f16": L.KV_F16, "bf16": L.KV_BF16}[kv_dtype]
         cfg.steps_per_graph = steps_per_graph
         if prefill_gemm_min is not None:
