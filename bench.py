@@ -345,12 +345,14 @@ def cpu_baseline(path, steps: int = 3):
     kc = [rng.standard_normal((sample_ctx, 8, 128), dtype=np.float32) for _ in range(NL)]
     vc = [rng.standard_normal((sample_ctx, 8, 128), dtype=np.float32) for _ in range(NL)]
     model.inject_kv(kc, vc)
-    model.decode_step(1)  # warm-up
-    t1 = time.perf_counter()
-    for i in range(steps):
-        model.decode_step(100 + i)
-    dt = time.perf_counter() - t1
-    return {"value": round(steps / dt, 4), "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)), "kind": "port",
+    limiter, cores = host_blas_threads()
+    with limiter:
+        model.decode_step(1)  # warm-up
+        t1 = time.perf_counter()
+        for i in range(steps):
+            model.decode_step(100 + i)
+        dt = time.perf_counter() - t1
+    return {"value": round(steps / dt, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
             "sample": f"{steps} decode tokens at context {sample_ctx}, numpy fp32 oracle on dequantized weights "
                       f"(setup {t1 - t0:.0f}s untimed)"}
 
@@ -577,6 +579,14 @@ def run_batched(args):
     }))
 
 
+def host_blas_threads():
+    """All host cores for the numpy oracle's BLAS, whatever OMP_NUM_THREADS torchrun exported."""
+    from threadpoolctl import threadpool_limits
+
+    cores = len(os.sched_getaffinity(0))
+    return threadpool_limits(limits=cores), cores
+
+
 def run_reference(args):
     """The reference's own CPU path (the numpy port of tools/reference/qwen3vl_ref.py): each step
     decodes one token at 4K context through a 4-of-28-layer sample plus 1/7 of the lm_head rows,
@@ -595,14 +605,15 @@ def run_reference(args):
     kc = [rng.standard_normal((CTX, 8, 128), dtype=np.float32) for _ in range(n_layers)]
     vc = [rng.standard_normal((CTX, 8, 128), dtype=np.float32) for _ in range(n_layers)]
     model.inject_kv(kc, vc)
-    for i in range(args.warmup):
-        model.decode_step(i)
-    t0 = time.perf_counter()
-    for i in range(args.steps):
-        model.decode_step(i)
-    dt = time.perf_counter() - t0
+    limiter, cores = host_blas_threads()
+    with limiter:
+        for i in range(args.warmup):
+            model.decode_step(i)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            model.decode_step(i)
+        dt = time.perf_counter() - t0
     tok_s = args.steps / 7 / dt
-    cores = len(os.sched_getaffinity(0))
     sample = (f"each step: 1 decode token through 4 of 28 layers + 1/7 of the lm_head rows at context {CTX}; "
               f"7 steps = 1 token; numpy fp32 oracle, BLAS on {cores} threads")
     print(json.dumps({

@@ -923,10 +923,12 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
             a.vc = reinterpret_cast<KVT*>(e->vc_all) + kv_layer * l;
             a.sess_kv_elems = (long long)e->kv_elems;
             a.max_ctx = e->cfg.max_context;
-            // one cluster per (row, kv head): one part, normalised in place.  With enough rows to
-            // fill the GPU twice over, one CTA per (row, kv head) streams the whole context.
-            a.n_split = (n_rows * NKV >= 2 * e->n_sm) ? 1 : e->att_cluster;
-            a.cluster = a.n_split;
+            // one cluster per (row, kv head): one part, normalised in place.  The cluster size is
+            // the smallest that gives about six waves of CTAs (short tail), up to the decode's.
+            int cl = 1;
+            while (cl < e->att_cluster && n_rows * NKV * cl < 6 * e->n_sm) cl *= 2;
+            a.n_split = cl;
+            a.cluster = cl;
             a.part = e->att_part;
             a.st = e->st_all;
             a.rows_sess = e->batch_rows;

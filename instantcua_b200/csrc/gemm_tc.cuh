@@ -157,7 +157,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 2-D TMA tile load (no multicast).  x (the contiguous dimension) is a multiple of 64 elements.
+// 2-D TMA tile load into this CTA's shared memory.  x (the contiguous dimension) is a multiple of 64 elements.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::

@@ -25,7 +25,7 @@ def tensors(require_gpu):
 
 
 def make_engine(tensors, kv="f16", sessions=4, **kw):
-    args = dict(n_layers=2, vocab=1024, max_context=512, max_pass=64, max_steps=64, kv_dtype=kv, steps_per_graph=4,
+    args = dict(n_layers=2, vocab=1024, max_context=256, max_pass=64, max_steps=64, kv_dtype=kv, steps_per_graph=4,
                 max_sessions=sessions)
     args.update(kw)
     e = Engine(tensors=tensors, **args)
@@ -38,13 +38,14 @@ def prompts(n, seed=5):
     return [rng.integers(0, 1024, int(rng.integers(5, 40))).astype(np.int32) for _ in range(n)]
 
 
-@pytest.mark.parametrize("kv", ["f16", "bf16"])
-def test_batch_matches_one_at_a_time(tensors, kv):
-    n, steps = 4, 6
+@pytest.mark.parametrize("kv,n", [("f16", 4), ("bf16", 4), ("bf16", 56)])
+def test_batch_matches_one_at_a_time(tensors, kv, n):
+    """4 rows run the attention in clusters of 4 CTAs per (row, head), 56 rows in clusters of 2."""
+    steps = 6
     ps = prompts(n)
     # batched: sessions in a shuffled order
-    order = [2, 0, 3, 1]
-    e = make_engine(tensors, kv)
+    order = [int(v) for v in np.random.default_rng(n).permutation(n)]
+    e = make_engine(tensors, kv, sessions=n)
     for s in range(n):
         e.prefill(ps[s], session=s)
     cap = e.capture_batch_logits(n)
@@ -52,7 +53,7 @@ def test_batch_matches_one_at_a_time(tensors, kv):
     got_logits = cap.copy()
     e.close()
     # one session at a time through the batch-1 decode
-    e = make_engine(tensors, kv)
+    e = make_engine(tensors, kv, sessions=n)
     want, want_logits = [], []
     for s in order:
         e.prefill(ps[s], session=s)
