@@ -187,7 +187,8 @@ icua_status icua_get_timing(icua_engine* eng, icua_timing* out);
 icua_status icua_session_position(icua_engine* eng, int32_t session, int32_t* pos);
 
 /* ---- kernel-level entry points (device pointers; used by the microbench and the tests) -------- */
-/* Packed device size of an [n_rows, k] matrix in format fmt (ICUA_FMT_Q4S or ICUA_FMT_Q8). */
+/* Packed device size of an [n_rows, k] matrix in format fmt (ICUA_FMT_Q4S, ICUA_FMT_Q8 or the
+ * reference's affine ICUA_FMT_Q4, whose "scales" are the (scale, bias) fp16 pairs per 64 columns). */
 uint64_t icua_packed_bytes(int32_t fmt, int32_t n_rows, int32_t k);
 /* Repacks reference-layout host codes + scales into the device tile layout (host to host). */
 icua_status icua_pack_matrix(int32_t fmt, int32_t n_rows, int32_t k, const void* codes,

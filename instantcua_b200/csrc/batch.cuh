@@ -15,11 +15,11 @@ namespace icua {
 
 // x[r] = embedding row of session rows_sess[r]'s current token.  One CTA per row.
 __global__ void batch_embed_kernel(const int* rows_sess, const DevState* st_all, const uint8_t* embed, int embed_tiles,
-                                   float* x) {
+                                   int embed_fmt, float* x) {
     const int r = blockIdx.x;
     const int tok = st_all[rows_sess[r]].cur_token;
     float* xr = x + (size_t)r * H;
-    for (int k = threadIdx.x; k < H; k += blockDim.x) xr[k] = q8_tile_value(embed, embed_tiles, H, tok, k);
+    for (int k = threadIdx.x; k < H; k += blockDim.x) xr[k] = embed_value(embed_fmt, embed, embed_tiles, tok, k);
 }
 
 // Reduces row r's lm_head partials (best value and vocabulary row per 128-row tile, lowest row on

@@ -23,10 +23,12 @@ constexpr float EPS = 1e-6f;
 constexpr int UNIT_K = 64;
 constexpr int Q4_UNIT_BYTES = 576;   // 512 B nibbles (32 lanes x 16 B) + 64 B scales
 constexpr int Q8_UNIT_BYTES = 1088;  // 1024 B bytes (32 lanes x 32 B) + 64 B scales
-enum Fmt { FMT_F16 = 0, FMT_Q8 = 1, FMT_Q4S = 3 };  // FMT_F16: weights already dequantised (row-major fp16)
+// FMT_F16: weights already dequantised (row-major fp16, the prefill GEMM operand);
+// FMT_Q4A: the reference's affine q4 (codes 0..15, fp16 scale and bias per 64 columns)
+enum Fmt { FMT_F16 = 0, FMT_Q8 = 1, FMT_Q4A = 2, FMT_Q4S = 3 };
 
 __host__ __device__ constexpr int unit_bytes(int fmt) {
-    return fmt == FMT_Q8 ? Q8_UNIT_BYTES : fmt == FMT_Q4S ? Q4_UNIT_BYTES : 0;
+    return fmt == FMT_Q8 ? Q8_UNIT_BYTES : (fmt == FMT_Q4S || fmt == FMT_Q4A) ? Q4_UNIT_BYTES : 0;
 }
 __host__ __device__ constexpr int unit_wbytes(int fmt) { return fmt == FMT_Q8 ? 1024 : 512; }
 

@@ -14,6 +14,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <chrono>
 #include <cmath>
 #include <cstdarg>
@@ -40,6 +41,7 @@ uint16_t f32_to_f16_bits(float f);
 float f16_bits_to_f32(uint16_t h);
 void pack_q4s(int n_rows, int k, const uint8_t* packed, const uint16_t* scales, const int* row_map, uint8_t* out);
 void pack_q8(int n_rows, int k, const int8_t* codes, const uint16_t* scales, const int* row_map, uint8_t* out);
+void pack_q4a(int n_rows, int k, const uint8_t* packed, const uint16_t* sb, const int* row_map, uint8_t* out);
 }  // namespace icua_host
 
 using namespace icua;
@@ -359,19 +361,22 @@ constexpr int SPLITK_MAX_ROWS = 128;  // split K only for batches of up to this 
 // (deterministic) before the epilogue.
 template <int EPI>
 cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmParams p, cudaStream_t s) {
-    const bool q8 = m.fmt == FMT_Q8;
     const TcTile t = choose_tc_tile(p.n_rows, p.m_tok, e->n_sm, true);
     const int tiles = (p.n_rows / (TC_BM * t.mh)) * ((p.m_tok + t.bn - 1) / t.bn);
     int ks = std::min(SPLITK_MAX, e->n_sm / std::max(tiles, 1));
     ks = std::min(ks, p.k / TC_BK / 4);  // at least four k-blocks per slice
-    if (ks < 2 || p.m_tok > SPLITK_MAX_ROWS)
-        return q8 ? launch_tc_gemm<EPI, FMT_Q8>(x, e->cfg.max_pass, p, s) : launch_tc_gemm<EPI>(x, e->cfg.max_pass, p, s);
+    auto run = [&](auto epi_tag, const TcGemmParams& q, int ksplit) -> cudaError_t {
+        constexpr int E = decltype(epi_tag)::value;
+        if (m.fmt == FMT_Q8) return launch_tc_gemm<E, FMT_Q8>(x, e->cfg.max_pass, q, s, nullptr, ksplit);
+        if (m.fmt == FMT_Q4A) return launch_tc_gemm<E, FMT_Q4A>(x, e->cfg.max_pass, q, s, nullptr, ksplit);
+        return launch_tc_gemm<E, FMT_Q4S>(x, e->cfg.max_pass, q, s, nullptr, ksplit);
+    };
+    if (ks < 2 || p.m_tok > SPLITK_MAX_ROWS) return run(std::integral_constant<int, EPI>{}, p, 1);
     TcGemmParams q = p;
     q.out = e->splitk_part;
     q.ldo = p.n_rows;
     q.out_zstride = (long long)p.m_tok * p.n_rows;
-    cudaError_t err = q8 ? launch_tc_gemm<TC_STORE, FMT_Q8>(x, e->cfg.max_pass, q, s, nullptr, ks)
-                         : launch_tc_gemm<TC_STORE>(x, e->cfg.max_pass, q, s, nullptr, ks);
+    cudaError_t err = run(std::integral_constant<int, TC_STORE>{}, q, ks);
     if (err != cudaSuccess) return err;
     const long long total = (long long)p.m_tok * p.n_rows;
     const int grid = (int)std::min<long long>((total + 255) / 256, 4LL * e->n_sm);
@@ -384,6 +389,8 @@ cudaError_t launch_dequant_f16(const Matrix& m, __half* out, int n_sm, cudaStrea
     const int grid = (int)std::min<long long>((n8 + 255) / 256, 8LL * n_sm);
     if (m.fmt == FMT_Q8)
         return launch(dequant_q8_f16_kernel, grid, 256, 0, s, false, (const uint8_t*)m.dev, m.n_rows, m.k, out);
+    if (m.fmt == FMT_Q4A)
+        return launch(dequant_q4a_f16_kernel, grid, 256, 0, s, false, (const uint8_t*)m.dev, m.n_rows, m.k, out);
     return launch(dequant_q4s_f16_kernel, grid, 256, 0, s, false, (const uint8_t*)m.dev, m.n_rows, m.k, out);
 }
 
@@ -415,6 +422,13 @@ cudaError_t set_smem_attrs() {
     SETA((gemv_kernel<FMT_Q8, EPI_RESID, 2048, true, IN_ATTN>));
     SETA((gemv_kernel<FMT_Q8, EPI_SWIGLU, 2048, true, IN_F32>));
     SETA((gemv_kernel<FMT_Q8, EPI_RESID, 6144, true, IN_F32>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_STORE, 2048, false, IN_EMBED>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_STORE, 2048, false, IN_F32>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_RESID, 2048, false, IN_ATTN>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_SWIGLU, 2048, false, IN_F32>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_RESID, 6144, false, IN_F32>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_LOGITS, 2048, true, IN_F32>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_LOGITS, 2048, false, IN_F32>));
     SETA((attn_decode_kernel<__half>));
     SETA((attn_decode_kernel<__nv_bfloat16>));
     SETA(commit_kernel);
@@ -431,7 +445,10 @@ cudaError_t set_smem_attrs() {
           (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_F16, 2>, (const void*)tc_gemm_kernel<TC_STORE, FMT_Q8, 1>,
           (const void*)tc_gemm_kernel<TC_RESID, FMT_Q8, 1>, (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q8, 1>,
           (const void*)tc_gemm_kernel<TC_STORE, FMT_Q8, 2>, (const void*)tc_gemm_kernel<TC_RESID, FMT_Q8, 2>,
-          (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q8, 2>}) {
+          (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q8, 2>, (const void*)tc_gemm_kernel<TC_STORE, FMT_Q4A, 1>,
+          (const void*)tc_gemm_kernel<TC_RESID, FMT_Q4A, 1>, (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q4A, 1>,
+          (const void*)tc_gemm_kernel<TC_STORE, FMT_Q4A, 2>, (const void*)tc_gemm_kernel<TC_RESID, FMT_Q4A, 2>,
+          (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q4A, 2>, (const void*)tc_gemm_kernel<TC_ARGMAX, FMT_Q4A, 1>}) {
         if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)) != cudaSuccess)
             return e;
     }
@@ -455,6 +472,7 @@ GemvParams base_params(icua_engine* e, const Matrix& m) {
     p.chunk = m.chunk;
     p.embed = e->embed.dev;
     p.embed_tiles = e->embed.n_tiles;
+    p.embed_fmt = e->embed.fmt;
     return p;
 }
 
@@ -484,6 +502,7 @@ L2Plan plan_kv(icua_engine* e, Session& S, int layer) {
 template <int EPI, int KMAX, int IN>
 cudaError_t launch_layer_gemv(const icua_engine* e, const Matrix& m, const GemvParams& p, cudaStream_t s) {
     if (m.fmt == FMT_Q8) return launch_gemv<FMT_Q8, EPI, KMAX, true, IN>(m, p, s);
+    if (m.fmt == FMT_Q4A) return launch_gemv<FMT_Q4A, EPI, KMAX, false, IN>(m, p, s);
     return launch_gemv<FMT_Q4S, EPI, KMAX, false, IN>(m, p, s);
 }
 
@@ -584,7 +603,10 @@ cudaError_t record_head(icua_engine* e, Session& S) {
     p.cta_best_i = e->cta_best_i;
     p.step_logits = e->step_logits;
     p.st = S.st;
-    cudaError_t err = launch_gemv<FMT_Q8, EPI_LOGITS, 2048, true, IN_F32>(e->embed, p, e->stream);
+    // q8 heads always stream; a q4a head streams unless the vocabulary is small (tests)
+    cudaError_t err = e->embed.fmt != FMT_Q4A ? launch_gemv<FMT_Q8, EPI_LOGITS, 2048, true, IN_F32>(e->embed, p, e->stream)
+                      : e->embed.stream       ? launch_gemv<FMT_Q4A, EPI_LOGITS, 2048, true, IN_F32>(e->embed, p, e->stream)
+                                              : launch_gemv<FMT_Q4A, EPI_LOGITS, 2048, false, IN_F32>(e->embed, p, e->stream);
     if (err != cudaSuccess) return err;
     return launch(commit_kernel, 1, 256, 0, e->stream, true, (const float*)e->cta_best_v, (const int*)e->cta_best_i,
                   e->embed.grid, S.out_tokens, S.st);
@@ -689,13 +711,18 @@ icua_status sync_and_check(icua_engine* eng, Session& S) {
 size_t expected_bytes(const icua_engine* e, int id) {
     const int fmt = e->cfg.format;
     const size_t V = (size_t)e->cfg.vocab;
-    if (id == ICUA_TID_EMBED) return V * H;            // q8 codes
-    if (id == ICUA_TID_EMBED_SB) return V * (H / 32) * 2;
+    // embedding: q8 codes + scales, except in reference q4 files (affine q4 like every matrix)
+    if (id == ICUA_TID_EMBED) return fmt == ICUA_FMT_Q4 ? V * H / 2 : V * H;
+    if (id == ICUA_TID_EMBED_SB) return fmt == ICUA_FMT_Q4 ? V * (H / 64) * 4 : V * (H / 32) * 2;
     if (id == ICUA_TID_FINAL_NORM) return H * 4;
     const int rel = id - ICUA_TID_LAYER_BASE;
     const int slot = rel % ICUA_TID_PER_LAYER;
-    auto mat = [&](int rows, int k) -> size_t { return fmt == ICUA_FMT_Q4S ? (size_t)rows * k / 2 : (size_t)rows * k; };
-    auto sb = [&](int rows, int k) -> size_t { return (size_t)rows * (k / 32) * 2; };
+    auto mat = [&](int rows, int k) -> size_t {
+        return (fmt == ICUA_FMT_Q4S || fmt == ICUA_FMT_Q4) ? (size_t)rows * k / 2 : (size_t)rows * k;
+    };
+    auto sb = [&](int rows, int k) -> size_t {
+        return fmt == ICUA_FMT_Q4 ? (size_t)rows * (k / 64) * 4 : (size_t)rows * (k / 32) * 2;  // half2 / half
+    };
     switch (slot) {
         case ICUA_SLOT_ATTN_NORM:
         case ICUA_SLOT_MLP_NORM: return H * 4;
@@ -734,6 +761,8 @@ icua_status upload_matrix(icua_engine* eng, Matrix& m, int fmt, int rows, int k,
     std::vector<uint8_t> packed(bytes);
     if (fmt == FMT_Q4S)
         icua_host::pack_q4s(rows, k, codes.data(), reinterpret_cast<const uint16_t*>(sb.data()), row_map, packed.data());
+    else if (fmt == FMT_Q4A)
+        icua_host::pack_q4a(rows, k, codes.data(), reinterpret_cast<const uint16_t*>(sb.data()), row_map, packed.data());
     else
         icua_host::pack_q8(rows, k, reinterpret_cast<const int8_t*>(codes.data()),
                            reinterpret_cast<const uint16_t*>(sb.data()), row_map, packed.data());
@@ -750,8 +779,10 @@ icua_status try_finalize(icua_engine* eng) {
     CK(cudaSetDevice(eng->cfg.device));
     icua_status s;
     auto& st = eng->staged;
-    const int fmt = eng->cfg.format == ICUA_FMT_Q8 ? FMT_Q8 : FMT_Q4S;  // decoder layers; the embedding is q8
-    if ((s = upload_matrix(eng, eng->embed, FMT_Q8, eng->cfg.vocab, H, st[ICUA_TID_EMBED], st[ICUA_TID_EMBED_SB],
+    // decoder layers in the file's format; the tied embedding is q8, or affine q4 in reference q4 files
+    const int fmt = eng->cfg.format == ICUA_FMT_Q8 ? FMT_Q8 : eng->cfg.format == ICUA_FMT_Q4 ? FMT_Q4A : FMT_Q4S;
+    const int efmt = eng->cfg.format == ICUA_FMT_Q4 ? FMT_Q4A : FMT_Q8;
+    if ((s = upload_matrix(eng, eng->embed, efmt, eng->cfg.vocab, H, st[ICUA_TID_EMBED], st[ICUA_TID_EMBED_SB],
                            nullptr)) != ICUA_OK)
         return s;
     if ((s = upload_f32(eng, &eng->final_norm, st[ICUA_TID_FINAL_NORM])) != ICUA_OK) return s;
@@ -796,7 +827,7 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
     const int L = e->cfg.n_layers, pos0 = S.pos;
     int* errp = &S.st->error;
     if ((err = launch(prefill_embed_kernel, n_rows, 256, 0, st, false, (const int*)S.prompt, n_rows, vis_off, n_vis,
-                      (const float*)e->pooler, (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->px)) != cudaSuccess)
+                      (const float*)e->pooler, (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->embed.fmt, e->px)) != cudaSuccess)
         return err;
     const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
     // The layer matrices in GEMM order (the last layer only projects K/V).  Matrix i is
@@ -899,7 +930,7 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
     cudaStream_t st = e->stream;
     const int L = e->cfg.n_layers;
     if ((err = launch(batch_embed_kernel, n_rows, 256, 0, st, false, (const int*)e->batch_rows,
-                      (const DevState*)e->st_all, (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->px)) != cudaSuccess)
+                      (const DevState*)e->st_all, (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->embed.fmt, e->px)) != cudaSuccess)
         return err;
     const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
     for (int l = 0; l < L; ++l) {
@@ -971,7 +1002,9 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
     p.best_i = e->batch_best_i;
     p.out = e->batch_logits;  // nullptr unless the logits of the step were requested
     p.ldo = e->cfg.vocab;
-    if ((err = launch_tc_gemm<TC_ARGMAX, FMT_Q8>(e->pxn, e->cfg.max_pass, p, st)) != cudaSuccess) return err;
+    err = e->embed.fmt == FMT_Q4A ? launch_tc_gemm<TC_ARGMAX, FMT_Q4A>(e->pxn, e->cfg.max_pass, p, st)
+                                  : launch_tc_gemm<TC_ARGMAX, FMT_Q8>(e->pxn, e->cfg.max_pass, p, st);
+    if (err != cudaSuccess) return err;
     return launch(batch_commit_kernel, n_rows, 256, 0, st, false, (const float*)e->batch_best_v,
                   (const int*)e->batch_best_i, e->cfg.vocab / TC_BM, n_rows, (const int*)e->batch_rows, e->st_all,
                   e->out_all, e->out_stride);
@@ -1030,7 +1063,7 @@ void icua_default_config(icua_config* c) {
 icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
     if (!cfg || !out) return fail(nullptr, ICUA_ERR_INVALID, "null argument");
     *out = nullptr;
-    if (cfg->format != ICUA_FMT_Q4S && cfg->format != ICUA_FMT_Q8)
+    if (cfg->format != ICUA_FMT_Q4S && cfg->format != ICUA_FMT_Q8 && cfg->format != ICUA_FMT_Q4)
         return fail(nullptr, ICUA_ERR_UNSUPPORTED, "weight format %d is not implemented by the kernels", cfg->format);
     if (cfg->n_layers < 1 || cfg->n_layers > 28 || cfg->vocab < 16 || cfg->vocab % 16 || cfg->max_context < 2 ||
         cfg->max_pass < 1 || cfg->max_steps < 1 || cfg->max_sessions < 1 || cfg->steps_per_graph < 1 ||

@@ -240,6 +240,40 @@ __device__ __forceinline__ void dequant_q8_lane(const uint8_t* unit, int l, uint
     }
 }
 
+// Reference affine q4 (codes 0..15, one fp16 (scale, bias) per row and 64-column unit):
+// fp16(1024 + u) - 1024 = u exactly, then one fused rounding of u * scale + bias.
+__device__ __forceinline__ void dequant_q4a_lane(const uint8_t* unit, int l, uint8_t* A, int row0) {
+    const uint4 nib = *reinterpret_cast<const uint4*>(unit + l * 16);
+    const int g = l >> 2, t = l & 3;
+    const uint2 sbw = *reinterpret_cast<const uint2*>(unit + 512 + g * 8);  // (scale, bias) rows g, g+8
+    const __half2 sba = *reinterpret_cast<const __half2*>(&sbw.x), sbb = *reinterpret_cast<const __half2*>(&sbw.y);
+    const __half2 sa = __half2half2(__low2half(sba)), ba = __half2half2(__high2half(sba));
+    const __half2 sb = __half2half2(__low2half(sbb)), bb = __half2half2(__high2half(sbb));
+    const __half2 base = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));  // 1024
+    const int ra = row0 + g, rb = ra + 8;
+    const uint32_t w[4] = {nib.x, nib.y, nib.z, nib.w};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const int k0 = 16 * s + 2 * t;
+        const uint32_t v = w[s];
+        uint32_t h[4];
+        h[0] = (v & 0x000F000Fu) | 0x64006400u;
+        h[1] = ((v >> 4) & 0x000F000Fu) | 0x64006400u;
+        h[2] = ((v >> 8) & 0x000F000Fu) | 0x64006400u;
+        h[3] = ((v >> 12) & 0x000F000Fu) | 0x64006400u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            __half2 x = __hsub2(*reinterpret_cast<__half2*>(&h[i]), base);
+            x = (i & 1) ? __hfma2(x, sb, bb) : __hfma2(x, sa, ba);
+            h[i] = *reinterpret_cast<uint32_t*>(&x);
+        }
+        *reinterpret_cast<uint32_t*>(A + sw128_off(ra, k0)) = h[0];
+        *reinterpret_cast<uint32_t*>(A + sw128_off(rb, k0)) = h[1];
+        *reinterpret_cast<uint32_t*>(A + sw128_off(ra, k0 + 8)) = h[2];
+        *reinterpret_cast<uint32_t*>(A + sw128_off(rb, k0 + 8)) = h[3];
+    }
+}
+
 template <int EPI, int FMT, int MH>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
                                                                 const __grid_constant__ CUtensorMap wmap,
@@ -371,6 +405,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                     dequant_q4s_lane(raw + t * UB, pi & 31, A, t * 16);
                 else if constexpr (FMT == FMT_Q8)
                     dequant_q8_lane(raw + t * UB, pi & 31, A, t * 16);
+                else if constexpr (FMT == FMT_Q4A)
+                    dequant_q4a_lane(raw + t * UB, pi & 31, A, t * 16);
             }
             fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
             __syncwarp();
@@ -516,6 +552,30 @@ __global__ void __launch_bounds__(256) dequant_q8_f16_kernel(const uint8_t* tile
             const float a = sf * (float)((int)((w >> (8 * up)) & 0xFF) - 128);
             const float b = sf * (float)((int)((w >> (16 + 8 * up)) & 0xFF) - 128);
             const __half2 hv = __floats2half2_rn(a, b);
+            o[t] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+        *reinterpret_cast<uint4*>(out + (size_t)row * K + (size_t)j8 * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// Affine q4 counterpart of dequant_q4s_f16_kernel: one rounding of scale * u + bias.
+__global__ void __launch_bounds__(256) dequant_q4a_f16_kernel(const uint8_t* tiles, int n_rows, int K, __half* out) {
+    const long long n8 = (long long)n_rows * (K / 8);
+    const int n_tiles = n_rows / 16, upt = K / 64;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+        const int row = (int)(i / (K / 8)), j8 = (int)(i % (K / 8));
+        const uint8_t* ub = tiles + icua_layout::unit_offset(FMT_Q4A, n_tiles, upt, row >> 4, j8 >> 3);
+        const int rt = row & 15, g = rt & 7, up = rt >> 3;
+        const int j = j8 & 7, step = j >> 1, hi8 = j & 1;
+        const __half2 sbh = *reinterpret_cast<const __half2*>(ub + 512 + g * 8 + up * 4);
+        const __half2 sc = __half2half2(__low2half(sbh)), bi = __half2half2(__high2half(sbh));
+        uint32_t o[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(ub + (g * 4 + t) * 16 + step * 4);
+            const int sh = hi8 * 8 + up * 4;
+            const __half2 u = __floats2half2_rn((float)((w >> sh) & 0xF), (float)((w >> (16 + sh)) & 0xF));
+            const __half2 hv = __hfma2(u, sc, bi);  // the fused path's single rounding of u * scale + bias
             o[t] = *reinterpret_cast<const uint32_t*>(&hv);
         }
         *reinterpret_cast<uint4*>(out + (size_t)row * K + (size_t)j8 * 8) = make_uint4(o[0], o[1], o[2], o[3]);

@@ -51,6 +51,7 @@ struct GemvParams {
     const float* norm_w;     // RMSNorm weight [k] or nullptr
     const uint8_t* embed;    // IN_EMBED: q8 packed embedding [vocab, 2048]
     int embed_tiles;         // IN_EMBED: vocab / 16
+    int embed_fmt;           // IN_EMBED: FMT_Q8 or FMT_Q4A
     const int* prompt;       // IN_EMBED: prompt tokens of the session
     const float* pooler;     // IN_EMBED: visual rows [n_vis, 2048] or nullptr
     const float* att_part;   // IN_ATTN: [NKV][att_parts][ATT_PART]
@@ -108,6 +109,24 @@ __device__ __forceinline__ float q4s_tile_value(const uint8_t* tiles, int n_tile
     const __half2 s2 = *reinterpret_cast<const __half2*>(ub + 512 + gq * 8 + (kin >> 5) * 4);
     const float s = up ? __high2float(s2) : __low2float(s2);
     return s * (float)(u - 8);
+}
+
+// fp32 value of element (row, k) of a q4a (reference affine q4) packed matrix: scale * u + bias
+// (Shaders.swift:471-476).
+__device__ __forceinline__ float q4a_tile_value(const uint8_t* tiles, int n_tiles, int K, int row, int k) {
+    const uint8_t* ub = tiles + unit_offset(FMT_Q4A, n_tiles, K / UNIT_K, row >> 4, k >> 6);
+    const int rt = row & 15, gq = rt & 7, up = rt >> 3;
+    const int kin = k & 63, step = kin >> 4, kk = kin & 15;
+    const int t = (kk & 7) >> 1, odd = kk & 1, hi8 = kk >> 3;
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(ub + (gq * 4 + t) * 16 + step * 4);
+    const int u = (w >> (odd * 16 + hi8 * 8 + up * 4)) & 0xF;
+    const float2 sb = __half22float2(*reinterpret_cast<const __half2*>(ub + 512 + gq * 8 + up * 4));
+    return fmaf(sb.x, (float)u, sb.y);
+}
+
+// Embedding row element for the engine's embedding format (q8, or q4a for reference q4 files).
+__device__ __forceinline__ float embed_value(int fmt, const uint8_t* tiles, int n_tiles, int row, int k) {
+    return fmt == FMT_Q4A ? q4a_tile_value(tiles, n_tiles, H, row, k) : q8_tile_value(tiles, n_tiles, H, row, k);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -187,7 +206,7 @@ __device__ __forceinline__ void load_input(InputRegs<KMAX, NT>& r, const GemvPar
             const int kk[4] = {k0, k0 + 1, k0 + 8, k0 + 9};
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-                r.v[j][i] = vis_row ? vis_row[kk[i]] : q8_tile_value(p.embed, p.embed_tiles, H, tok, kk[i]);
+                r.v[j][i] = vis_row ? vis_row[kk[i]] : embed_value(p.embed_fmt, p.embed, p.embed_tiles, tok, kk[i]);
         }
     }
 }
@@ -262,6 +281,7 @@ template <int FMT>
 struct UnitConst {
     uint32_t b[4][2];
     float c0[2], c1[2];
+    float xu24;  // q4a: sum of the unit's 64 inputs x 2^-24 (the bias term)
 };
 
 template <int FMT>
@@ -274,13 +294,16 @@ __device__ __forceinline__ void load_unit_const(UnitConst<FMT>& uc, int kk, cons
         uc.b[step][0] = b.x;
         uc.b[step][1] = b.y;
     }
-    const float off = (FMT == FMT_Q4S) ? 8.0f : 128.0f;
+    // q4s / q8 store offset-binary codes: the offset enters through the accumulator start; q4a
+    // codes are plain 0..15 and its bias multiplies the unit's input sum instead
+    const float off = (FMT == FMT_Q4S) ? 8.0f : (FMT == FMT_Q8) ? 128.0f : 0.0f;
 #pragma unroll
     for (int grp = 0; grp < 2; ++grp) {
         const float c = -off * xsum[kk * 2 + grp] * 5.9604644775390625e-08f;  // 2^-24
         uc.c0[grp] = c;
-        uc.c1[grp] = (FMT == FMT_Q4S) ? 16.0f * c : c;
+        uc.c1[grp] = (FMT != FMT_Q8) ? 16.0f * c : c;
     }
+    uc.xu24 = (xsum[kk * 2] + xsum[kk * 2 + 1]) * 5.9604644775390625e-08f;
 }
 
 __device__ __forceinline__ void mma_16816_c(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, float c0,
@@ -300,7 +323,7 @@ __device__ __forceinline__ void gemv_unit(const uint8_t* ub, const UnitConst<FMT
     const int g = lane >> 2;
     const uint2 sc = *reinterpret_cast<const uint2*>(ub + unit_wbytes(FMT) + g * 8);
     uint32_t wq[8];
-    if (FMT == FMT_Q4S) {
+    if (FMT != FMT_Q8) {
         const uint4 w = *reinterpret_cast<const uint4*>(ub + lane * 16);
         wq[0] = w.x; wq[1] = w.y; wq[2] = w.z; wq[3] = w.w;
     } else {
@@ -313,7 +336,7 @@ __device__ __forceinline__ void gemv_unit(const uint8_t* ub, const UnitConst<FMT
 #pragma unroll
     for (int step = 0; step < 4; ++step) {
         uint32_t a[4];
-        if (FMT == FMT_Q4S) {
+        if (FMT != FMT_Q8) {
             const uint32_t w = wq[step];
             a[0] = w & 0x000F000Fu;
             a[1] = w & 0x00F000F0u;
@@ -332,11 +355,21 @@ __device__ __forceinline__ void gemv_unit(const uint8_t* ub, const UnitConst<FMT
         else
             mma_16816(d[grp], a, uc.b[step][0], uc.b[step][1]);
     }
+    if (FMT == FMT_Q4A) {
+        // one 64-column group: (scale, bias) of row g in sc.x, of row g+8 in sc.y
+        const float2 sa = __half22float2(*reinterpret_cast<const __half2*>(&sc.x));
+        const float2 sb = __half22float2(*reinterpret_cast<const __half2*>(&sc.y));
+        acc0 = fmaf(sa.x, (d[0][0] + d[0][1]) + (d[1][0] + d[1][1]), acc0);
+        acc0 = fmaf(sa.y, uc.xu24, acc0);
+        acc1 = fmaf(sb.x, (d[0][2] + d[0][3]) + (d[1][2] + d[1][3]), acc1);
+        acc1 = fmaf(sb.y, 16.0f * uc.xu24, acc1);  // rows g+8 accumulate in units of 2^-20
+    } else {
 #pragma unroll
-    for (int grp = 0; grp < 2; ++grp) {
-        const float2 s = __half22float2(*reinterpret_cast<const __half2*>(grp == 0 ? &sc.x : &sc.y));
-        acc0 = fmaf(s.x, d[grp][0] + d[grp][1], acc0);
-        acc1 = fmaf(s.y, d[grp][2] + d[grp][3], acc1);
+        for (int grp = 0; grp < 2; ++grp) {
+            const float2 s = __half22float2(*reinterpret_cast<const __half2*>(grp == 0 ? &sc.x : &sc.y));
+            acc0 = fmaf(s.x, d[grp][0] + d[grp][1], acc0);
+            acc1 = fmaf(s.y, d[grp][2] + d[grp][3], acc1);
+        }
     }
 }
 
@@ -448,7 +481,7 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
             if (u < ku) load_unit_const<FMT>(uc[u], warp * ku + u, xfrag, xsum, lane);
     }
     const int g = lane >> 2, t = lane & 3;
-    const float f1 = (FMT == FMT_Q4S) ? 1048576.0f : 16777216.0f;
+    const float f1 = (FMT != FMT_Q8) ? 1048576.0f : 16777216.0f;
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
 

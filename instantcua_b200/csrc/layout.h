@@ -11,8 +11,10 @@
 
 namespace icua_layout {
 
-constexpr int FMT_Q8 = 1, FMT_Q4S = 3;
-constexpr int Q4_UNIT_BYTES = 576;   // 32 lanes x 16 B nibbles + 8 rows x 2 groups x (2 x fp16) scales
+constexpr int FMT_Q8 = 1, FMT_Q4A = 2, FMT_Q4S = 3;
+// q4s: 32 lanes x 16 B nibbles + 8 rows x 2 groups x (2 x fp16) scales;
+// q4a (reference affine q4, groups of 64): the same nibbles + 8 x (scale, bias) of rows g, g+8
+constexpr int Q4_UNIT_BYTES = 576;
 constexpr int Q8_UNIT_BYTES = 1088;  // 32 lanes x 32 B bytes + scales
 
 #if defined(__CUDACC__)
@@ -22,7 +24,7 @@ constexpr int Q8_UNIT_BYTES = 1088;  // 32 lanes x 32 B bytes + scales
 #endif
 
 ICUA_HD constexpr int unit_bytes(int fmt) { return fmt == FMT_Q8 ? Q8_UNIT_BYTES : Q4_UNIT_BYTES; }
-// K slices (= GEMV warps): q4s decode projections 16, the q8 embedding / lm_head 8.
+// K slices (= GEMV warps): q4 decode projections 16, q8 matrices 8.
 ICUA_HD constexpr int fmt_slices(int fmt) { return fmt == FMT_Q8 ? 8 : 16; }
 
 ICUA_HD inline long long unit_offset(int fmt, int n_tiles, int upt, int tile, int kk) {

@@ -143,6 +143,38 @@ void pack_q4s(int n_rows, int k, const uint8_t* packed, const uint16_t* scales, 
     });
 }
 
+// Reference affine q4 (Convert.swift:246-320): nibbles placed exactly as pack_q4s (codes 0..15,
+// no offset); the unit's 64 bytes hold, per lane group g, the fp16 (scale, bias) of rows g and g+8
+// for the unit's one 64-column group.  `sb` is the reference's half2 [rows][K / 64] array.
+void pack_q4a(int n_rows, int k, const uint8_t* packed, const uint16_t* sb, const int* row_map, uint8_t* out) {
+    const int upt = k / 64;
+    parallel_rows(n_rows / 16, [&](int tile) {
+        for (int kk = 0; kk < upt; ++kk) {
+            uint8_t* ub = out + icua_layout::unit_offset(icua_layout::FMT_Q4A, n_rows / 16, upt, tile, kk);
+            for (int lane = 0; lane < 32; ++lane) {
+                const int g = lane >> 2, t = lane & 3;
+                const int ra = src_row(row_map, tile * 16 + g), rb = src_row(row_map, tile * 16 + g + 8);
+                auto u = [&](int r, int kc) -> uint32_t {
+                    const uint8_t b = packed[(long long)r * (k / 2) + (kc >> 1)];
+                    return (kc & 1) ? (b >> 4) : (b & 0xF);
+                };
+                for (int step = 0; step < 4; ++step) {
+                    const int k0 = kk * 64 + step * 16 + 2 * t;
+                    const uint32_t w = u(ra, k0) | (u(rb, k0) << 4) | (u(ra, k0 + 8) << 8) | (u(rb, k0 + 8) << 12) |
+                                       (u(ra, k0 + 1) << 16) | (u(rb, k0 + 1) << 20) | (u(ra, k0 + 9) << 24) |
+                                       (u(rb, k0 + 9) << 28);
+                    std::memcpy(ub + lane * 16 + step * 4, &w, 4);
+                }
+            }
+            for (int g = 0; g < 8; ++g) {
+                const int ra = src_row(row_map, tile * 16 + g), rb = src_row(row_map, tile * 16 + g + 8);
+                std::memcpy(ub + 512 + g * 8, sb + ((long long)ra * upt + kk) * 2, 4);      // scale, bias of row g
+                std::memcpy(ub + 512 + g * 8 + 4, sb + ((long long)rb * upt + kk) * 2, 4);  // of row g + 8
+            }
+        }
+    });
+}
+
 void pack_q8(int n_rows, int k, const int8_t* codes, const uint16_t* scales, const int* row_map, uint8_t* out) {
     const int upt = k / 64, groups = k / 32;
     parallel_rows(n_rows / 16, [&](int tile) {
@@ -206,7 +238,7 @@ icua_status icua_quantize_q4s(const float* w, int32_t rows, int32_t cols, uint8_
 uint64_t icua_packed_bytes(int32_t fmt, int32_t n_rows, int32_t k) {
     if (n_rows <= 0 || k <= 0 || n_rows % 16 || k % 1024) return 0;
     const uint64_t units = (uint64_t)(n_rows / 16) * (uint64_t)(k / 64);
-    if (fmt == ICUA_FMT_Q4S) return units * 576;
+    if (fmt == ICUA_FMT_Q4S || fmt == ICUA_FMT_Q4) return units * 576;
     if (fmt == ICUA_FMT_Q8) return units * 1088;
     return 0;
 }
@@ -216,6 +248,8 @@ icua_status icua_pack_matrix(int32_t fmt, int32_t n_rows, int32_t k, const void*
     if (!codes || !scales || !packed_out || icua_packed_bytes(fmt, n_rows, k) == 0) return ICUA_ERR_INVALID;
     if (fmt == ICUA_FMT_Q4S)
         pack_q4s(n_rows, k, (const uint8_t*)codes, scales, nullptr, (uint8_t*)packed_out);
+    else if (fmt == ICUA_FMT_Q4)
+        pack_q4a(n_rows, k, (const uint8_t*)codes, scales, nullptr, (uint8_t*)packed_out);
     else
         pack_q8(n_rows, k, (const int8_t*)codes, scales, nullptr, (uint8_t*)packed_out);
     return ICUA_OK;

@@ -15,7 +15,7 @@ namespace icua {
 // x[i] = pooler row (IMAGE_PAD tokens inside the visual block) or the dequantised embedding row.
 // One CTA of 256 threads per prompt row.
 __global__ void prefill_embed_kernel(const int* prompt, int n, int vis_off, int n_vis, const float* pooler,
-                                     const uint8_t* embed, int embed_tiles, float* x) {
+                                     const uint8_t* embed, int embed_tiles, int embed_fmt, float* x) {
     const int i = blockIdx.x;
     if (i >= n) return;
     const int tok = prompt[i];
@@ -24,7 +24,7 @@ __global__ void prefill_embed_kernel(const int* prompt, int n, int vis_off, int 
                                ? pooler + (size_t)v * H : nullptr;
     float* xr = x + (size_t)i * H;
     for (int k = threadIdx.x; k < H; k += blockDim.x)
-        xr[k] = vis_row ? vis_row[k] : q8_tile_value(embed, embed_tiles, H, tok, k);
+        xr[k] = vis_row ? vis_row[k] : embed_value(embed_fmt, embed, embed_tiles, tok, k);
 }
 
 // out[i] = fp16(x[i] * rsqrt(mean(x[i]^2) + eps) * w): the fp16 GEMM input of a prompt row.

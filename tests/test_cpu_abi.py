@@ -73,9 +73,10 @@ def decode_tiles(fmt, packed, n_rows, k):
     Units of 16 rows x 64 columns, stored slice-major: K is split into `slices` slices (16 for
     q4s, 8 for q8); unit (tile, kk) of slice w = kk // ku lives at ((w * tiles + tile) * ku + kk % ku).
     """
-    ub = 576 if fmt == L.FMT_Q4S else 1088
-    wb = 512 if fmt == L.FMT_Q4S else 1024
-    slices = 16 if fmt == L.FMT_Q4S else 8
+    q4 = fmt in (L.FMT_Q4S, L.FMT_Q4)
+    ub = 576 if q4 else 1088
+    wb = 512 if q4 else 1024
+    slices = 16 if q4 else 8
     upt, tiles = k // 64, n_rows // 16
     ku = upt // slices
     raw = packed.reshape(slices, tiles, ku, ub)
@@ -86,35 +87,45 @@ def decode_tiles(fmt, packed, n_rows, k):
     for step in range(4):
         for (dk, rowoff) in ((0, 0), (1, 0), (8, 0), (9, 0), (0, 8), (1, 8), (8, 8), (9, 8)):
             kin = step * 16 + 2 * t + dk
-            if fmt == L.FMT_Q4S:
+            if q4:
                 words = units[:, :, :wb].reshape(tiles, upt, 32, 4, 4)[:, :, :, step, :].copy().view(np.uint32)[..., 0]
                 shift = (dk & 1) * 16 + (dk >> 3) * 8 + (rowoff >> 3) * 4
-                u = ((words >> shift) & 0xF).astype(np.int32) - 8
+                u = ((words >> shift) & 0xF).astype(np.int32) - (8 if fmt == L.FMT_Q4S else 0)
             else:
                 grp16 = units[:, :, (step >> 1) * 512:(step >> 1) * 512 + 512].reshape(tiles, upt, 32, 16)
                 byte = (step & 1) * 8 + (dk >> 3) * 4 + (dk & 1) * 2 + (rowoff >> 3)
                 u = grp16[..., byte].astype(np.int32) - 128
-            sc = units[:, :, wb:wb + 64].reshape(tiles, upt, 8, 2, 4).copy().view(np.float16)
-            grp = kin >> 5
-            s = sc[:, :, g, grp, (rowoff >> 3)]  # [tiles, upt, 32]
             rows = (np.arange(tiles)[:, None, None] * 16 + g[None, None, :] + rowoff)
             cols = np.arange(upt)[None, :, None] * 64 + kin[None, None, :]
-            out[np.broadcast_to(rows, u.shape), np.broadcast_to(cols, u.shape)] = s.astype(np.float32) * u
+            if fmt == L.FMT_Q4:  # affine: (scale, bias) of rows g, g+8 for the unit's 64 columns
+                sb = units[:, :, wb:wb + 64].reshape(tiles, upt, 8, 2, 4).copy().view(np.float16)
+                sb = sb.reshape(tiles, upt, 8, 2, 2)[:, :, g, rowoff >> 3, :].astype(np.float32)
+                val = sb[..., 0] * u + sb[..., 1]
+            else:
+                sc = units[:, :, wb:wb + 64].reshape(tiles, upt, 8, 2, 4).copy().view(np.float16)
+                grp = kin >> 5
+                s = sc[:, :, g, grp, (rowoff >> 3)]  # [tiles, upt, 32]
+                val = s.astype(np.float32) * u
+            out[np.broadcast_to(rows, u.shape), np.broadcast_to(cols, u.shape)] = val
     return out
 
 
-@pytest.mark.parametrize("fmt", [L.FMT_Q4S, L.FMT_Q8])
+@pytest.mark.parametrize("fmt", [L.FMT_Q4S, L.FMT_Q8, L.FMT_Q4])
 def test_pack_layout_roundtrip(fmt):
     rows, k = 48, 2048
     w = (np.random.default_rng(3).standard_normal((rows, k)) * 0.02).astype(np.float32)
     if fmt == L.FMT_Q4S:
         codes, scales = model.quantize_q4s(w)
         ref = O.dequant_q4s(codes, scales.view(np.float16))
+    elif fmt == L.FMT_Q4:  # reference affine q4 (the oracle's quantizer makes the test codes)
+        codes, sb = O.quantize_q4_affine(w)
+        scales = np.ascontiguousarray(sb).view(np.uint16)
+        ref = O.dequant_q4_affine(codes, sb)
     else:
         codes, scales = model.quantize_q8(w)
         ref = O.dequant_q8(codes, scales.view(np.float16))
     nbytes = L.lib().icua_packed_bytes(fmt, rows, k)
-    assert nbytes == rows // 16 * k // 64 * (576 if fmt == L.FMT_Q4S else 1088)
+    assert nbytes == rows // 16 * k // 64 * (1088 if fmt == L.FMT_Q8 else 576)
     out = np.zeros(nbytes, np.uint8)
     L.check(L.lib().icua_pack_matrix(fmt, rows, k, codes.ctypes.data, scales.ctypes.data, out.ctypes.data))
     assert np.array_equal(decode_tiles(fmt, out, rows, k), ref)

@@ -40,35 +40,40 @@ def prompts(n, seed=5):
 
 @pytest.mark.parametrize("kv,n", [("f16", 4), ("bf16", 4), ("bf16", 56)])
 def test_batch_matches_one_at_a_time(tensors, kv, n):
-    """4 rows run the attention in clusters of 4 CTAs per (row, head), 56 rows in clusters of 2."""
-    steps = 6
+    """Teacher-forced: every step both paths get the same input token per session (the batch-1
+    path's choice), so the per-row logits are compared on identical contexts.  4 rows run the
+    attention in clusters of 4 CTAs per (row, head), 56 rows in clusters of 2."""
+    steps = 4
     ps = prompts(n)
-    # batched: sessions in a shuffled order
-    order = [int(v) for v in np.random.default_rng(n).permutation(n)]
-    e = make_engine(tensors, kv, sessions=n)
+    order = [int(v) for v in np.random.default_rng(n).permutation(n)]  # batch rows in a shuffled order
+    eb = make_engine(tensors, kv, sessions=n)  # batched
+    e1 = make_engine(tensors, kv, sessions=n)  # one session at a time
+    first = {}
     for s in range(n):
-        e.prefill(ps[s], session=s)
-    cap = e.capture_batch_logits(n)
-    got = e.decode_batch(order, steps)
-    got_logits = cap.copy()
-    e.close()
-    # one session at a time through the batch-1 decode
-    e = make_engine(tensors, kv, sessions=n)
-    want, want_logits = [], []
-    for s in order:
-        e.prefill(ps[s], session=s)
-        c = e.capture_step_logits(steps)
-        want.append(e.decode(steps, session=s))
-        want_logits.append(c[steps - 1].copy())
-    e.close()
-    agree = np.mean(np.array(want) == got)
-    for r in range(n):
-        err = float(np.abs(got_logits[r] - want_logits[r]).max())
-        c = cos_sim(got_logits[r], want_logits[r])
-        print(f"row {r} (session {order[r]}): max|d| {err:.3e} cos {c:.6f}")
-        assert err <= ATOL and c >= COS
-    print(f"batched vs one-at-a-time ({kv}): agreement {agree:.3f}")
-    assert agree >= 0.99
+        eb.prefill(ps[s], session=s)
+        first[s] = e1.prefill(ps[s], session=s)
+    cap = eb.capture_batch_logits(n)
+    cur = [first[s] for s in order]
+    worst, flips = 0.0, 0
+    for step in range(steps):
+        got = eb.decode_batch(order, 1, in_tokens=cur)[:, 0]
+        nxt = []
+        for r, s in enumerate(order):
+            t1 = e1.decode_step(cur[r], session=s)
+            want = e1.logits()
+            err = float(np.abs(cap[r] - want).max())
+            c = cos_sim(cap[r], want)
+            worst = max(worst, err)
+            assert err <= ATOL and c >= COS, f"step {step} row {r} (session {s}): max|d|={err} cos={c}"
+            if got[r] != t1:  # only where the two best logits nearly tie
+                flips += 1
+                assert abs(want[got[r]] - want[t1]) <= 2 * ATOL, (step, r, got[r], t1)
+            nxt.append(t1)
+        cur = nxt
+    eb.close()
+    e1.close()
+    print(f"batched vs one-at-a-time ({kv}, {n} rows): max|d| {worst:.3e}, near-tie flips {flips}/{steps * n}")
+    assert flips <= 0.01 * steps * n + 1
 
 
 def test_batch_in_tokens_and_continuation(tensors):
