@@ -52,6 +52,7 @@ thread_local std::string g_error;
 
 struct Matrix {
     uint8_t* dev = nullptr;
+    uint8_t* tc = nullptr;     // the same matrix in tensor-core tile order (tensor-core GEMMs)
     int fmt = 0, n_rows = 0, k = 0;
     int n_tiles = 0, grid = 0;
     bool stream = false;      // streaming (ring) path; otherwise all tiles of a CTA in one copy
@@ -280,6 +281,7 @@ bool make_act_map(CUtensorMap* map, const void* base, int rows, int k, int box_r
 TcGemmParams tc_params(const Matrix& m, int m_tok, int* err) {
     TcGemmParams p{};
     p.w = m.dev;
+    p.wtc = m.tc;
     p.n_rows = m.n_rows;
     p.k = m.k;
     p.n_tiles = m.n_tiles;
@@ -367,6 +369,8 @@ cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmPar
     ks = std::min(ks, p.k / TC_BK / 4);  // at least four k-blocks per slice
     auto run = [&](auto epi_tag, const TcGemmParams& q, int ksplit) -> cudaError_t {
         constexpr int E = decltype(epi_tag)::value;
+        if (m.fmt == FMT_F16)
+            return launch_tc_gemm<E, FMT_F16>(x, e->cfg.max_pass, q, s, reinterpret_cast<const __half*>(m.dev), ksplit);
         if (m.fmt == FMT_Q8) return launch_tc_gemm<E, FMT_Q8>(x, e->cfg.max_pass, q, s, nullptr, ksplit);
         if (m.fmt == FMT_Q4A) return launch_tc_gemm<E, FMT_Q4A>(x, e->cfg.max_pass, q, s, nullptr, ksplit);
         return launch_tc_gemm<E, FMT_Q4S>(x, e->cfg.max_pass, q, s, nullptr, ksplit);
@@ -448,7 +452,8 @@ cudaError_t set_smem_attrs() {
           (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q8, 2>, (const void*)tc_gemm_kernel<TC_STORE, FMT_Q4A, 1>,
           (const void*)tc_gemm_kernel<TC_RESID, FMT_Q4A, 1>, (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q4A, 1>,
           (const void*)tc_gemm_kernel<TC_STORE, FMT_Q4A, 2>, (const void*)tc_gemm_kernel<TC_RESID, FMT_Q4A, 2>,
-          (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q4A, 2>, (const void*)tc_gemm_kernel<TC_ARGMAX, FMT_Q4A, 1>}) {
+          (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q4A, 2>, (const void*)tc_gemm_kernel<TC_ARGMAX, FMT_Q4A, 1>,
+          (const void*)tc_gemm_kernel<TC_ARGMAX, FMT_F16, 1>}) {
         if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)) != cudaSuccess)
             return e;
     }
@@ -648,6 +653,7 @@ void drop_graphs(Session& S) {
 
 icua_status ensure_graphs(icua_engine* eng, Session& S) {
     icua_status s;
+    if (eng->cfg.format == ICUA_FMT_F16) return ICUA_OK;  // f16 engines decode through the batched step
     if (!S.g_prefill_tok && (s = build_graph(eng, S, 0, &S.g_prefill_tok)) != ICUA_OK) return s;
     if (!S.g_step1 && (s = build_graph(eng, S, 1, &S.g_step1)) != ICUA_OK) return s;
     if (!S.g_stepn && (s = build_graph(eng, S, 2, &S.g_stepn)) != ICUA_OK) return s;
@@ -711,16 +717,19 @@ icua_status sync_and_check(icua_engine* eng, Session& S) {
 size_t expected_bytes(const icua_engine* e, int id) {
     const int fmt = e->cfg.format;
     const size_t V = (size_t)e->cfg.vocab;
-    // embedding: q8 codes + scales, except in reference q4 files (affine q4 like every matrix)
-    if (id == ICUA_TID_EMBED) return fmt == ICUA_FMT_Q4 ? V * H / 2 : V * H;
-    if (id == ICUA_TID_EMBED_SB) return fmt == ICUA_FMT_Q4 ? V * (H / 64) * 4 : V * (H / 32) * 2;
+    // embedding: q8 codes + scales, except in reference q4 files (affine q4 like every matrix) and
+    // f16 files (fp16 values, no scale tensors)
+    if (id == ICUA_TID_EMBED) return fmt == ICUA_FMT_Q4 ? V * H / 2 : fmt == ICUA_FMT_F16 ? V * H * 2 : V * H;
+    if (id == ICUA_TID_EMBED_SB) return fmt == ICUA_FMT_Q4 ? V * (H / 64) * 4 : fmt == ICUA_FMT_F16 ? 0 : V * (H / 32) * 2;
     if (id == ICUA_TID_FINAL_NORM) return H * 4;
     const int rel = id - ICUA_TID_LAYER_BASE;
     const int slot = rel % ICUA_TID_PER_LAYER;
     auto mat = [&](int rows, int k) -> size_t {
+        if (fmt == ICUA_FMT_F16) return (size_t)rows * k * 2;
         return (fmt == ICUA_FMT_Q4S || fmt == ICUA_FMT_Q4) ? (size_t)rows * k / 2 : (size_t)rows * k;
     };
     auto sb = [&](int rows, int k) -> size_t {
+        if (fmt == ICUA_FMT_F16) return 0;
         return fmt == ICUA_FMT_Q4 ? (size_t)rows * (k / 64) * 4 : (size_t)rows * (k / 32) * 2;  // half2 / half
     };
     switch (slot) {
@@ -741,6 +750,7 @@ size_t expected_bytes(const icua_engine* e, int id) {
 }
 
 bool id_used(const icua_engine* e, int id) {
+    if (expected_bytes(e, id) == 0) return false;  // f16 files carry no scale tensors
     if (id == ICUA_TID_EMBED || id == ICUA_TID_EMBED_SB || id == ICUA_TID_FINAL_NORM) return true;
     const int rel = id - ICUA_TID_LAYER_BASE;
     if (rel < 0 || rel >= e->cfg.n_layers * ICUA_TID_PER_LAYER) return false;
@@ -754,8 +764,27 @@ icua_status upload_f32(icua_engine* eng, float** dst, const std::vector<uint8_t>
     return ICUA_OK;
 }
 
+// Reference f16 files: the matrix stays row-major fp16 (rows permuted by row_map), the operand of
+// the tensor-core GEMMs as it is.
+icua_status upload_f16_matrix(icua_engine* eng, Matrix& m, int rows, int k, const std::vector<uint8_t>& codes,
+                              const int* row_map) {
+    m.fmt = FMT_F16;
+    m.n_rows = rows;
+    m.k = k;
+    m.n_tiles = rows / 16;
+    const size_t row_bytes = (size_t)k * 2;
+    std::vector<uint8_t> host(codes.size());
+    for (int d = 0; d < rows; ++d)
+        std::memcpy(host.data() + d * row_bytes, codes.data() + (size_t)(row_map ? row_map[d] : d) * row_bytes, row_bytes);
+    icua_status s = dalloc(eng, reinterpret_cast<void**>(&m.dev), host.size());
+    if (s != ICUA_OK) return s;
+    CK(cudaMemcpy(m.dev, host.data(), host.size(), cudaMemcpyHostToDevice));
+    return ICUA_OK;
+}
+
 icua_status upload_matrix(icua_engine* eng, Matrix& m, int fmt, int rows, int k, const std::vector<uint8_t>& codes,
                           const std::vector<uint8_t>& sb, const int* row_map) {
+    if (fmt == FMT_F16) return upload_f16_matrix(eng, m, rows, k, codes, row_map);
     setup_matrix(m, fmt, rows, k, eng->n_sm);
     const size_t bytes = icua_packed_bytes(fmt, rows, k);
     std::vector<uint8_t> packed(bytes);
@@ -769,6 +798,12 @@ icua_status upload_matrix(icua_engine* eng, Matrix& m, int fmt, int rows, int k,
     icua_status s = dalloc(eng, reinterpret_cast<void**>(&m.dev), bytes);
     if (s != ICUA_OK) return s;
     CK(cudaMemcpy(m.dev, packed.data(), bytes, cudaMemcpyHostToDevice));
+    if (rows % TC_BM == 0) {  // every matrix the tensor-core GEMMs read
+        if ((s = dalloc(eng, reinterpret_cast<void**>(&m.tc), bytes)) != ICUA_OK) return s;
+        const long long nv = (long long)bytes / 16;
+        tc_order_kernel<<<(int)std::min<long long>((nv + 255) / 256, 4096), 256>>>(m.dev, fmt, rows / 16, k / 64, m.tc);
+        CK(cudaGetLastError());
+    }
     return ICUA_OK;
 }
 
@@ -780,8 +815,9 @@ icua_status try_finalize(icua_engine* eng) {
     icua_status s;
     auto& st = eng->staged;
     // decoder layers in the file's format; the tied embedding is q8, or affine q4 in reference q4 files
-    const int fmt = eng->cfg.format == ICUA_FMT_Q8 ? FMT_Q8 : eng->cfg.format == ICUA_FMT_Q4 ? FMT_Q4A : FMT_Q4S;
-    const int efmt = eng->cfg.format == ICUA_FMT_Q4 ? FMT_Q4A : FMT_Q8;
+    const int cf = eng->cfg.format;
+    const int fmt = cf == ICUA_FMT_Q8 ? FMT_Q8 : cf == ICUA_FMT_Q4 ? FMT_Q4A : cf == ICUA_FMT_F16 ? FMT_F16 : FMT_Q4S;
+    const int efmt = cf == ICUA_FMT_Q4 ? FMT_Q4A : cf == ICUA_FMT_F16 ? FMT_F16 : FMT_Q8;
     if ((s = upload_matrix(eng, eng->embed, efmt, eng->cfg.vocab, H, st[ICUA_TID_EMBED], st[ICUA_TID_EMBED_SB],
                            nullptr)) != ICUA_OK)
         return s;
@@ -809,6 +845,7 @@ icua_status try_finalize(icua_engine* eng) {
         if ((s = upload_matrix(eng, ly.d, fmt, H, FF, st[id(ICUA_SLOT_WD)], st[id(ICUA_SLOT_WD_SB)], nullptr)) != ICUA_OK)
             return s;
     }
+    CK(cudaDeviceSynchronize());  // the re-layout kernels ran on the legacy stream
     eng->staged.clear();
     eng->uploaded = true;
     return ICUA_OK;
@@ -841,8 +878,9 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
         const int kind = seq[i].second;
         return kind == 0 ? ly.qkv : kind == 1 ? ly.o : kind == 2 ? ly.gu : ly.d;
     };
+    const bool f16w = e->layers[0].qkv.fmt == FMT_F16;  // reference f16 files: no dequantisation
     auto dequant = [&](int i) -> cudaError_t {
-        if (i >= (int)seq.size()) return cudaSuccess;
+        if (f16w || i >= (int)seq.size()) return cudaSuccess;
         cudaError_t er;
         if (i >= 2 && (er = cudaStreamWaitEvent(e->side, e->ev_done[(i - 2) % 8], 0)) != cudaSuccess) return er;
         if ((er = launch_dequant_f16(matrix_of(i), e->wscr[seq[i].first & 1][seq[i].second], e->n_sm, e->side)) !=
@@ -851,22 +889,32 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
         return cudaEventRecord(e->ev_ready[i % 8], e->side);
     };
     int gi = 0;  // next GEMM of the sequence
-    auto gemm_ready = [&]() { return cudaStreamWaitEvent(st, e->ev_ready[gi % 8], 0); };
+    auto gemm_ready = [&]() { return f16w ? cudaSuccess : cudaStreamWaitEvent(st, e->ev_ready[gi % 8], 0); };
     auto gemm_issued = [&]() -> cudaError_t {
+        if (f16w) return cudaSuccess;
         cudaError_t er = cudaEventRecord(e->ev_done[gi % 8], st);
         if (er != cudaSuccess) return er;
         ++gi;
         return dequant(gi + 1);
     };
     // the side stream starts behind everything already queued on the main stream
-    if ((err = cudaEventRecord(e->ev_done[7], st)) != cudaSuccess) return err;
-    if ((err = cudaStreamWaitEvent(e->side, e->ev_done[7], 0)) != cudaSuccess) return err;
-    if ((err = dequant(0)) != cudaSuccess || (err = dequant(1)) != cudaSuccess) return err;
+    if (!f16w) {
+        if ((err = cudaEventRecord(e->ev_done[7], st)) != cudaSuccess) return err;
+        if ((err = cudaStreamWaitEvent(e->side, e->ev_done[7], 0)) != cudaSuccess) return err;
+        if ((err = dequant(0)) != cudaSuccess || (err = dequant(1)) != cudaSuccess) return err;
+    }
     for (int l = 0; l < L; ++l) {
         Layer& ly = e->layers[l];
         KVT* kc = reinterpret_cast<KVT*>(S.kc) + kv_layer * l;
         KVT* vc = reinterpret_cast<KVT*>(S.vc) + kv_layer * l;
-        __half* const* w16 = e->wscr[l & 1];
+        const __half* w16[4];
+        for (int kind = 0; kind < 4; ++kind) w16[kind] = e->wscr[l & 1][kind];
+        if (f16w) {
+            w16[0] = reinterpret_cast<const __half*>(ly.qkv.dev);
+            w16[1] = reinterpret_cast<const __half*>(ly.o.dev);
+            w16[2] = reinterpret_cast<const __half*>(ly.gu.dev);
+            w16[3] = reinterpret_cast<const __half*>(ly.d.dev);
+        }
         if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
                           (const float*)ly.attn_norm, n_rows, e->pxn)) != cudaSuccess)
             return err;
@@ -1000,9 +1048,13 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
     TcGemmParams p = tc_params(e->embed, n_rows, e->gemm_err);
     p.best_v = e->batch_best_v;
     p.best_i = e->batch_best_i;
-    p.out = e->batch_logits;  // nullptr unless the logits of the step were requested
+    // logits when requested; a one-row step of an f16 engine (its batch-1 decode) keeps them like
+    // the GEMV head does
+    p.out = e->batch_logits ? e->batch_logits : (e->embed.fmt == FMT_F16 && n_rows == 1 ? e->logits : nullptr);
     p.ldo = e->cfg.vocab;
     err = e->embed.fmt == FMT_Q4A ? launch_tc_gemm<TC_ARGMAX, FMT_Q4A>(e->pxn, e->cfg.max_pass, p, st)
+        : e->embed.fmt == FMT_F16 ? launch_tc_gemm<TC_ARGMAX, FMT_F16>(e->pxn, e->cfg.max_pass, p, st,
+                                                                       reinterpret_cast<const __half*>(e->embed.dev))
                                   : launch_tc_gemm<TC_ARGMAX, FMT_Q8>(e->pxn, e->cfg.max_pass, p, st);
     if (err != cudaSuccess) return err;
     return launch(batch_commit_kernel, n_rows, 256, 0, st, false, (const float*)e->batch_best_v,
@@ -1063,7 +1115,8 @@ void icua_default_config(icua_config* c) {
 icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
     if (!cfg || !out) return fail(nullptr, ICUA_ERR_INVALID, "null argument");
     *out = nullptr;
-    if (cfg->format != ICUA_FMT_Q4S && cfg->format != ICUA_FMT_Q8 && cfg->format != ICUA_FMT_Q4)
+    if (cfg->format != ICUA_FMT_Q4S && cfg->format != ICUA_FMT_Q8 && cfg->format != ICUA_FMT_Q4 &&
+        cfg->format != ICUA_FMT_F16)
         return fail(nullptr, ICUA_ERR_UNSUPPORTED, "weight format %d is not implemented by the kernels", cfg->format);
     if (cfg->n_layers < 1 || cfg->n_layers > 28 || cfg->vocab < 16 || cfg->vocab % 16 || cfg->max_context < 2 ||
         cfg->max_pass < 1 || cfg->max_steps < 1 || cfg->max_sessions < 1 || cfg->steps_per_graph < 1 ||
@@ -1480,6 +1533,9 @@ static icua_status prepare_prefill(icua_engine* eng, Session& S, int session, co
     return ICUA_OK;
 }
 
+static icua_status decode_batch_impl(icua_engine* eng, const int32_t* sessions, int32_t n_sessions,
+                                     const int32_t* in_tokens, int32_t steps, int32_t* out);
+
 icua_status icua_prefill(icua_engine* eng, int32_t session, const int32_t* tokens, int32_t n, const icua_visual* vis,
                          int32_t write_logits, int32_t* first_token) {
     if (!eng || !tokens) return fail(eng, ICUA_ERR_INVALID, "null argument");
@@ -1494,6 +1550,33 @@ icua_status icua_prefill(icua_engine* eng, int32_t session, const int32_t* token
     if ((s = prepare_prefill(eng, *S, session, tokens, n, vis, write_logits, &vis_off, &n_vis)) != ICUA_OK) return s;
     CK(cudaEventRecord(eng->ev[0], eng->stream));
     const int n_rows = n - 1;  // rows before the last one, which runs as a decode step
+    if (eng->cfg.format == ICUA_FMT_F16) {
+        // f16 engines: every row before the last through the tensor-core path, the last one as a
+        // one-row batched step (its head gives the first token and keeps the logits)
+        if (tokens[n - 1] == IMAGE_PAD_ID)
+            return fail(eng, ICUA_ERR_UNSUPPORTED, "f16 engines need a text token at the end of the prompt");
+        if (n_rows > 0) {
+            const cudaError_t e2 = eng->cfg.kv_dtype == ICUA_KV_BF16
+                                       ? record_prefill_rows<__nv_bfloat16>(eng, *S, n_rows, vis_off, n_vis)
+                                       : record_prefill_rows<__half>(eng, *S, n_rows, vis_off, n_vis);
+            if (e2 != cudaSuccess) return fail(eng, ICUA_ERR_CUDA, "prefill launch: %s", cudaGetErrorString(e2));
+        }
+        const int pos = S->pos + n_rows;
+        CK(cudaMemcpyAsync(&S->st->pos, &pos, 4, cudaMemcpyHostToDevice, eng->stream));
+        S->pos = pos;
+        int32_t tok1 = 0;
+        const float keep_decode_ms = eng->timing.decode_ms;
+        if ((s = decode_batch_impl(eng, &session, 1, &tokens[n - 1], 1, &tok1)) != ICUA_OK) return s;
+        eng->timing.decode_ms = keep_decode_ms;
+        CK(cudaEventRecord(eng->ev[1], eng->stream));
+        CK(cudaStreamSynchronize(eng->stream));
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, eng->ev[0], eng->ev[1]);
+        eng->timing.prefill_ms = ms;
+        eng->timing.prefill_tokens = n;
+        if (first_token) *first_token = tok1;
+        return ICUA_OK;
+    }
     if (eng->cfg.prefill_gemm_min > 0 && n_rows >= eng->cfg.prefill_gemm_min) {
         const cudaError_t e2 = eng->cfg.kv_dtype == ICUA_KV_BF16
                                    ? record_prefill_rows<__nv_bfloat16>(eng, *S, n_rows, vis_off, n_vis)
@@ -1524,6 +1607,17 @@ icua_status icua_prefill(icua_engine* eng, int32_t session, const int32_t* token
 
 icua_status icua_decode(icua_engine* eng, int32_t session, int32_t max_new, int32_t* out, int32_t* n_out) {
     if (!eng || !out || !n_out) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    if (eng->cfg.format == ICUA_FMT_F16 && max_new > 0) {
+        // f16 engines: the batched step with this one session
+        std::vector<int32_t> toks(max_new);
+        icua_status s2 = decode_batch_impl(eng, &session, 1, nullptr, max_new, toks.data());
+        if (s2 != ICUA_OK) return s2;
+        int n = 0;
+        while (n < max_new && toks[n] >= 0 && !(eng->stop_on_eos && (toks[n] == eng->eos0 || toks[n] == eng->eos1)))
+            out[n] = toks[n], ++n;
+        *n_out = n;
+        return ICUA_OK;
+    }
     icua_status s;
     if ((s = check_ready(eng)) != ICUA_OK) return s;
     Session* S = get_session(eng, session);
@@ -1585,6 +1679,7 @@ icua_status icua_decode(icua_engine* eng, int32_t session, int32_t max_new, int3
 
 icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token, int32_t* out_token) {
     if (!eng || !out_token) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    if (eng->cfg.format == ICUA_FMT_F16) return decode_batch_impl(eng, &session, 1, &in_token, 1, out_token);
     icua_status s;
     if ((s = check_ready(eng)) != ICUA_OK) return s;
     Session* S = get_session(eng, session);
@@ -1613,6 +1708,11 @@ icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token
 
 icua_status icua_decode_batch(icua_engine* eng, const int32_t* sessions, int32_t n_sessions, const int32_t* in_tokens,
                               int32_t steps, int32_t* out) {
+    return decode_batch_impl(eng, sessions, n_sessions, in_tokens, steps, out);
+}
+
+static icua_status decode_batch_impl(icua_engine* eng, const int32_t* sessions, int32_t n_sessions,
+                                     const int32_t* in_tokens, int32_t steps, int32_t* out) {
     if (!eng || !sessions || !out) return fail(eng, ICUA_ERR_INVALID, "null argument");
     icua_status s;
     if ((s = check_ready(eng)) != ICUA_OK) return s;

@@ -37,7 +37,9 @@ constexpr int TC_SMEM_BUDGET = 225 * 1024;
 enum TcEpi { TC_STORE = 0, TC_RESID = 1, TC_SWIGLU = 2, TC_ARGMAX = 3 };
 
 struct TcGemmParams {
-    const uint8_t* w;          // weights in the device tile layout [n_rows, k] (q4s or q8)
+    const uint8_t* w;          // weights in the device tile layout [n_rows, k] (q4s, q4a or q8)
+    const uint8_t* wtc;        // the same weights in tensor-core tile order (tc_order_kernel), or
+                               //   nullptr: then each stage gathers 8 x MH units from `w`
     int n_rows, k, n_tiles, upt;
     int m_tok;                 // activation rows (tokens)
     int bn;                    // tokens per CTA tile (multiple of 16, <= 256; the TMA box height)
@@ -347,12 +349,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                                     (kb0 + (kc + krot) % nk) * TC_BK, row0 + h * TC_BM, &bfull[s]);
                 } else {
                     uint8_t* raw = smem + SM.raw_off + s * SM.raw_bytes;
+                    const int kblk = kb0 + (kc + krot) % nk;
                     mbar_expect_tx(&rawfull[s], NU * UB);
+                    if (p.wtc != nullptr) {
+                        // tensor-core tile order: the 8 units of a 128-row group are contiguous
+#pragma unroll
+                        for (int h = 0; h < MH; ++h)
+                            bulk_g2s(raw + h * 8 * UB, p.wtc + ((size_t)(rtile * MH + h) * p.upt + kblk) * 8 * UB, 8 * UB,
+                                     &rawfull[s]);
+                    } else {
 #pragma unroll 1
-                    for (int t = 0; t < NU; ++t)
-                        bulk_g2s(raw + t * UB,
-                                 p.w + icua_layout::unit_offset(FMT, p.n_tiles, p.upt, tile0 + t, kb0 + (kc + krot) % nk),
-                                 UB, &rawfull[s]);
+                        for (int t = 0; t < NU; ++t)
+                            bulk_g2s(raw + t * UB, p.w + icua_layout::unit_offset(FMT, p.n_tiles, p.upt, tile0 + t, kblk),
+                                     UB, &rawfull[s]);
+                    }
                     mbar_expect_tx(&bfull[s], (uint32_t)SM.b_bytes);
                 }
                 tma_load_2d(smem + SM.b_off + s * SM.b_bytes, &xmap, (kb0 + (kc + krot) % nk) * TC_BK, tok0, &bfull[s]);
@@ -579,6 +589,24 @@ __global__ void __launch_bounds__(256) dequant_q4a_f16_kernel(const uint8_t* til
             o[t] = *reinterpret_cast<const uint32_t*>(&hv);
         }
         *reinterpret_cast<uint4*>(out + (size_t)row * K + (size_t)j8 * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// Tensor-core tile order: unit (tile, kk) of the slice-major layout moves to
+// ((tile / 8) * upt + kk) * 8 + tile % 8, so that a GEMM stage (8 consecutive tiles, one k-block)
+// is one contiguous run of 8 units: one bulk copy instead of eight small ones, whose per-request
+// cost bounded the fused dequant-GEMM.  One thread per 16 bytes.
+__global__ void tc_order_kernel(const uint8_t* src, int fmt, int n_tiles, int upt, uint8_t* dst) {
+    const int ub = unit_bytes(fmt), v_per_unit = ub / 16;
+    const long long total = (long long)n_tiles * upt * v_per_unit;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const long long unit = i / v_per_unit;
+        const int v = (int)(i % v_per_unit);
+        const int t8 = (int)(unit % 8);
+        const long long rest = unit / 8;
+        const int kk = (int)(rest % upt), g8 = (int)(rest / upt);
+        const long long so = icua_layout::unit_offset(fmt, n_tiles, upt, g8 * 8 + t8, kk);
+        reinterpret_cast<uint4*>(dst + unit * ub)[v] = reinterpret_cast<const uint4*>(src + so)[v];
     }
 }
 

@@ -124,8 +124,10 @@ __device__ __forceinline__ float q4a_tile_value(const uint8_t* tiles, int n_tile
     return fmaf(sb.x, (float)u, sb.y);
 }
 
-// Embedding row element for the engine's embedding format (q8, or q4a for reference q4 files).
+// Embedding row element for the engine's embedding format (q8; q4a for reference q4 files; the
+// row-major fp16 matrix of reference f16 files).
 __device__ __forceinline__ float embed_value(int fmt, const uint8_t* tiles, int n_tiles, int row, int k) {
+    if (fmt == FMT_F16) return __half2float(reinterpret_cast<const __half*>(tiles)[(size_t)row * H + k]);
     return fmt == FMT_Q4A ? q4a_tile_value(tiles, n_tiles, H, row, k) : q8_tile_value(tiles, n_tiles, H, row, k);
 }
 

@@ -45,7 +45,7 @@ class Engine:
         cfg.max_pass = max_pass
         cfg.max_steps = max_steps
         cfg.max_sessions = max_sessions
-        cfg.format = {"q4s": L.FMT_Q4S, "q8": L.FMT_Q8, "q4": L.FMT_Q4}[weight_format]
+        cfg.format = {"q4s": L.FMT_Q4S, "q8": L.FMT_Q8, "q4": L.FMT_Q4, "f16": L.FMT_F16}[weight_format]
         cfg.kv_dtype = {"f16": L.KV_F16, "bf16": L.KV_BF16}[kv_dtype]
         cfg.steps_per_graph = steps_per_graph
         if prefill_gemm_min is not None:

@@ -95,16 +95,22 @@ def synthetic_fp32_fast(seed: int = 0, n_layers: int = 28, vocab: int = 151936, 
 def quantize_stream(fp32_stream, keep_fp32: bool = False, fmt: int = L.FMT_Q4S):
     """Quantizes a (tid, array) stream to {tensor id: bytes} in the .icua tensor layout.
 
-    ``fmt``: decoder-layer format, L.FMT_Q4S (BASELINE: symmetric int4 g32) or L.FMT_Q8 (the
-    reference's q8 files, Convert.swift:215-241); the tied embedding is q8 in both.
+    ``fmt``: decoder-layer format, L.FMT_Q4S (BASELINE: symmetric int4 g32), L.FMT_Q8 (the
+    reference's q8 files, Convert.swift:215-241; the tied embedding is q8 in both) or L.FMT_F16
+    (the reference converter's default: every matrix fp16).
     ``keep_fp32`` also returns the fp32 arrays (by tensor id of the codes) for checkers.
     """
-    if fmt not in (L.FMT_Q4S, L.FMT_Q8):
+    if fmt not in (L.FMT_Q4S, L.FMT_Q8, L.FMT_F16):
         raise ValueError(f"unsupported layer format {fmt}")
     out, raw = {}, {}
     for tid, w in fp32_stream:
         if isinstance(tid, tuple):
             codes_id, sb_id = tid
+            if fmt == L.FMT_F16:  # reference f16 files: fp16 values, no scale tensors
+                out[codes_id] = np.ascontiguousarray(w, np.float32).astype(np.float16).tobytes()
+                if keep_fp32:
+                    raw[codes_id] = w
+                continue
             if codes_id == L.TID_EMBED or fmt == L.FMT_Q8:
                 codes, scales = quantize_q8(w)
             else:

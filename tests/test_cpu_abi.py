@@ -154,7 +154,7 @@ def test_invalid_arguments_are_errors_not_crashes():
     cfg = L.IcuaConfig()
     lib.icua_default_config(C.byref(cfg))
     assert (cfg.n_layers, cfg.vocab, cfg.max_context, cfg.max_pass, cfg.max_steps) == (28, 151936, 2048, 512, 256)
-    cfg.format = L.FMT_F16
+    cfg.format = 7  # no such weight format (0 f16, 1 q8, 2 affine q4, 3 q4s are all loadable)
     h = C.c_void_p()
     assert lib.icua_engine_create(C.byref(cfg), C.byref(h)) == L.ERR_UNSUPPORTED
     assert b"format" in lib.icua_global_error()
