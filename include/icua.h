@@ -160,6 +160,23 @@ icua_status icua_capture_batch_logits(icua_engine* eng, float* host_out, int32_t
  * write to the session's cache (icua_reset_session, icua_inject_kv*) forgets the prefix. */
 icua_status icua_set_prefix_cache(icua_engine* eng, int32_t enable);
 
+/* Grammar-guided 2-token commit (reference k_commit, Shaders.swift:1497-1571; off by default,
+ * since it changes greedy output).  After each committed token a deterministic syntax token may
+ * follow it without a model step: `open` after an `action` word that is the call's first output,
+ * `space` after `comma`; the next decode pass runs both tokens through one read of the weights
+ * (the reference's dual-token GEMVs, Shaders.swift:529-595) and predicts the token after the pair.
+ * `close` ends the call like EOS.  rule == NULL selects the reference's ids (its tokenizer: '('
+ * 7, ')' 8, ',' 11, ' ' 220, eight action words).  Applies to icua_generate / icua_prefill +
+ * icua_decode on quantized engines (not to icua_decode_step, whose inputs come from the caller,
+ * nor to icua_decode_batch); ICUA_ERR_INVALID on f16 engines or ids outside the vocabulary.
+ * Session graphs are rebuilt on the next call. */
+typedef struct icua_grammar {
+    int32_t n_action;   /* 0..8 */
+    int32_t action[8];
+    int32_t comma, space, open, close;
+} icua_grammar;
+icua_status icua_set_grammar_commit(icua_engine* eng, int32_t enable, const icua_grammar* rule);
+
 /* Whole call: reset session (keeping a cached prefix), prefill, decode; returns tokens like
  * generateVision. */
 icua_status icua_generate(icua_engine* eng, int32_t session, const int32_t* tokens, int32_t n,

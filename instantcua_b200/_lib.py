@@ -31,6 +31,11 @@ class IcuaTiming(C.Structure):
                 ("total_ms", C.c_double), ("prefill_tokens", C.c_int32), ("generated_tokens", C.c_int32)]
 
 
+class IcuaGrammar(C.Structure):
+    _fields_ = [("n_action", C.c_int32), ("action", C.c_int32 * 8), ("comma", C.c_int32), ("space", C.c_int32),
+                ("open", C.c_int32), ("close", C.c_int32)]
+
+
 class IcuaVisual(C.Structure):
     _fields_ = [("pooler", C.POINTER(C.c_float)), ("deepstack", C.POINTER(C.c_float) * 3), ("n_vis", C.c_int32),
                 ("llm_h", C.c_int32), ("llm_w", C.c_int32)]
@@ -74,6 +79,7 @@ PROTOTYPES = {
     "icua_gemv": (_I, [_I, _I, _I, _P, _P, _I, _P, _P]),
     "icua_decode_batch": (_I, [_P, _IP, _I, _IP, _I, _IP]),
     "icua_set_prefix_cache": (_I, [_P, _I]),
+    "icua_set_grammar_commit": (_I, [_P, _I, C.POINTER(IcuaGrammar)]),
     "icua_capture_batch_logits": (_I, [_P, _FP, _I]),
     "icua_gemm_q4s": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),
     "icua_dequant_q4s_f16": (_I, [_I, _I, _P, _P, _P]),

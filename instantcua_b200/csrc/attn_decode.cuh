@@ -52,17 +52,18 @@ struct AttnParams {
     __half* out16;
 };
 
-template <typename KVT>
+// NT: query tokens per pass the layout holds (2 in the grammar-commit kernels).
+template <typename KVT, int NT = 1>
 struct AttnSmem {
     static constexpr int row_bytes = HD * (int)sizeof(KVT);
     static constexpr int slot_bytes = 2 * ATT_SLOT * row_bytes;   // K rows then V rows
     static constexpr int ring_warp = ATT_NS * slot_bytes;
     static constexpr int ring_off = 0;
-    static constexpr int new_off = 8 * ring_warp;                 // K, V rows of the new position
-    static constexpr int q_off = new_off + 2 * row_bytes;         // float q[2][128] (scaled)
-    static constexpr int wpart_off = q_off + 2 * HD * 4;          // float [8][ATT_PART]
-    static constexpr int cpart_off = wpart_off + 8 * ATT_PART * 4;  // float [8 cluster ranks][ATT_PART]
-    static constexpr int bars_off = cpart_off + 8 * ATT_PART * 4;
+    static constexpr int new_off = 8 * ring_warp;                 // K rows, then V rows, of the new positions
+    static constexpr int q_off = new_off + 2 * NT * row_bytes;    // float q[NT][2][128] (scaled)
+    static constexpr int wpart_off = q_off + NT * 2 * HD * 4;     // float [8 warps][NT][ATT_PART]
+    static constexpr int cpart_off = wpart_off + 8 * NT * ATT_PART * 4;  // float [8 cluster ranks][NT][ATT_PART]
+    static constexpr int bars_off = cpart_off + 8 * NT * ATT_PART * 4;
     static constexpr int total = bars_off + 8 * ATT_NS * 8;
 };
 
@@ -154,15 +155,19 @@ struct AttnAcc {
 
 // One block of up to 16 cache rows (rows [0, n) of a slot whose first row is position r0) with
 // tensor-core QK^T and PV.  Row addresses past n are clamped to row n-1 (finite data, p = 0).
+// Two-token passes (two = true): columns 4..7 are the second token's, which sees n1 >= n rows of
+// the block (the causal mask of the pass's own new rows); lanes t = 2, 3 track it.
 template <typename KVT>
 __device__ __forceinline__ void attn_block(uint32_t kslot, uint32_t vslot, int r0, int n, const uint32_t (&qb)[8][2],
-                                           AttnAcc& acc, int lane) {
+                                           AttnAcc& acc, int lane, bool two = false, int n1 = 0) {
     constexpr int RB = HD * (int)sizeof(KVT);
     const int g = lane >> 2, t = lane & 3;
+    const int nv = (two && t >= 2) ? n1 : n;  // rows this lane's column may see
+    const int nmax = two ? n1 : n;
     // ---- scores S[16 rows][cols: h0 hi, h0 lo, h1 hi, h1 lo, dup x4] ----
     float d[4] = {0.f, 0.f, 0.f, 0.f};
     {
-        const int row = min((lane & 7) + ((lane >> 3) & 1) * 8, n - 1);
+        const int row = min((lane & 7) + ((lane >> 3) & 1) * 8, nmax - 1);
         const int key = (r0 + row) & 7;
         const uint32_t rowaddr = kslot + row * RB;
 #pragma unroll
@@ -173,7 +178,7 @@ __device__ __forceinline__ void attn_block(uint32_t kslot, uint32_t vslot, int r
             mma_kv<KVT>(d, a, qb[kk][0], qb[kk][1]);
         }
     }
-    const bool va = g < n, vb = g + 8 < n;
+    const bool va = g < nv, vb = g + 8 < nv;
     const float sa = va ? d[0] + d[1] : -INFINITY;
     const float sb = vb ? d[2] + d[3] : -INFINITY;
     float mb = fmaxf(sa, sb);
@@ -187,7 +192,7 @@ __device__ __forceinline__ void attn_block(uint32_t kslot, uint32_t vslot, int r
     acc.m = mn;
     acc.l = fmaf(acc.l, corr, pa + pb);
     // ---- P as the B operand: lane (g, t) needs rows 2t, 2t+1, 2t+8, 2t+9 of column g ----
-    const int hh = (g >> 1) & 1, part = g & 1;
+    const int hh = two ? g >> 1 : (g >> 1) & 1, part = g & 1;  // column g -> lane t' = hh holds its scores
     const int src0 = (2 * t) * 4 + hh, src1 = (2 * t + 1) * 4 + hh;
     const float p0 = __shfl_sync(0xffffffffu, pa, src0);
     const float p1 = __shfl_sync(0xffffffffu, pa, src1);
@@ -199,7 +204,7 @@ __device__ __forceinline__ void attn_block(uint32_t kslot, uint32_t vslot, int r
     const float c = corr;
     // ---- O[16 dims x 8 cols] += V^T[dims x rows] P[rows x cols], 8 blocks of 16 dims ----
     {
-        const int row = min((lane & 7) + ((lane >> 4) & 1) * 8, n - 1);
+        const int row = min((lane & 7) + ((lane >> 4) & 1) * 8, nmax - 1);
         const int key = (r0 + row) & 7;
         const uint32_t rowaddr = vslot + row * RB;
 #pragma unroll
@@ -214,10 +219,15 @@ __device__ __forceinline__ void attn_block(uint32_t kslot, uint32_t vslot, int r
     }
 }
 
-template <typename KVT>
+// DUAL: the kernel of the grammar-commit engines, whose passes may carry two tokens
+// (DevState::n_tok) at positions pos and pos + 1: both are normalised, rotated and appended, the
+// second token's queries take MMA columns 4..7 next to the first's, so every K/V byte is still read
+// once, and each token writes its own parts (token 1 after token 0's).
+template <typename KVT, bool DUAL = false>
 __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KVT> p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    using S = AttnSmem<KVT>;
+    using S = AttnSmem<KVT, DUAL ? 2 : 1>;
+    constexpr int NTK = DUAL ? 2 : 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int NSP = p.n_split;
     const int h = blockIdx.x / NSP, j = blockIdx.x % NSP;
@@ -233,12 +243,15 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
     float* qs = reinterpret_cast<float*>(smem + S::q_off);
     float* wpart = reinterpret_cast<float*>(smem + S::wpart_off);
     float* cpart = reinterpret_cast<float*>(smem + S::cpart_off);
-    KVT* knew = reinterpret_cast<KVT*>(smem + S::new_off);
-    KVT* vnew = knew + HD;
+    KVT* knew = reinterpret_cast<KVT*>(smem + S::new_off);  // [NTK][HD]
+    KVT* vnew = knew + NTK * HD;                              // [NTK][HD]
 
-    // The cache position was written by a kernel at least two launches earlier (the commit or
-    // the prompt cursor advance of the previous step), so it can be read before the wait.
+    // The cache position (and the pass's token count) was written by a kernel at least two launches
+    // earlier (the commit or the prompt cursor advance of the previous step), so it can be read
+    // before the wait.
     const int pos = *(volatile int*)&st->pos;
+    const int ntok = DUAL ? *(volatile int*)&st->n_tok : 1;
+    const bool two = DUAL && ntok == 2;
     const long long Ls = pos;
     const int p0 = (int)(Ls * j / NSP), p1 = (int)(Ls * (j + 1) / NSP);
     const int a = p0 + (int)((long long)(p1 - p0) * warp / 8), b = p0 + (int)((long long)(p1 - p0) * (warp + 1) / 8);
@@ -263,13 +276,16 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
     }
     if (tid == 32) l2_prefetch_plan(p.l2, pos);
     // norm weights and this position's rotation are inputs that do not depend on the producer
+    // warps 0..3 prepare token 0 (q heads 2h, 2h+1, k, v), warps 4..7 token 1 of a 2-token pass
+    const int role = warp & 3, tk = warp >> 2;
+    const bool prep = warp < 4 || two;
     float nw[4] = {1.f, 1.f, 1.f, 1.f};
     float2 cs4[4];
-    if (warp < 3) {
-        const float4 w4 = *reinterpret_cast<const float4*>((warp < 2 ? p.q_norm : p.k_norm) + 4 * lane);
+    if (prep && role < 3) {
+        const float4 w4 = *reinterpret_cast<const float4*>((role < 2 ? p.q_norm : p.k_norm) + 4 * lane);
         nw[0] = w4.x; nw[1] = w4.y; nw[2] = w4.z; nw[3] = w4.w;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) cs4[e] = rope[(long long)pos * 64 + 4 * (lane & 15) + e];
+        for (int e = 0; e < 4; ++e) cs4[e] = rope[(long long)(pos + tk) * 64 + 4 * (lane & 15) + e];
     }
     __syncwarp();
 
@@ -285,11 +301,12 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
     cluster_arrive_relaxed();  // every CTA of the cluster has started (waited on before the push)
 
     // ---- q/k norm + RoPE for the new position: warp 0/1 -> q heads 2h, 2h+1, warp 2 -> k, 3 -> v ----
-    if (warp < 4) {
-        const int base = warp < 2 ? (2 * h + warp) * HD : (warp == 2 ? 2048 + h * HD : 3072 + h * HD);
-        const float4 x4 = *reinterpret_cast<const float4*>(qkv + base + 4 * lane);
+    if (prep) {
+        const int base = role < 2 ? (2 * h + role) * HD : (role == 2 ? 2048 + h * HD : 3072 + h * HD);
+        const int tpos = pos + tk;
+        const float4 x4 = *reinterpret_cast<const float4*>(qkv + tk * QKV_ROWS + base + 4 * lane);
         float x[4] = {x4.x, x4.y, x4.z, x4.w};
-        if (warp < 3) {
+        if (role < 3) {
             const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
             const float r = 1.0f / sqrtf(ss / (float)HD + EPS);
             float y[4];
@@ -301,24 +318,25 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
                 const float2 cs = cs4[e];
                 y[e] = lane < 16 ? x[e] * cs.x - partner * cs.y : x[e] * cs.x + partner * cs.y;
             }
-            if (warp < 2) {
+            if (role < 2) {
                 const float sc = 0.08838834764831845f;  // 1 / sqrt(128)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) qs[warp * HD + 4 * lane + e] = y[e] * sc;
+                for (int e = 0; e < 4; ++e) qs[(tk * 2 + role) * HD + 4 * lane + e] = y[e] * sc;
             } else {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) knew[kv_swz(4 * lane + e, pos)] = float_to_kv<KVT>(y[e]);
+                for (int e = 0; e < 4; ++e) knew[tk * HD + kv_swz(4 * lane + e, tpos)] = float_to_kv<KVT>(y[e]);
             }
         } else {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) vnew[kv_swz(4 * lane + e, pos)] = float_to_kv<KVT>(x[e]);
+            for (int e = 0; e < 4; ++e) vnew[tk * HD + kv_swz(4 * lane + e, tpos)] = float_to_kv<KVT>(x[e]);
         }
     }
     __syncthreads();
     pdl_launch_dependents();  // after the latency-bound q/k/v loads
-    if (j == 0 && tid < HD) {  // append the new row (already in the swizzled order)
-        kc[((long long)h * p.max_ctx + pos) * HD + tid] = knew[tid];
-        vc[((long long)h * p.max_ctx + pos) * HD + tid] = vnew[tid];
+    if (j == 0 && tid < ntok * HD) {  // append the new row(s) (already in the swizzled order)
+        const int r = tid >> 7, d = tid & 127;
+        kc[((long long)h * p.max_ctx + pos + r) * HD + d] = knew[r * HD + d];
+        vc[((long long)h * p.max_ctx + pos + r) * HD + d] = vnew[r * HD + d];
     }
 
     // ---- per-warp flash-decode over rows [a, b) ------------------------------------------------
@@ -327,7 +345,7 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
     uint32_t qb[8][2];
     {
         const int g = lane >> 2, t = lane & 3;
-        const int hh = (g >> 1) & 1, part = g & 1;
+        const int hh = two ? g >> 1 : (g >> 1) & 1, part = g & 1;  // two tokens: (token, head) = (hh >> 1, hh & 1)
         const float* q = qs + hh * HD;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
@@ -351,88 +369,103 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
         }
         const uint32_t kslot = smem_u32(ring + slot * S::slot_bytes);
         const int r0 = a + c * ATT_SLOT;
-        attn_block<KVT>(kslot, kslot + ATT_SLOT * S::row_bytes, r0, min(ATT_SLOT, b - r0), qb, acc, lane);
+        const int nr = min(ATT_SLOT, b - r0);
+        attn_block<KVT>(kslot, kslot + ATT_SLOT * S::row_bytes, r0, nr, qb, acc, lane, two, nr);
         __syncwarp();
         if (lane == 0 && c + ATT_NS < n_chunks) {
             fence_proxy_async_smem();
             issue(c + ATT_NS);
         }
     }
-    if (j == NSP - 1 && warp == 7) {
+    if (j == NSP - 1 && warp == 7) {  // the new row(s): token 0 sees row pos, token 1 rows pos, pos + 1
         const uint32_t kn = smem_u32(knew);
-        attn_block<KVT>(kn, kn + S::row_bytes, pos, 1, qb, acc, lane);
+        attn_block<KVT>(kn, kn + NTK * S::row_bytes, pos, 1, qb, acc, lane, two, ntok);
     }
 
-    // warp result: lanes with t = 0 / 1 own head 0 / 1
+    // warp result: lanes with t = 0 / 1 own head 0 / 1 of token 0, t = 2 / 3 those of token 1
     {
         const int g = lane >> 2, t = lane & 3;
         float l = acc.l;
         l += __shfl_xor_sync(0xffffffffu, l, 4);
         l += __shfl_xor_sync(0xffffffffu, l, 8);
         l += __shfl_xor_sync(0xffffffffu, l, 16);
-        float* wp = wpart + warp * ATT_PART;
-        if (t < 2) {
+        const int hw = t & 1;
+        float* wp = wpart + (warp * NTK + (t >> 1)) * ATT_PART;
+        if (t < 2 * ntok) {
 #pragma unroll
             for (int db = 0; db < 8; ++db) {
-                wp[4 + t * HD + 16 * db + g] = acc.o[db][0] + acc.o[db][1];
-                wp[4 + t * HD + 16 * db + g + 8] = acc.o[db][2] + acc.o[db][3];
+                wp[4 + hw * HD + 16 * db + g] = acc.o[db][0] + acc.o[db][1];
+                wp[4 + hw * HD + 16 * db + g + 8] = acc.o[db][2] + acc.o[db][3];
             }
             if (g == 0) {
-                wp[t] = acc.m;
-                wp[2 + t] = l;
+                wp[hw] = acc.m;
+                wp[2 + hw] = l;
             }
         }
     }
     __syncthreads();
-    // CTA combine of the 8 warps: thread (hh, d)
-    {
-        const int hh = tid >> 7, d = tid & 127;
-        float M = -INFINITY;
+    // CTA combine of the 8 warps: thread (hh, d), per token
+    const int hh = tid >> 7, d = tid & 127;
+    float Mt[NTK], Lt[NTK], Ot[NTK];
 #pragma unroll
-        for (int w2 = 0; w2 < 8; ++w2) M = fmaxf(M, wpart[w2 * ATT_PART + hh]);
-        float Lsum = 0.f, O = 0.f;
+    for (int q = 0; q < NTK; ++q) {
+        Mt[q] = -INFINITY;
+        Lt[q] = Ot[q] = 0.f;
+        if (q >= ntok) continue;
+#pragma unroll
+        for (int w2 = 0; w2 < 8; ++w2) Mt[q] = fmaxf(Mt[q], wpart[(w2 * NTK + q) * ATT_PART + hh]);
 #pragma unroll
         for (int w2 = 0; w2 < 8; ++w2) {
-            const float mw = wpart[w2 * ATT_PART + hh];
-            const float f = (mw == -INFINITY) ? 0.f : expf(mw - M);
-            Lsum = fmaf(wpart[w2 * ATT_PART + 2 + hh], f, Lsum);
-            O = fmaf(wpart[w2 * ATT_PART + 4 + hh * HD + d], f, O);
+            const float* wq = wpart + (w2 * NTK + q) * ATT_PART;
+            const float mw = wq[hh];
+            const float f = (mw == -INFINITY) ? 0.f : expf(mw - Mt[q]);
+            Lt[q] = fmaf(wq[2 + hh], f, Lt[q]);
+            Ot[q] = fmaf(wq[4 + hh * HD + d], f, Ot[q]);
         }
-        // push this CTA's part into slot `rank` of the cluster leader's (rank 0) shared memory
-        cluster_wait();
+    }
+    // push this CTA's part(s) into slot `rank` of the cluster leader's (rank 0) shared memory
+    cluster_wait();
+    {
         const uint32_t rank = cluster_ctarank();
-        float* slot = cpart + rank * ATT_PART;
-        st_dsmem(&slot[4 + hh * HD + d], 0, O);
-        if (d == 0) {
-            st_dsmem(&slot[hh], 0, M);
-            st_dsmem(&slot[2 + hh], 0, Lsum);
+#pragma unroll
+        for (int q = 0; q < NTK; ++q) {
+            if (q >= ntok) continue;
+            float* slot = cpart + (rank * NTK + q) * ATT_PART;
+            st_dsmem(&slot[4 + hh * HD + d], 0, Ot[q]);
+            if (d == 0) {
+                st_dsmem(&slot[hh], 0, Mt[q]);
+                st_dsmem(&slot[2 + hh], 0, Lt[q]);
+            }
         }
     }
     // one cluster barrier: the pushes (release) are visible to the leader (acquire); the other
     // CTAs are done, since nobody reads their shared memory
     cluster_sync_all();
     if (cluster_ctarank() != 0) return;
-    {
-        const int CL = p.cluster;
-        const int hh = tid >> 7, d = tid & 127;
+    const int CL = p.cluster;
+#pragma unroll
+    for (int tq = 0; tq < NTK; ++tq) {
+        if (tq >= ntok) continue;
         float M = -INFINITY;
 #pragma unroll
         for (int q = 0; q < 8; ++q)
-            if (q < CL) M = fmaxf(M, cpart[q * ATT_PART + hh]);
+            if (q < CL) M = fmaxf(M, cpart[(q * NTK + tq) * ATT_PART + hh]);
         float Lsum = 0.f, O = 0.f;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
             if (q < CL) {
-                const float mq = cpart[q * ATT_PART + hh];
+                const float* cq = cpart + (q * NTK + tq) * ATT_PART;
+                const float mq = cq[hh];
                 const float f = (mq == -INFINITY) ? 0.f : expf(mq - M);
-                Lsum = fmaf(cpart[q * ATT_PART + 2 + hh], f, Lsum);
-                O = fmaf(cpart[q * ATT_PART + 4 + hh * HD + d], f, O);
+                Lsum = fmaf(cq[2 + hh], f, Lsum);
+                O = fmaf(cq[4 + hh * HD + d], f, O);
             }
         }
         if (p.out16 != nullptr) {
             p.out16[(size_t)row * H + (2 * h + hh) * HD + d] = __float2half_rn(O / Lsum);
         } else {
-            float* out = p.part + ((long long)h * (NSP / CL) + j / CL) * ATT_PART;
+            // token tq's parts follow token 0's ([NTK][NKV][parts][ATT_PART])
+            float* out = p.part + ((long long)(tq * NKV + h) * (NSP / CL) + j / CL) * ATT_PART;
             out[4 + hh * HD + d] = O;
             if (d == 0) {
                 out[hh] = M;

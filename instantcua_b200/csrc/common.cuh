@@ -49,8 +49,31 @@ struct DevState {
     int write_logits; // lm_head also stores fp32 logits when set
     int error;        // bit flags set by bounded waits that gave up
     int session;
-    int pad[1];
+    int n_tok;        // tokens of the current decode pass: 2 after a grammar-forced pair, else 1
+    int cur_token2;   // second input token of a 2-token pass (the forced syntax token)
+    int grammar;      // grammar-guided 2-token commit applies to this call's commits
 };
+
+// Grammar-guided 2-token commit (reference k_commit, Shaders.swift:1497-1571).  After the greedy
+// token `tok` is committed as output number `step` (1-based), a deterministic syntax token follows
+// it: `open` after one of the `action` tokens when it is the call's first output, `space` after
+// `comma`; the next pass then runs both tokens through the model with one weight read.  `close`
+// ends the call.  The reference's ids (its Qwen tokenizer: 7 '(', 8 ')', 11 ',', 220 ' ' and eight
+// action words) are the defaults; tests substitute ids of a small vocabulary.
+struct GrammarRule {
+    int n_action;
+    int action[8];
+    int comma, space, open, close;
+};
+
+// The forced token after committing `tok` as output `step`, or -1.
+__host__ __device__ inline int grammar_syntax(const GrammarRule& r, int tok, int step) {
+    if (tok == r.comma) return r.space;
+    if (step == 1)
+        for (int i = 0; i < r.n_action && i < 8; ++i)
+            if (tok == r.action[i]) return r.open;
+    return -1;
+}
 
 // ---------------------------------------------------------------------------------------------
 // inline PTX helpers

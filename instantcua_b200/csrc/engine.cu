@@ -58,6 +58,8 @@ struct Matrix {
     bool stream = false;      // streaming (ring) path; otherwise all tiles of a CTA in one copy
     int n_slots = 1, chunk = 1;
     size_t smem = 0;
+    int n_slots2 = 1;  // ring depth and shared memory of the two-token (grammar-commit) kernels
+    size_t smem2 = 0;
 };
 
 struct Layer {
@@ -114,6 +116,9 @@ struct icua_engine {
     std::vector<void*> allocations;
     int eos0 = 151645, eos1 = 151643, stop_on_eos = 1;
     int prefix_cache = 1;  // reference Engine.usePrefixCache (Engine.swift:40), on by default
+    // grammar-guided 2-token commit (reference k_commit): off unless icua_set_grammar_commit
+    bool grammar = false;
+    GrammarRule rule{8, {3678, 7241, 12476, 10855, 11862, 1339, 1472, 24769}, 11, 220, 7, 8};
     icua_timing timing{};
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     float inv_freq[64];
@@ -190,21 +195,26 @@ void setup_matrix(Matrix& m, int fmt, int n_rows, int k, int n_sm) {
     const int tpc = gemv_tiles_per_cta(m.n_tiles, m.grid);
     const int nw = fmt_slices(fmt), ku = k / 64 / nw;
     m.stream = fmt == FMT_Q8 || tpc > SMALL_MAX_TILES;  // q8 kernels are built for the streaming path only
-    m.chunk = m.stream ? 1 : tpc;
+    // streaming chunk: tiles per bulk copy.  Each copy request has a fixed cost in the copy engine,
+    // so the q8 lm_head moves two tiles (8.7 KB) per request
+    m.chunk = !m.stream ? tpc : (fmt == FMT_Q8 && k <= 2048 ? 2 : 1);
     // streaming ring depth: up to 4 tiles per warp in flight (~140 KB per SM for the q8 lm_head,
     // enough to cover HBM latency at full bandwidth), as many as fit next to the input vector and
     // the RMSNorm weights
-    m.n_slots = 1;
-    for (int ns : {4, 2, 1}) {
-        if (!m.stream && ns > 1) continue;
-        GemvSmem L{k, nw, ns, m.chunk, unit_bytes(fmt), ku, tpc, 0};
-        if ((size_t)L.total() + (size_t)k * 4 <= 216 * 1024) {
-            m.n_slots = ns;
-            break;
+    for (int ntok : {1, 2}) {
+        int& slots = ntok == 1 ? m.n_slots : m.n_slots2;
+        slots = 1;
+        for (int ns : {4, 2, 1}) {
+            if (!m.stream && ns > 1) continue;
+            GemvSmem L{k, nw, ns, m.chunk, unit_bytes(fmt), ku, tpc, 0, ntok};
+            if ((size_t)L.total() + (size_t)k * 4 <= 216 * 1024) {
+                slots = ns;
+                break;
+            }
         }
+        GemvSmem L{k, nw, slots, m.chunk, unit_bytes(fmt), ku, tpc, 0, ntok};
+        (ntok == 1 ? m.smem : m.smem2) = (size_t)L.total();  // without the RMSNorm weight copy; launch_gemv adds it
     }
-    GemvSmem L{k, nw, m.n_slots, m.chunk, unit_bytes(fmt), ku, tpc, 0};
-    m.smem = (size_t)L.total();  // without the RMSNorm weight copy; launch_gemv adds it
 }
 
 template <typename Kern, typename... A>
@@ -241,12 +251,15 @@ cudaError_t launch_cluster(Kern kernel, int grid, int cluster, int block, size_t
     return cudaLaunchKernelEx(&cfg, kernel, params);
 }
 
-template <int FMT, int EPI, int KMAX, bool STREAM, int IN>
+template <int FMT, int EPI, int KMAX, bool STREAM, int IN, bool DUAL = false>
 cudaError_t launch_gemv(const Matrix& m, const GemvParams& p, cudaStream_t s, bool pdl = true) {
     const int nt = fmt_slices(FMT) * 32;
-    const size_t smem = m.smem + (p.norm_w != nullptr ? (size_t)m.k * 4 : 0);
+    constexpr bool two = DUAL && EPI != EPI_LOGITS;  // the lm_head of a 2-token pass reads one row
+    const size_t smem = (two ? m.smem2 : m.smem) + (p.norm_w != nullptr ? (size_t)m.k * 4 : 0);
     if (m.stream != STREAM || p.in_mode != IN) return cudaErrorInvalidValue;
-    return launch(gemv_kernel<FMT, EPI, KMAX, STREAM, IN>, m.grid, nt, smem, s, pdl, p);
+    GemvParams q = p;
+    if (two) q.n_slots = m.n_slots2;
+    return launch(gemv_kernel<FMT, EPI, KMAX, STREAM, IN, DUAL>, m.grid, nt, smem, s, pdl, q);
 }
 
 // ---- tensor-core GEMM launch ------------------------------------------------------------------
@@ -435,6 +448,27 @@ cudaError_t set_smem_attrs() {
     SETA((gemv_kernel<FMT_Q4A, EPI_LOGITS, 2048, false, IN_F32>));
     SETA((attn_decode_kernel<__half>));
     SETA((attn_decode_kernel<__nv_bfloat16>));
+    // the two-token kernels of grammar-commit engines
+    SETA((gemv_kernel<FMT_Q4S, EPI_STORE, 2048, false, IN_F32, true>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_STORE, 2048, false, IN_EMBED, true>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_RESID, 2048, false, IN_ATTN, true>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_SWIGLU, 2048, false, IN_F32, true>));
+    SETA((gemv_kernel<FMT_Q4S, EPI_RESID, 6144, false, IN_F32, true>));
+    SETA((gemv_kernel<FMT_Q8, EPI_STORE, 2048, true, IN_F32, true>));
+    SETA((gemv_kernel<FMT_Q8, EPI_STORE, 2048, true, IN_EMBED, true>));
+    SETA((gemv_kernel<FMT_Q8, EPI_RESID, 2048, true, IN_ATTN, true>));
+    SETA((gemv_kernel<FMT_Q8, EPI_SWIGLU, 2048, true, IN_F32, true>));
+    SETA((gemv_kernel<FMT_Q8, EPI_RESID, 6144, true, IN_F32, true>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_STORE, 2048, false, IN_F32, true>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_STORE, 2048, false, IN_EMBED, true>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_RESID, 2048, false, IN_ATTN, true>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_SWIGLU, 2048, false, IN_F32, true>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_RESID, 6144, false, IN_F32, true>));
+    SETA((gemv_kernel<FMT_Q8, EPI_LOGITS, 2048, true, IN_F32, true>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_LOGITS, 2048, true, IN_F32, true>));
+    SETA((gemv_kernel<FMT_Q4A, EPI_LOGITS, 2048, false, IN_F32, true>));
+    SETA((attn_decode_kernel<__half, true>));
+    SETA((attn_decode_kernel<__nv_bfloat16, true>));
     SETA(commit_kernel);
     SETA(advance_kernel);
     SETA(argmax_parts_kernel);
@@ -504,14 +538,16 @@ L2Plan plan_kv(icua_engine* e, Session& S, int layer) {
 
 // Layer GEMV launch for the engine's weight format: q4s matrices run the whole-tile path, q8
 // matrices (reference FMT 1 files) the streaming path.
-template <int EPI, int KMAX, int IN>
+template <int EPI, int KMAX, int IN, bool DUAL = false>
 cudaError_t launch_layer_gemv(const icua_engine* e, const Matrix& m, const GemvParams& p, cudaStream_t s) {
-    if (m.fmt == FMT_Q8) return launch_gemv<FMT_Q8, EPI, KMAX, true, IN>(m, p, s);
-    if (m.fmt == FMT_Q4A) return launch_gemv<FMT_Q4A, EPI, KMAX, false, IN>(m, p, s);
-    return launch_gemv<FMT_Q4S, EPI, KMAX, false, IN>(m, p, s);
+    if (m.fmt == FMT_Q8) return launch_gemv<FMT_Q8, EPI, KMAX, true, IN, DUAL>(m, p, s);
+    if (m.fmt == FMT_Q4A) return launch_gemv<FMT_Q4A, EPI, KMAX, false, IN, DUAL>(m, p, s);
+    return launch_gemv<FMT_Q4S, EPI, KMAX, false, IN, DUAL>(m, p, s);
 }
 
-cudaError_t record_layers(icua_engine* e, Session& S) {
+// DUAL: the kernels of grammar-commit engines (passes of one or two tokens).
+template <bool DUAL>
+cudaError_t record_layers_t(icua_engine* e, Session& S) {
     cudaError_t err;
     const int L = e->cfg.n_layers;
     for (int l = 0; l < L; ++l) {
@@ -528,8 +564,8 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.out = e->qkv;
         p.st = S.st;
         p.l2 = plan_weights(ly.o);
-        err = (l == 0) ? launch_layer_gemv<EPI_STORE, 2048, IN_EMBED>(e, ly.qkv, p, e->stream)
-                       : launch_layer_gemv<EPI_STORE, 2048, IN_F32>(e, ly.qkv, p, e->stream);
+        err = (l == 0) ? launch_layer_gemv<EPI_STORE, 2048, IN_EMBED, DUAL>(e, ly.qkv, p, e->stream)
+                       : launch_layer_gemv<EPI_STORE, 2048, IN_F32, DUAL>(e, ly.qkv, p, e->stream);
         if (err != cudaSuccess) return err;
         // 2. QK norm + RoPE + KV append + split-K attention (clusters combine the splits)
         const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
@@ -547,8 +583,8 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
             a.part = e->att_part;
             a.st = S.st;
             a.l2 = plan_weights(ly.gu);
-            err = launch_cluster(attn_decode_kernel<__nv_bfloat16>, NKV * e->att_split, e->att_cluster, 256,
-                                 AttnSmem<__nv_bfloat16>::total, e->stream, a);
+            err = launch_cluster(attn_decode_kernel<__nv_bfloat16, DUAL>, NKV * e->att_split, e->att_cluster, 256,
+                                 AttnSmem<__nv_bfloat16, DUAL ? 2 : 1>::total, e->stream, a);
         } else {
             AttnParams<__half> a{};
             a.qkv = e->qkv;
@@ -563,8 +599,8 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
             a.part = e->att_part;
             a.st = S.st;
             a.l2 = plan_weights(ly.gu);
-            err = launch_cluster(attn_decode_kernel<__half>, NKV * e->att_split, e->att_cluster, 256,
-                                 AttnSmem<__half>::total, e->stream, a);
+            err = launch_cluster(attn_decode_kernel<__half, DUAL>, NKV * e->att_split, e->att_cluster, 256,
+                                 AttnSmem<__half, DUAL ? 2 : 1>::total, e->stream, a);
         }
         if (err != cudaSuccess) return err;
         // 3. o-proj + residual
@@ -575,7 +611,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.x_resid = e->x;
         p.st = S.st;
         p.l2 = plan_weights(ly.d);
-        if ((err = launch_layer_gemv<EPI_RESID, 2048, IN_ATTN>(e, ly.o, p, e->stream)) != cudaSuccess) return err;
+        if ((err = launch_layer_gemv<EPI_RESID, 2048, IN_ATTN, DUAL>(e, ly.o, p, e->stream)) != cudaSuccess) return err;
         // 4. RMSNorm + gate/up + SwiGLU
         p = base_params(e, ly.gu);
         p.in_mode = IN_F32;
@@ -584,7 +620,7 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.out = e->h;
         p.st = S.st;
         if (l + 1 < L) p.l2 = plan_weights(e->layers[l + 1].qkv);
-        if ((err = launch_layer_gemv<EPI_SWIGLU, 2048, IN_F32>(e, ly.gu, p, e->stream)) != cudaSuccess) return err;
+        if ((err = launch_layer_gemv<EPI_SWIGLU, 2048, IN_F32, DUAL>(e, ly.gu, p, e->stream)) != cudaSuccess) return err;
         // 5. down + residual (+ DeepStack rows after layers 0..2 while prefilling visual rows)
         p = base_params(e, ly.d);
         p.in_mode = IN_F32;
@@ -593,9 +629,13 @@ cudaError_t record_layers(icua_engine* e, Session& S) {
         p.deepstack = (l < 3) ? e->deepstack[l] : nullptr;
         p.st = S.st;
         p.l2 = (l + 1 < L) ? plan_kv(e, S, l + 1) : plan_weights(e->embed);
-        if ((err = launch_layer_gemv<EPI_RESID, 6144, IN_F32>(e, ly.d, p, e->stream)) != cudaSuccess) return err;
+        if ((err = launch_layer_gemv<EPI_RESID, 6144, IN_F32, DUAL>(e, ly.d, p, e->stream)) != cudaSuccess) return err;
     }
     return cudaSuccess;
+}
+
+cudaError_t record_layers(icua_engine* e, Session& S) {
+    return e->grammar ? record_layers_t<true>(e, S) : record_layers_t<false>(e, S);
 }
 
 cudaError_t record_head(icua_engine* e, Session& S) {
@@ -608,13 +648,22 @@ cudaError_t record_head(icua_engine* e, Session& S) {
     p.cta_best_i = e->cta_best_i;
     p.step_logits = e->step_logits;
     p.st = S.st;
-    // q8 heads always stream; a q4a head streams unless the vocabulary is small (tests)
-    cudaError_t err = e->embed.fmt != FMT_Q4A ? launch_gemv<FMT_Q8, EPI_LOGITS, 2048, true, IN_F32>(e->embed, p, e->stream)
-                      : e->embed.stream       ? launch_gemv<FMT_Q4A, EPI_LOGITS, 2048, true, IN_F32>(e->embed, p, e->stream)
-                                              : launch_gemv<FMT_Q4A, EPI_LOGITS, 2048, false, IN_F32>(e->embed, p, e->stream);
+    // q8 heads always stream; a q4a head streams unless the vocabulary is small (tests).  Grammar
+    // engines' heads read the last row of the pass.
+    cudaError_t err;
+    if (e->grammar)
+        err = e->embed.fmt != FMT_Q4A ? launch_gemv<FMT_Q8, EPI_LOGITS, 2048, true, IN_F32, true>(e->embed, p, e->stream)
+              : e->embed.stream       ? launch_gemv<FMT_Q4A, EPI_LOGITS, 2048, true, IN_F32, true>(e->embed, p, e->stream)
+                                      : launch_gemv<FMT_Q4A, EPI_LOGITS, 2048, false, IN_F32, true>(e->embed, p, e->stream);
+    else
+        err = e->embed.fmt != FMT_Q4A ? launch_gemv<FMT_Q8, EPI_LOGITS, 2048, true, IN_F32>(e->embed, p, e->stream)
+              : e->embed.stream       ? launch_gemv<FMT_Q4A, EPI_LOGITS, 2048, true, IN_F32>(e->embed, p, e->stream)
+                                      : launch_gemv<FMT_Q4A, EPI_LOGITS, 2048, false, IN_F32>(e->embed, p, e->stream);
     if (err != cudaSuccess) return err;
+    GrammarRule rule = e->rule;
+    if (!e->grammar) rule.n_action = -1;  // the commit never applies the rule
     return launch(commit_kernel, 1, 256, 0, e->stream, true, (const float*)e->cta_best_v, (const int*)e->cta_best_i,
-                  e->embed.grid, S.out_tokens, S.st);
+                  e->embed.grid, S.out_tokens, S.st, rule);
 }
 
 icua_status build_graph(icua_engine* eng, Session& S, int kind, cudaGraphExec_t* out) {
@@ -1184,14 +1233,15 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
     }
     for (int i = 0; i < 4; ++i) cudaEventCreate(&eng->ev[i]);
     eng->layers.resize(cfg->n_layers);
-    TRY(dalloc_t(eng, &eng->x, H));
-    TRY(dalloc_t(eng, &eng->qkv, QKV_ROWS));
+    // two rows: a grammar-commit pass may carry two tokens
+    TRY(dalloc_t(eng, &eng->x, 2 * H));
+    TRY(dalloc_t(eng, &eng->qkv, 2 * QKV_ROWS));
     TRY(dalloc_t(eng, &eng->attn, H));
-    TRY(dalloc_t(eng, &eng->h, FF));
+    TRY(dalloc_t(eng, &eng->h, 2 * FF));
     TRY(dalloc_t(eng, &eng->logits, (size_t)cfg->vocab));
     TRY(dalloc_t(eng, &eng->pooler, (size_t)cfg->max_pass * H));
     for (int i = 0; i < 3; ++i) TRY(dalloc_t(eng, &eng->deepstack[i], (size_t)cfg->max_pass * H));
-    TRY(dalloc_t(eng, &eng->att_part, (size_t)NKV * eng->att_split * ATT_PART));
+    TRY(dalloc_t(eng, &eng->att_part, (size_t)2 * NKV * eng->att_split * ATT_PART));
     TRY(dalloc_t(eng, &eng->cta_best_v, (size_t)eng->n_sm));
     TRY(dalloc_t(eng, &eng->cta_best_i, (size_t)eng->n_sm));
     {
@@ -1363,6 +1413,36 @@ icua_status icua_set_prefix_cache(icua_engine* eng, int32_t enable) {
     return ICUA_OK;
 }
 
+icua_status icua_set_grammar_commit(icua_engine* eng, int32_t enable, const icua_grammar* rule) {
+    if (!eng) return fail(nullptr, ICUA_ERR_INVALID, "null engine");
+    if (enable && eng->cfg.format == ICUA_FMT_F16)
+        return fail(eng, ICUA_ERR_INVALID, "grammar commit runs on the batch-1 decode graphs of quantized engines");
+    GrammarRule r = eng->rule;
+    if (rule) {
+        if (rule->n_action < 0 || rule->n_action > 8) return fail(eng, ICUA_ERR_INVALID, "n_action %d", rule->n_action);
+        const int V = eng->cfg.vocab;
+        auto ok = [V](int t) { return t >= 0 && t < V; };
+        for (int i = 0; i < rule->n_action; ++i)
+            if (!ok(rule->action[i])) return fail(eng, ICUA_ERR_INVALID, "action id %d", rule->action[i]);
+        if (!ok(rule->comma) || !ok(rule->space) || !ok(rule->open) || !ok(rule->close))
+            return fail(eng, ICUA_ERR_INVALID, "syntax id outside the vocabulary");
+        r.n_action = rule->n_action;
+        for (int i = 0; i < 8; ++i) r.action[i] = i < rule->n_action ? rule->action[i] : -1;
+        r.comma = rule->comma;
+        r.space = rule->space;
+        r.open = rule->open;
+        r.close = rule->close;
+    } else if (enable && (r.space >= eng->cfg.vocab || r.open >= eng->cfg.vocab)) {
+        return fail(eng, ICUA_ERR_INVALID, "the reference's syntax ids need a vocabulary of %d", eng->cfg.vocab);
+    }
+    eng->rule = r;
+    eng->grammar = enable != 0;
+    // the session graphs hold the one- or two-token kernels and the rule (a kernel parameter)
+    CK(cudaSetDevice(eng->cfg.device));
+    for (Session& S : eng->sessions) drop_graphs(S);
+    return ICUA_OK;
+}
+
 static icua_status reset_session_impl(icua_engine* eng, int32_t session, bool keep_prefix) {
     if (!eng) return fail(nullptr, ICUA_ERR_INVALID, "null engine");
     Session* S = get_session(eng, session);
@@ -1379,6 +1459,7 @@ static icua_status reset_session_impl(icua_engine* eng, int32_t session, bool ke
     DevState hs{};
     hs.vis_offset = -1;
     hs.session = session;
+    hs.n_tok = 1;
     CK(cudaMemcpy(S->st, &hs, sizeof hs, cudaMemcpyHostToDevice));
     return ICUA_OK;
 }
@@ -1524,6 +1605,8 @@ static icua_status prepare_prefill(icua_engine* eng, Session& S, int session, co
     hs.n_vis = n_vis;
     hs.write_logits = write_logits ? 1 : 0;
     hs.session = session;
+    hs.n_tok = 1;
+    hs.grammar = eng->grammar ? 1 : 0;
     *vis_off_out = vis_off;
     *n_vis_out = n_vis;
     CK(cudaMemcpyAsync(S.st, &hs, sizeof hs, cudaMemcpyHostToDevice, eng->stream));
@@ -1639,8 +1722,33 @@ icua_status icua_decode(icua_engine* eng, int32_t session, int32_t max_new, int3
     if (S->pos + max_new + eng->cfg.steps_per_graph > eng->cfg.max_context)
         return fail(eng, ICUA_ERR_CAPACITY, "context %d + %d exceeds max_context", S->pos, max_new);
     const int ms_val = base_step + max_new, zero = 0;
-    CK(cudaMemcpyAsync(&S->st->max_steps, &ms_val, 4, cudaMemcpyHostToDevice, eng->stream));
-    CK(cudaMemcpyAsync(&S->st->done, &zero, 4, cudaMemcpyHostToDevice, eng->stream));
+    if (eng->grammar) {
+        // The commit that ended the previous call (the prefill's first token, or max_steps) did not
+        // apply the rule to its token: apply it now, as the reference's single loop would have.
+        DevState hs;
+        CK(cudaMemcpy(&hs, S->st, sizeof hs, cudaMemcpyDeviceToHost));
+        if (hs.n_tok != 2 && hs.cur_token == eng->rule.close) return ICUA_OK;  // ')' ended the output
+        hs.grammar = 1;
+        hs.max_steps = ms_val;
+        hs.done = 0;
+        if (hs.n_tok != 2) {
+            hs.n_tok = 1;
+            const int syn = grammar_syntax(eng->rule, hs.cur_token, hs.step);
+            if (syn >= 0) {
+                CK(cudaMemcpy(S->out_tokens + hs.step, &syn, 4, cudaMemcpyHostToDevice));
+                hs.step += 1;
+                hs.n_tok = 2;
+                hs.cur_token2 = syn;
+                if (hs.step >= ms_val) hs.done = 1;
+            }
+        }
+        // a pass of two tokens follows a commit of two outputs: positions still grow by at most
+        // one per output token, so the capacity check above holds
+        CK(cudaMemcpy(S->st, &hs, sizeof hs, cudaMemcpyHostToDevice));
+    } else {
+        CK(cudaMemcpyAsync(&S->st->max_steps, &ms_val, 4, cudaMemcpyHostToDevice, eng->stream));
+        CK(cudaMemcpyAsync(&S->st->done, &zero, 4, cudaMemcpyHostToDevice, eng->stream));
+    }
     const auto t0 = std::chrono::steady_clock::now();
     CK(cudaEventRecord(eng->ev[2], eng->stream));
     const int spg = eng->cfg.steps_per_graph;
@@ -1698,6 +1806,11 @@ icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token
     const int big = 1 << 30, one = 1;
     CK(cudaMemcpyAsync(&S->st->prompt_idx, &big, 4, cudaMemcpyHostToDevice, eng->stream));
     CK(cudaMemcpyAsync(&S->st->write_logits, &one, 4, cudaMemcpyHostToDevice, eng->stream));
+    if (eng->grammar) {
+        // caller-driven steps carry one token and never force one
+        static const int one_tok[3] = {1, 0, 0};  // n_tok, cur_token2, grammar
+        CK(cudaMemcpyAsync(&S->st->n_tok, one_tok, sizeof one_tok, cudaMemcpyHostToDevice, eng->stream));
+    }
     CK(cudaGraphLaunch(S->g_step1, eng->stream));
     CK(cudaMemcpyAsync(out_token, S->out_tokens + S->step, 4, cudaMemcpyDeviceToHost, eng->stream));
     CK(cudaStreamSynchronize(eng->stream));

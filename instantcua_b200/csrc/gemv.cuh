@@ -72,12 +72,15 @@ __host__ __device__ inline int gemv_tiles_per_cta(int n_tiles, int grid) { retur
 
 struct GemvSmem {
     int k, nw, n_slots, chunk, ub, ku, tiles_per_cta, has_norm;
-    __host__ __device__ int xfrag_bytes() const { return (k / 16) * 4 * 2 * 8; }
-    __host__ __device__ int xsum_off() const { return xfrag_bytes(); }
-    __host__ __device__ int red_off() const { return xsum_off() + (k / 32) * 4; }              // float[64]
+    int ntok = 1;  // input vectors held (2 in the kernels of the grammar-commit 2-token pass)
+    __host__ __device__ int xfrag_tok() const { return (k / 16) * 4 * 2 * 8; }  // bytes per input vector
+    __host__ __device__ int xfrag_bytes() const { return ntok * xfrag_tok(); }
+    __host__ __device__ int xsum_off() const { return xfrag_bytes(); }                       // float[ntok][k / 32]
+    __host__ __device__ int red_off() const { return xsum_off() + ntok * (k / 32) * 4; }     // float[64]
     __host__ __device__ int normw_off() const { return red_off() + 64 * 4; }                 // float[k] if has_norm
-    __host__ __device__ int part_off() const { return normw_off() + (has_norm ? k * 4 : 0); }  // float[tpc][nw][16]
-    __host__ __device__ int cnt_off() const { return part_off() + tiles_per_cta * nw * 16 * 4; }
+    __host__ __device__ int part_off() const { return normw_off() + (has_norm ? k * 4 : 0); }  // float[ntok][tpc][nw][16]
+    __host__ __device__ int part_tok() const { return tiles_per_cta * nw * 16; }             // floats per vector
+    __host__ __device__ int cnt_off() const { return part_off() + ntok * part_tok() * 4; }
     __host__ __device__ int bars_off() const { return (cnt_off() + tiles_per_cta * 4 + 15) & ~15; }  // + norm bar
     __host__ __device__ int ring_off() const { return ((bars_off() + (nw * n_slots + 1) * 8) + 127) & ~127; }
     __host__ __device__ int slot_bytes() const { return chunk * ku * ub; }
@@ -142,16 +145,19 @@ struct InputRegs {
 
 // Issues the input loads (independent) into registers.  IN_ATTN folds the attention parts of
 // the element's head (max, sum, output) with their softmax weights; IN_EMBED first reads the
-// prompt cursor (one extra round trip, layer 0 only).
+// prompt cursor (one extra round trip, layer 0 only).  `row` selects the input vector of a
+// 2-token pass (x row, attention parts or embedded token of that row).
 template <int KMAX, int NT, int IN>
-__device__ __forceinline__ void load_input(InputRegs<KMAX, NT>& r, const GemvParams& p) {
+__device__ __forceinline__ void load_input(InputRegs<KMAX, NT>& r, const GemvParams& p, int row = 0) {
     const int npairs = p.k / 4;
     const float* vis_row = nullptr;
     int tok = 0;
     if (IN == IN_EMBED) {
         const DevState* st = p.st;
         const int idx = st->prompt_idx;
-        if (idx < st->prompt_len) {
+        if (row == 1) {
+            tok = st->cur_token2;
+        } else if (idx < st->prompt_len) {
             tok = p.prompt[idx];
             const int v = idx - st->vis_offset;
             if (tok == IMAGE_PAD_ID && st->vis_offset >= 0 && p.pooler != nullptr && v >= 0 && v < st->n_vis)
@@ -166,7 +172,7 @@ __device__ __forceinline__ void load_input(InputRegs<KMAX, NT>& r, const GemvPar
         if (q >= npairs) continue;
         const int s = q >> 2, t = q & 3, k0 = s * 16 + 2 * t;
         if (IN == IN_F32) {
-            const float* x = reinterpret_cast<const float*>(p.x);
+            const float* x = reinterpret_cast<const float*>(p.x) + (long long)row * p.k;
             const float2 a = *reinterpret_cast<const float2*>(x + k0);
             const float2 b = *reinterpret_cast<const float2*>(x + k0 + 8);
             r.v[j][0] = a.x;
@@ -182,7 +188,7 @@ __device__ __forceinline__ void load_input(InputRegs<KMAX, NT>& r, const GemvPar
         } else if (IN == IN_ATTN) {
             // the four elements belong to one query head: fold its parts with a running max
             const int qh = k0 >> 7, h = qh >> 1, hh = qh & 1, P = p.att_parts;
-            const float* b = p.att_part + (long long)h * P * ATT_PART;
+            const float* b = p.att_part + ((long long)row * NKV + h) * P * ATT_PART;
             float M = -INFINITY, Ls = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
             for (int q2 = 0; q2 < P; ++q2) {
@@ -217,10 +223,10 @@ __device__ __forceinline__ void load_input(InputRegs<KMAX, NT>& r, const GemvPar
 // The RMSNorm weights were bulk-copied to shared memory before griddepcontrol.wait (nbar).
 template <int KMAX, int NT>
 __device__ __forceinline__ void store_input(const InputRegs<KMAX, NT>& r, const GemvParams& p, uint8_t* smem,
-                                            const GemvSmem& L, uint64_t* nbar) {
+                                            const GemvSmem& L, uint64_t* nbar, int row = 0) {
     const int tid = threadIdx.x, npairs = p.k / 4;
-    uint2* xfrag = reinterpret_cast<uint2*>(smem);
-    float* xsum = reinterpret_cast<float*>(smem + L.xsum_off());
+    uint2* xfrag = reinterpret_cast<uint2*>(smem + row * L.xfrag_tok());
+    float* xsum = reinterpret_cast<float*>(smem + L.xsum_off()) + row * (p.k / 32);
     float* red = reinterpret_cast<float*>(smem + L.red_off());
     const float* nws = reinterpret_cast<const float*>(smem + L.normw_off());
     float scale = 1.0f;
@@ -251,7 +257,7 @@ __device__ __forceinline__ void store_input(const InputRegs<KMAX, NT>& r, const 
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             float x = r.v[j][i];
-            if (p.in_mode == IN_EMBED && blockIdx.x == 0) p.x_resid[kk[i]] = x;  // layer 0 keeps the embedded row
+            if (p.in_mode == IN_EMBED && blockIdx.x == 0) p.x_resid[row * H + kk[i]] = x;  // layer 0 keeps the embedded row
             if (p.norm_w != nullptr) x = x * scale * nws[kk[i]];
             hi[i] = __float2half_rn(x);
             lo[i] = __float2half_rn(x - __half2float(hi[i]));
@@ -391,17 +397,24 @@ __device__ __forceinline__ void gemv_row_epilogue(const GemvParams& p, int r, fl
 }
 
 // ---------------------------------------------------------------------------------------------
-template <int FMT, int EPI, int KMAX, bool STREAM, int IN>
+// DUAL: the kernel of the grammar-commit engines.  A pass may carry two tokens (DevState::n_tok);
+// their input vectors take the B columns (tok0 hi, tok0 lo, tok1 hi, tok1 lo) x 2 of the same
+// MMAs, so both rows come out of one read of the weights (the reference's dot64_row2 branches,
+// Shaders.swift:529-595).  Lane (g, t) accumulates token t & 1.  The lm_head (EPI_LOGITS) reads
+// only the pass's last row.  With one token the columns repeat it and the arithmetic is that of
+// the single-token kernel.
+template <int FMT, int EPI, int KMAX, bool STREAM, int IN, bool DUAL = false>
 __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NW = fmt_slices(FMT), NT = NW * 32;
     constexpr int KU = KMAX / 64 / NW;  // units of a tile per warp at K = KMAX
+    constexpr bool TWO = DUAL && EPI != EPI_LOGITS;  // two output rows per pass possible
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tpc = gemv_tiles_per_cta(p.n_tiles, gridDim.x);
     const int ku = p.upt / NW;
     const int chunk = STREAM ? p.chunk : tpc;
     const int NS = STREAM ? p.n_slots : 1;
-    const GemvSmem L{p.k, NW, NS, chunk, unit_bytes(FMT), ku, tpc, p.norm_w != nullptr};
+    const GemvSmem L{p.k, NW, NS, chunk, unit_bytes(FMT), ku, tpc, p.norm_w != nullptr, TWO ? 2 : 1};
     const int UB = L.ub;
     const uint2* xfrag = reinterpret_cast<const uint2*>(smem);
     const float* xsum = reinterpret_cast<const float*>(smem + L.xsum_off());
@@ -445,9 +458,12 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
     if (!STREAM && EPI == EPI_RESID && (int)threadIdx.x < nt * 16) xold = p.x_resid[t_begin * 16 + threadIdx.x];
     __syncwarp();
 
+    // the lm_head of a 2-token pass reads its last row; n_tok was set by the previous step's commit
+    const int head_row = (DUAL && EPI == EPI_LOGITS && p.st != nullptr) ? *(volatile int*)&p.st->n_tok - 1 : 0;
     pdl_wait();
-    load_input<KMAX, NT, IN>(in, p);  // issued before the stop-flag read so neither waits on the other
+    load_input<KMAX, NT, IN>(in, p, head_row);  // issued before the stop-flag read so neither waits on the other
     const bool skip = (p.st != nullptr) && (*(volatile int*)&p.st->done != 0);
+    const int ntok = (TWO && p.st != nullptr) ? *(volatile int*)&p.st->n_tok : 1;
     if (skip) {
         pdl_launch_dependents();
         if (lane == 0)
@@ -470,10 +486,20 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
         }
     }
     store_input<KMAX, NT>(in, p, smem, L, nbar);  // ends with __syncthreads (also publishes cnt[] = 0)
+    if (TWO && ntok == 2) {
+        load_input<KMAX, NT, IN>(in, p, 1);
+        store_input<KMAX, NT>(in, p, smem, L, nbar, 1);
+    }
     // The next kernel's weight prefetch starts only now, so that it does not queue ahead of the
     // latency-bound input loads above.
     pdl_launch_dependents();
 
+    const int g = lane >> 2, t = lane & 3;
+    if (TWO && ntok == 2) {
+        // B column g holds token (g >> 1) & 1; this lane's accumulator columns 2t, 2t+1 token t & 1
+        xfrag += ((g >> 1) & 1) * (L.xfrag_tok() / 8);
+        xsum += (t & 1) * (p.k / 32);
+    }
     // the warp's K slice is the same for every tile: keep its constants in registers when small
     constexpr bool HOIST = KU <= 2;
     UnitConst<FMT> uc[HOIST ? KU : 1];
@@ -482,7 +508,6 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
         for (int u = 0; u < (HOIST ? KU : 1); ++u)
             if (u < ku) load_unit_const<FMT>(uc[u], warp * ku + u, xfrag, xsum, lane);
     }
-    const int g = lane >> 2, t = lane & 3;
     const float f1 = (FMT != FMT_Q8) ? 1048576.0f : 16777216.0f;
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
@@ -509,8 +534,8 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
         for (int j = 0; j < nt; ++j) {
             float acc0, acc1;
             tile_sum(ring + j * ku * UB, acc0, acc1);
-            if (t == 0) {
-                float* pt = part + (j * NW + warp) * 16;
+            if (t < (TWO ? ntok : 1)) {  // lane t = 0 (and t = 1 for the second token)
+                float* pt = part + (TWO ? t * L.part_tok() : 0) + (j * NW + warp) * 16;
                 pt[g] = acc0 * 16777216.0f;
                 pt[g + 8] = acc1 * f1;
             }
@@ -518,24 +543,33 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
         __syncthreads();
         // thread i finalises row i of the CTA: fixed-order sum over the K slices
         const int i = threadIdx.x;
-        if (EPI == EPI_SWIGLU) {
-            if (i < nt * 8) {
-                const int j = i >> 3, r8 = i & 7;
-                float gv = 0.f, uv = 0.f;
+        for (int tk = 0; tk < (TWO ? ntok : 1); ++tk) {
+            const float* pk = part + tk * L.part_tok();
+            if (EPI == EPI_SWIGLU) {
+                if (i < nt * 8) {
+                    const int j = i >> 3, r8 = i & 7;
+                    float gv = 0.f, uv = 0.f;
 #pragma unroll
-                for (int w2 = 0; w2 < NW; ++w2) {
-                    gv += part[(j * NW + w2) * 16 + r8];
-                    uv += part[(j * NW + w2) * 16 + 8 + r8];
+                    for (int w2 = 0; w2 < NW; ++w2) {
+                        gv += pk[(j * NW + w2) * 16 + r8];
+                        uv += pk[(j * NW + w2) * 16 + 8 + r8];
+                    }
+                    // tile rows 0..7 are gate units, rows 8..15 the matching up units
+                    p.out[tk * (p.n_rows / 2) + (t_begin + j) * 8 + r8] = (gv / (1.0f + expf(-gv))) * uv;
                 }
-                // tile rows 0..7 are gate units, rows 8..15 the matching up units
-                p.out[(t_begin + j) * 8 + r8] = (gv / (1.0f + expf(-gv))) * uv;
-            }
-        } else if (i < nt * 16) {
-            const int j = i >> 4, r = i & 15;
-            float v = 0.f;
+            } else if (i < nt * 16) {
+                const int j = i >> 4, r = i & 15;
+                float v = 0.f;
 #pragma unroll
-            for (int w2 = 0; w2 < NW; ++w2) v += part[(j * NW + w2) * 16 + r];
-            gemv_row_epilogue<EPI>(p, (t_begin + j) * 16 + r, v, xold, ds, write_logits, step, best_v, best_i);
+                for (int w2 = 0; w2 < NW; ++w2) v += pk[(j * NW + w2) * 16 + r];
+                const int row = (t_begin + j) * 16 + r;
+                if (TWO && tk == 1) {
+                    if (EPI == EPI_STORE) p.out[p.n_rows + row] = v;
+                    if (EPI == EPI_RESID) p.x_resid[p.n_rows + row] += v;
+                } else {
+                    gemv_row_epilogue<EPI>(p, row, v, xold, ds, write_logits, step, best_v, best_i);
+                }
+            }
         }
     } else {
         for (int c = 0; c < n_chunks; ++c) {
@@ -549,8 +583,8 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
                 const int j = c * chunk + jj;
                 float acc0, acc1;
                 tile_sum(ring + slot * L.slot_bytes() + jj * ku * UB, acc0, acc1);
-                float* pt = part + (j * NW + warp) * 16;
-                if (t == 0) {
+                if (t < (TWO ? ntok : 1)) {  // lane t = 0 (and t = 1 for the second token)
+                    float* pt = part + (TWO ? t * L.part_tok() : 0) + (j * NW + warp) * 16;
                     pt[g] = acc0 * 16777216.0f;
                     pt[g + 8] = acc1 * f1;
                 }
@@ -561,20 +595,23 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
                 prev = __shfl_sync(0xffffffffu, prev, 0);
                 if (prev == NW - 1) {  // this warp completed the tile: reduce the K slices in a fixed order
                     __threadfence_block();
-                    const int r = lane & 15;
+                    // lanes 0..15: rows of token 0; lanes 16..31: the same rows of token 1 (two-token kernels)
+                    const int r = lane & 15, tk = TWO ? lane >> 4 : 0;
+                    const float* pk = part + tk * L.part_tok();
                     float v = 0.f;
 #pragma unroll
-                    for (int w2 = 0; w2 < NW; ++w2) v += *(volatile float*)&part[(j * NW + w2) * 16 + r];
+                    for (int w2 = 0; w2 < NW; ++w2) v += *(volatile float*)&pk[(j * NW + w2) * 16 + r];
                     if (EPI == EPI_SWIGLU) {
                         // tile rows 0..7 are gate units, rows 8..15 the matching up units
                         const float uv = __shfl_down_sync(0xffffffffu, v, 8);
-                        if (lane < 8) p.out[(t_begin + j) * 8 + lane] = (v / (1.0f + expf(-v))) * uv;
-                    } else if (lane < 16) {
-                        const int row = (t_begin + j) * 16 + r;
+                        if (r < 8 && (TWO ? tk < ntok : lane < 8))
+                            p.out[tk * (p.n_rows / 2) + (t_begin + j) * 8 + r] = (v / (1.0f + expf(-v))) * uv;
+                    } else if (TWO ? tk < ntok : lane < 16) {
+                        const int row = (t_begin + j) * 16 + r + tk * p.n_rows;
                         float xo = 0.f, dsv = 0.f;
                         if (EPI == EPI_RESID) {
                             xo = p.x_resid[row];
-                            if (ds_vi >= 0) dsv = p.deepstack[(long long)ds_vi * H + row];
+                            if (ds_vi >= 0 && tk == 0) dsv = p.deepstack[(long long)ds_vi * H + row];
                         }
                         gemv_row_epilogue<EPI>(p, row, v, xo, dsv, write_logits, step, best_v, best_i);
                     }
@@ -631,9 +668,12 @@ __global__ void __launch_bounds__(256) argmax_parts_kernel(const float* best_v, 
 }
 
 // Reduces the lm_head's per-CTA argmax partials to the next token and commits it (reference
-// k_commit, Shaders.swift:1501-1547, without the grammar-forced pairs): one CTA.
+// k_commit, Shaders.swift:1501-1571): one CTA.  When the call has the grammar-guided commit
+// (st->grammar, engines built with it), ')' ends the call like EOS and a forced syntax token is
+// appended after ',' and after a first-output action word; the next pass then carries both tokens
+// (n_tok = 2) and advances the position by two.
 __global__ void __launch_bounds__(256) commit_kernel(const float* cta_best_v, const int* cta_best_i, int n_parts,
-                                                     int* out_tokens, DevState* st) {
+                                                     int* out_tokens, DevState* st, GrammarRule rule) {
     pdl_wait();
     pdl_launch_dependents();
     if (st->done) return;
@@ -652,13 +692,27 @@ __global__ void __launch_bounds__(256) commit_kernel(const float* cta_best_v, co
     if (threadIdx.x == 0) {
         for (int w2 = 1; w2 < (int)(blockDim.x >> 5); ++w2) argmax_merge(sv[0], si[0], sv[w2], si[w2]);
         const int tok = si[0];
-        st->pos += 1;
+        const bool gram = rule.n_action >= 0 && st->grammar;
+        st->pos += gram ? st->n_tok : 1;
         if (st->prompt_idx < st->prompt_len) st->prompt_idx += 1;
         out_tokens[st->step] = tok;
         st->step += 1;
         st->cur_token = tok;
-        const bool stop = (st->stop_on_eos && (tok == st->eos0 || tok == st->eos1)) || st->step >= st->max_steps;
-        if (stop) st->done = 1;
+        const bool stop = (st->stop_on_eos && (tok == st->eos0 || tok == st->eos1)) || st->step >= st->max_steps ||
+                          (gram && tok == rule.close);
+        if (gram) st->n_tok = 1;
+        if (stop) {
+            st->done = 1;
+        } else if (gram) {
+            const int syn = grammar_syntax(rule, tok, st->step);
+            if (syn >= 0) {
+                out_tokens[st->step] = syn;
+                st->step += 1;
+                st->n_tok = 2;
+                st->cur_token2 = syn;
+                if (st->step >= st->max_steps) st->done = 1;  // the forced token was the last output
+            }
+        }
     }
 }
 

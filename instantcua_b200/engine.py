@@ -17,6 +17,10 @@ from ._lib import IcuaError  # noqa: F401  (re-export)
 
 IMAGE_PAD = 151655
 
+# The reference's grammar-commit token ids (its Qwen tokenizer, Shaders.swift:1541-1548).
+REFERENCE_GRAMMAR = {"actions": (3678, 7241, 12476, 10855, 11862, 1339, 1472, 24769), "comma": 11, "space": 220,
+                     "open": 7, "close": 8}
+
 
 @dataclass
 class Timing:
@@ -156,6 +160,30 @@ class Engine:
         """Engine.usePrefixCache: reuse the K/V of an unchanged system prompt before the image."""
         L.check(self._lib.icua_set_prefix_cache(self._h, int(bool(on))), self._h)
         self._prefix_cache = bool(on)
+
+    def set_grammar_commit(self, enable: bool = True, actions=None, comma=None, space=None, open_=None,
+                           close=None) -> None:
+        """Grammar-guided 2-token commit (reference k_commit, Shaders.swift:1497-1571), opt-in.
+
+        With no ids the reference's are used ('(' 7, ')' 8, ',' 11, ' ' 220 and its eight action
+        words); passing any id replaces the whole rule, the others taking the reference's values.
+        """
+        rule = None
+        if any(v is not None for v in (actions, comma, space, open_, close)):
+            acts = list(actions) if actions is not None else list(REFERENCE_GRAMMAR["actions"])
+            if len(acts) > 8:
+                raise ValueError("at most 8 action ids")
+            rule = L.IcuaGrammar()
+            rule.n_action = len(acts)
+            for i, a in enumerate(acts):
+                rule.action[i] = int(a)
+            ref = REFERENCE_GRAMMAR
+            rule.comma = int(ref["comma"] if comma is None else comma)
+            rule.space = int(ref["space"] if space is None else space)
+            rule.open = int(ref["open"] if open_ is None else open_)
+            rule.close = int(ref["close"] if close is None else close)
+        L.check(self._lib.icua_set_grammar_commit(self._h, int(bool(enable)), C.byref(rule) if rule is not None else None),
+                self._h)
 
     def decode_batch(self, sessions, steps: int, in_tokens=None) -> np.ndarray:
         """Batched greedy decode of several sessions at once; returns int32 [len(sessions), steps]

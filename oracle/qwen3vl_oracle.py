@@ -17,6 +17,8 @@ What it restates, in numpy fp32, from the reference project (paths inside that p
 * ``Sources/Engine/Convert.swift:246-320``    ``quantizeQ4Raw``/``quantGroup`` -> :func:`quantize_q4_affine`
 * ``Sources/Engine/Shaders.swift:459-477``    ``embed_at`` (dequant per format) -> :func:`dequant_q8`,
   :func:`dequant_q4_affine`
+* ``Sources/Engine/Shaders.swift:1497-1571``  ``k_commit`` grammar-forced pairs and ')' stop ->
+  :func:`grammar_syntax`, :meth:`TextModel.generate_grammar`
 * BASELINE q4 (symmetric int4, groups of 32, fp16 scale) has no reference counterpart; it is
   defined by analogy with ``quantizeQ8`` -> :func:`quantize_q4s` / :func:`dequant_q4s`.
 
@@ -506,6 +508,58 @@ class TextModel:
             all_logits.append(lg)
             out.append(int(np.argmax(lg)))
         return out, all_logits
+
+
+# ----------------------------------------------------------------------------------------------
+# Grammar-guided 2-token commit (Sources/Engine/Shaders.swift:1497-1571)
+
+# The reference's ids (its Qwen tokenizer): '(' 7, ')' 8, ',' 11, ' ' 220 and eight action words.
+REFERENCE_GRAMMAR = {"actions": (3678, 7241, 12476, 10855, 11862, 1339, 1472, 24769), "comma": 11, "space": 220,
+                     "open": 7, "close": 8}
+
+
+def grammar_syntax(rule: dict, tok: int, step: int):
+    """Token forced after ``tok`` committed as output number ``step`` (1-based), or None
+    (Shaders.swift:1548-1549: ',' -> ' ', a first-output action word -> '(')."""
+    if tok == rule["comma"]:
+        return rule["space"]
+    if step == 1 and tok in rule["actions"]:
+        return rule["open"]
+    return None
+
+
+def _generate_grammar(model, tokens, max_new_tokens: int, rule=None, stop_on_eos: bool = False, pooler=None,
+                      deepstack=None, llm_hw=(0, 0)):
+    """Greedy loop with the grammar-forced pairs.  Returns (tokens, {output index: logits}).
+
+    A forced token gets no logits of its own; the step after a pair feeds both tokens at
+    consecutive positions (two single-token steps here, which is the same causal computation) and
+    its logits predict the token after the pair.  ')' ends the output; so does max_new_tokens,
+    also right after a forced token (Shaders.swift:1539-1559).
+    """
+    rule = REFERENCE_GRAMMAR if rule is None else rule
+    lg = model.prefill(tokens, pooler=pooler, deepstack=deepstack, llm_hw=llm_hw)
+    out = [int(np.argmax(lg))]
+    logits = {0: lg}
+    while True:
+        tok = out[-1]
+        if (stop_on_eos and tok in (IM_END, ENDOFTEXT)) or tok == rule["close"] or len(out) >= max_new_tokens:
+            break
+        syn = grammar_syntax(rule, tok, len(out))
+        if syn is not None:
+            out.append(syn)
+            if len(out) >= max_new_tokens:
+                break
+            model.decode_step(tok)
+            lg = model.decode_step(syn)
+        else:
+            lg = model.decode_step(tok)
+        logits[len(out)] = lg
+        out.append(int(np.argmax(lg)))
+    return out, logits
+
+
+TextModel.generate_grammar = _generate_grammar
 
 
 def cos_sim(a: np.ndarray, b: np.ndarray) -> float:

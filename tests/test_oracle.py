@@ -109,3 +109,47 @@ def test_multimodal_prefill_reproduces(golden, tiny_dequant):
     lg = model.prefill(golden["mm_tokens"].astype(np.int64), pooler=golden["mm_pooler"],
                        deepstack=list(golden["mm_deepstack"]), llm_hw=tuple(golden["mm_grid"].tolist()))[:1024]
     np.testing.assert_allclose(lg, golden["mm_first_logits"], rtol=0, atol=1e-5)
+
+
+def test_grammar_syntax_reference_ids():
+    """k_commit's forced pairs (Shaders.swift:1548-1549): ',' -> ' ' at any step, an action word
+    -> '(' only as the first output."""
+    R = O.REFERENCE_GRAMMAR
+    assert O.grammar_syntax(R, 11, 1) == 220 and O.grammar_syntax(R, 11, 7) == 220
+    for a in R["actions"]:
+        assert O.grammar_syntax(R, a, 1) == 7
+        assert O.grammar_syntax(R, a, 2) is None
+    assert O.grammar_syntax(R, 8, 1) is None and O.grammar_syntax(R, 100, 1) is None
+
+
+def test_grammar_pair_steps_equal_a_two_row_pass(tiny_dequant):
+    """The oracle feeds a forced pair as two single-token steps; that is the same causal
+    computation as one two-row pass at the same positions (what the engine runs)."""
+    _, wd = tiny_dequant
+    prompt = np.random.default_rng(4).integers(0, 1024, 12)
+    a = O.TextModel(wd, kv_dtype="f16")
+    a.prefill(prompt)
+    a.decode_step(17)
+    la = a.decode_step(220)
+    b = O.TextModel(wd, kv_dtype="f16")
+    b.prefill(prompt)
+    lb = b.prefill(np.array([17, 220]))
+    assert a.cur_len == b.cur_len
+    assert np.abs(la - lb).max() <= 1e-4 * np.abs(la).max()
+
+
+def test_grammar_generation_rule(tiny_dequant):
+    """Forced tokens follow their trigger, the closing token ends the output, the budget counts
+    forced tokens, and a rule that never fires is plain greedy decoding."""
+    _, wd = tiny_dequant
+    prompt = np.random.default_rng(4).integers(0, 1024, 12)
+    plain, _ = O.TextModel(wd).generate(prompt, 10)
+    never = {"actions": (), "comma": -1, "space": 220, "open": 7, "close": -1}
+    assert O.TextModel(wd).generate_grammar(prompt, 10, rule=never)[0] == plain
+    rule = {"actions": (plain[0],), "comma": -1, "space": 220, "open": 7, "close": -1}
+    out, lg = O.TextModel(wd).generate_grammar(prompt, 10, rule=rule)
+    assert out[:2] == [plain[0], 7] and len(out) == 10 and 1 not in lg
+    assert O.TextModel(wd).generate_grammar(prompt, 2, rule=rule)[0] == [plain[0], 7]
+    rule["close"] = out[4]
+    out2, _ = O.TextModel(wd).generate_grammar(prompt, 10, rule=rule)
+    assert out2 == out[:out.index(out[4]) + 1]
