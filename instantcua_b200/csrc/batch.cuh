@@ -16,6 +16,8 @@ namespace icua {
 // x[r] = embedding row of session rows_sess[r]'s current token.  One CTA per row.
 __global__ void batch_embed_kernel(const int* rows_sess, const DevState* st_all, const uint8_t* embed, int embed_tiles,
                                    int embed_fmt, float* x) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int r = blockIdx.x;
     const int tok = st_all[rows_sess[r]].cur_token;
     float* xr = x + (size_t)r * H;
@@ -27,6 +29,8 @@ __global__ void batch_embed_kernel(const int* rows_sess, const DevState* st_all,
 __global__ void __launch_bounds__(256) batch_commit_kernel(const float* best_v, const int* best_i, int n_tiles,
                                                            int n_rows, const int* rows_sess, DevState* st_all,
                                                            int* out_all, int out_stride) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int r = blockIdx.x;
     DevState* st = st_all + rows_sess[r];
     if (st->done) return;

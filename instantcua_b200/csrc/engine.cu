@@ -339,7 +339,7 @@ int g_n_sm_cache = 0;
 // dequant_q4s_f16_kernel), brought in by TMA as well.
 template <int EPI, int FMT = FMT_Q4S>
 cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaStream_t s, const __half* w16 = nullptr,
-                           int ksplit = 1) {
+                           int ksplit = 1, bool pdl = false) {
     if (p.n_rows % TC_BM || p.k % TC_BK || p.m_tok < 1 || p.m_tok > rows_alloc) return cudaErrorInvalidValue;
     if (!g_n_sm_cache) {
         int dev = 0;
@@ -361,6 +361,14 @@ cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaSt
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = TcLayout(t.bn, t.mh, FMT, EPI == TC_ARGMAX).alloc;
     cfg.stream = s;
+    // programmatic dependent launch: only where the weights are not the previous kernel's output
+    // (engine matrices); the kernel waits for the previous kernel before its activation loads
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    p.pdl = pdl ? 1 : 0;
     if (t.mh == 2) {
         if constexpr (EPI != TC_ARGMAX) return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI, FMT, 2>, map, wmap, p);
         return cudaErrorInvalidValue;
@@ -383,10 +391,11 @@ cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmPar
     auto run = [&](auto epi_tag, const TcGemmParams& q, int ksplit) -> cudaError_t {
         constexpr int E = decltype(epi_tag)::value;
         if (m.fmt == FMT_F16)
-            return launch_tc_gemm<E, FMT_F16>(x, e->cfg.max_pass, q, s, reinterpret_cast<const __half*>(m.dev), ksplit);
-        if (m.fmt == FMT_Q8) return launch_tc_gemm<E, FMT_Q8>(x, e->cfg.max_pass, q, s, nullptr, ksplit);
-        if (m.fmt == FMT_Q4A) return launch_tc_gemm<E, FMT_Q4A>(x, e->cfg.max_pass, q, s, nullptr, ksplit);
-        return launch_tc_gemm<E, FMT_Q4S>(x, e->cfg.max_pass, q, s, nullptr, ksplit);
+            return launch_tc_gemm<E, FMT_F16>(x, e->cfg.max_pass, q, s, reinterpret_cast<const __half*>(m.dev), ksplit,
+                                              true);
+        if (m.fmt == FMT_Q8) return launch_tc_gemm<E, FMT_Q8>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true);
+        if (m.fmt == FMT_Q4A) return launch_tc_gemm<E, FMT_Q4A>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true);
+        return launch_tc_gemm<E, FMT_Q4S>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true);
     };
     if (ks < 2 || p.m_tok > SPLITK_MAX_ROWS) return run(std::integral_constant<int, EPI>{}, p, 1);
     TcGemmParams q = p;
@@ -397,7 +406,7 @@ cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmPar
     if (err != cudaSuccess) return err;
     const long long total = (long long)p.m_tok * p.n_rows;
     const int grid = (int)std::min<long long>((total + 255) / 256, 4LL * e->n_sm);
-    return launch(splitk_finish_kernel<EPI>, grid, 256, 0, s, false, (const float*)e->splitk_part, ks, p.m_tok,
+    return launch(splitk_finish_kernel<EPI>, grid, 256, 0, s, true, (const float*)e->splitk_part, ks, p.m_tok,
                   p.n_rows, p.out, p.out_h);
 }
 
@@ -916,7 +925,9 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
                       (const float*)e->pooler, (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->embed.fmt, e->px)) != cudaSuccess)
         return err;
     const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
-    // The layer matrices in GEMM order (the last layer only projects K/V).  Matrix i is
+    // Launched without programmatic dependent launch: CTAs of a dependent kernel parked at
+    // griddepcontrol.wait would hold SMs that the side stream's dequantisation runs on (a run
+    // with it measured 3% slower).  The layer matrices in GEMM order (the last layer only projects K/V).  Matrix i is
     // dequantised to fp16 on the side stream while GEMM i-1 runs (after GEMM i-2 has finished), so
     // its tiles are still in L2 when GEMM i reads them; set (layer % 2, kind) holds it.
     std::vector<std::pair<int, int>> seq;  // (layer, kind: 0 QKV, 1 O, 2 gate/up, 3 down)
@@ -1026,13 +1037,13 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
     cudaError_t err;
     cudaStream_t st = e->stream;
     const int L = e->cfg.n_layers;
-    if ((err = launch(batch_embed_kernel, n_rows, 256, 0, st, false, (const int*)e->batch_rows,
+    if ((err = launch(batch_embed_kernel, n_rows, 256, 0, st, true, (const int*)e->batch_rows,
                       (const DevState*)e->st_all, (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->embed.fmt, e->px)) != cudaSuccess)
         return err;
     const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
     for (int l = 0; l < L; ++l) {
         Layer& ly = e->layers[l];
-        if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
+        if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, true, (const float*)e->px,
                           (const float*)ly.attn_norm, n_rows, e->pxn)) != cudaSuccess)
             return err;
         TcGemmParams p = tc_params(ly.qkv, n_rows, e->gemm_err);
@@ -1066,20 +1077,22 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
             cfg.blockDim = dim3(256);
             cfg.dynamicSmemBytes = AttnSmem<KVT>::total;
             cfg.stream = st;
-            cudaLaunchAttribute attr[1];
+            cudaLaunchAttribute attr[2];
             attr[0].id = cudaLaunchAttributeClusterDimension;
             attr[0].val.clusterDim.x = a.cluster;
             attr[0].val.clusterDim.y = 1;
             attr[0].val.clusterDim.z = 1;
+            attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[1].val.programmaticStreamSerializationAllowed = 1;
             cfg.attrs = attr;
-            cfg.numAttrs = 1;
+            cfg.numAttrs = 2;
             if ((err = cudaLaunchKernelEx(&cfg, attn_decode_kernel<KVT>, a)) != cudaSuccess) return err;
         }
         p = tc_params(ly.o, n_rows, e->gemm_err);
         p.out = e->px;
         p.ldo = H;
         if ((err = batch_gemm<TC_RESID>(e, ly.o, e->pattn, p, st)) != cudaSuccess) return err;
-        if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
+        if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, true, (const float*)e->px,
                           (const float*)ly.mlp_norm, n_rows, e->pxn)) != cudaSuccess)
             return err;
         p = tc_params(ly.gu, n_rows, e->gemm_err);
@@ -1091,7 +1104,7 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
         p.ldo = H;
         if ((err = batch_gemm<TC_RESID>(e, ly.d, e->ph, p, st)) != cudaSuccess) return err;
     }
-    if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
+    if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, true, (const float*)e->px,
                       (const float*)e->final_norm, n_rows, e->pxn)) != cudaSuccess)
         return err;
     TcGemmParams p = tc_params(e->embed, n_rows, e->gemm_err);
@@ -1101,12 +1114,13 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
     // the GEMV head does
     p.out = e->batch_logits ? e->batch_logits : (e->embed.fmt == FMT_F16 && n_rows == 1 ? e->logits : nullptr);
     p.ldo = e->cfg.vocab;
-    err = e->embed.fmt == FMT_Q4A ? launch_tc_gemm<TC_ARGMAX, FMT_Q4A>(e->pxn, e->cfg.max_pass, p, st)
+    err = e->embed.fmt == FMT_Q4A ? launch_tc_gemm<TC_ARGMAX, FMT_Q4A>(e->pxn, e->cfg.max_pass, p, st, nullptr, 1, true)
         : e->embed.fmt == FMT_F16 ? launch_tc_gemm<TC_ARGMAX, FMT_F16>(e->pxn, e->cfg.max_pass, p, st,
-                                                                       reinterpret_cast<const __half*>(e->embed.dev))
-                                  : launch_tc_gemm<TC_ARGMAX, FMT_Q8>(e->pxn, e->cfg.max_pass, p, st);
+                                                                       reinterpret_cast<const __half*>(e->embed.dev), 1,
+                                                                       true)
+                                  : launch_tc_gemm<TC_ARGMAX, FMT_Q8>(e->pxn, e->cfg.max_pass, p, st, nullptr, 1, true);
     if (err != cudaSuccess) return err;
-    return launch(batch_commit_kernel, n_rows, 256, 0, st, false, (const float*)e->batch_best_v,
+    return launch(batch_commit_kernel, n_rows, 256, 0, st, true, (const float*)e->batch_best_v,
                   (const int*)e->batch_best_i, e->cfg.vocab / TC_BM, n_rows, (const int*)e->batch_rows, e->st_all,
                   e->out_all, e->out_stride);
 }

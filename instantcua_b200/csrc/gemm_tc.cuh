@@ -21,6 +21,9 @@
 //               one weight row per thread, tokens along the registers
 // Every wait is bounded; a wait that gives up records an error flag, and the kernel still drains
 // its copies and frees its tensor memory before it exits.
+// Programmatic dependent launch: the weights do not depend on the previous kernel, so quantised
+// weights of the first stages are copied (and dequantised) before griddepcontrol.wait; the
+// activation loads and every global access of the epilogue come after it.
 #pragma once
 #include <cuda.h>
 
@@ -54,6 +57,10 @@ struct TcGemmParams {
     int* err;                  // error flags (bounded waits that gave up)
     long long out_zstride;     // split K (gridDim.z > 1, TC_STORE only): slice z covers k-blocks
                                //   [z nk / Z, (z+1) nk / Z) and stores to out + z * out_zstride
+    int pdl;                   // launched as a programmatic dependent: all S stages' quantised
+                               //   weights are requested before griddepcontrol.wait (else only the
+                               //   first, so that the first activation tile is not queued behind S
+                               //   weight tiles)
 };
 
 // Shared-memory layout of one CTA for a (BN, MH, format) choice; the same arithmetic runs on the
@@ -304,7 +311,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     const int nk_all = p.k / TC_BK;
     const int kb0 = (int)((long long)nk_all * blockIdx.z / gridDim.z);
     const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb0;
-    // CTAs that share an operand tile start at different k-blocks (rotation by the token-tile
+    // CTAs that share a weight tile start at different k-blocks (rotation by the token-tile
     // index), so they do not all request the same rows from L2 at the same moment
     const int krot = (int)((blockIdx.x * 5u) % (unsigned)nk);
     constexpr uint32_t tmem_cols = MH == 2 ? 512 : 256;
@@ -329,27 +336,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // the dependents may start their own weight prefetch on the SMs this grid leaves free
+    pdl_launch_dependents();
+
     if (warp == 0) {
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
             if (FMT == FMT_F16) asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
-            int kc = 0;
-            for (; kc < nk; ++kc) {
+            // weights of stage kc: the quantised units by bulk copy onto rawfull[s], or fp16 boxes by
+            // TMA onto bfull[s] with the stage's activation tile (one barrier: measured 5% faster on
+            // the prefill GEMMs than a barrier per operand), which is why fp16 weights are never
+            // requested ahead of griddepcontrol.wait
+            auto issue_w = [&](int kc) {
                 const int s = kc % S;
-                if (kc >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((kc / S - 1) & 1))) {
-                    atomicOr(p.err, ERR_WAIT_PREFILL);
-                    break;
-                }
+                const int kblk = kb0 + (kc + krot) % nk;
                 if constexpr (FMT == FMT_F16) {
-                    // dequantised weights: MH boxes of 128 rows x 64 columns by TMA, same barrier as X
                     mbar_expect_tx(&bfull[s], (uint32_t)(SM.a_bytes + SM.b_bytes));
 #pragma unroll
                     for (int h = 0; h < MH; ++h)
-                        tma_load_2d(smem + SM.a_off + s * SM.a_bytes + h * TC_BM * 128, &wmap,
-                                    (kb0 + (kc + krot) % nk) * TC_BK, row0 + h * TC_BM, &bfull[s]);
+                        tma_load_2d(smem + SM.a_off + s * SM.a_bytes + h * TC_BM * 128, &wmap, kblk * TC_BK,
+                                    row0 + h * TC_BM, &bfull[s]);
                 } else {
                     uint8_t* raw = smem + SM.raw_off + s * SM.raw_bytes;
-                    const int kblk = kb0 + (kc + krot) % nk;
                     mbar_expect_tx(&rawfull[s], NU * UB);
                     if (p.wtc != nullptr) {
                         // tensor-core tile order: the 8 units of a 128-row group are contiguous
@@ -363,14 +371,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                             bulk_g2s(raw + t * UB, p.w + icua_layout::unit_offset(FMT, p.n_tiles, p.upt, tile0 + t, kblk),
                                      UB, &rawfull[s]);
                     }
-                    mbar_expect_tx(&bfull[s], (uint32_t)SM.b_bytes);
                 }
+            };
+            const int pre = FMT == FMT_F16 ? 0 : min(p.pdl ? S : 1, nk);
+            for (int kc = 0; kc < pre; ++kc) issue_w(kc);
+            pdl_wait();  // the activations are the previous kernel's output
+            int kc = 0;
+            for (; kc < nk; ++kc) {
+                const int s = kc % S;
+                if (kc >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((kc / S - 1) & 1))) {
+                    atomicOr(p.err, ERR_WAIT_PREFILL);
+                    break;
+                }
+                if (kc >= pre) issue_w(kc);
+                if (FMT != FMT_F16) mbar_expect_tx(&bfull[s], (uint32_t)SM.b_bytes);
                 tma_load_2d(smem + SM.b_off + s * SM.b_bytes, &xmap, (kb0 + (kc + krot) % nk) * TC_BK, tok0, &bfull[s]);
             }
-            // the copies of the last stages complete before the CTA may exit (at once on success)
-            for (int c = (kc > S ? kc - S : 0); c < kc; ++c) {
+            // the copies of the last stages complete before the CTA may exit (at once on success);
+            // after a failed wait at kc >= S the stages issued are [0, kc), all within this range
+            // or consumed already
+            const int issued = kc < pre ? pre : kc;
+            for (int c = (issued > S ? issued - S : 0); c < issued; ++c) {
                 if (FMT != FMT_F16) mbar_wait_bounded(&rawfull[c % S], (uint32_t)((c / S) & 1));
-                mbar_wait_bounded(&bfull[c % S], (uint32_t)((c / S) & 1));
+                if (c < kc) mbar_wait_bounded(&bfull[c % S], (uint32_t)((c / S) & 1));
             }
         }
     } else if (warp == 1) {
@@ -379,6 +402,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             for (int kc = 0; kc < nk; ++kc) {
                 const int s = kc % S;
                 const uint32_t ph = (uint32_t)((kc / S) & 1);
+                // A operand: dequantised by the CUDA-core warps (afull), or fp16 weights by TMA (rawfull)
                 if ((FMT != FMT_F16 && !mbar_wait_bounded(&afull[s], ph)) || !mbar_wait_bounded(&bfull[s], ph)) {
                     atomicOr(p.err, ERR_WAIT_PREFILL);
                     break;
@@ -426,6 +450,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         // (MH == 2) or every other 32-column chunk (MH == 1) ----
         const bool done = __all_sync(0xffffffffu, mbar_wait_bounded(accfull, 0));
         tc_fence_after();
+        pdl_wait();  // (already satisfied: the MMAs consumed activations loaded after it)
         if (!done) {
             if (lane == 0) atomicOr(p.err, ERR_WAIT_PREFILL);
         } else {
@@ -616,6 +641,8 @@ __global__ void tc_order_kernel(const uint8_t* src, int fmt, int n_tiles, int up
 template <int EPI>
 __global__ void __launch_bounds__(256) splitk_finish_kernel(const float* part, int Z, int m, int n, float* out,
                                                             __half* out_h) {
+    pdl_wait();
+    pdl_launch_dependents();
     const long long total = (long long)m * n;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
         float acc = part[i];

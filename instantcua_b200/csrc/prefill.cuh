@@ -5,6 +5,8 @@
 // k_qk_norm_rope (871-923) and k_prefill_attn (1101-1216).  The reference materialises the score
 // matrix in threadgroup memory; here attention is a flash (online-softmax) kernel on the tensor
 // cores that never leaves registers, with K/V tiles bulk-copied from the swizzled cache rows.
+// Each kernel starts with griddepcontrol.wait, so it may be launched as a programmatic dependent
+// of the kernel before it (its launch then overlaps that kernel's tail).
 #pragma once
 #include "attn_decode.cuh"
 #include "common.cuh"
@@ -16,6 +18,8 @@ namespace icua {
 // One CTA of 256 threads per prompt row.
 __global__ void prefill_embed_kernel(const int* prompt, int n, int vis_off, int n_vis, const float* pooler,
                                      const uint8_t* embed, int embed_tiles, int embed_fmt, float* x) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int i = blockIdx.x;
     if (i >= n) return;
     const int tok = prompt[i];
@@ -31,6 +35,8 @@ __global__ void prefill_embed_kernel(const int* prompt, int n, int vis_off, int 
 // One CTA of 256 threads per row of 2048.
 __global__ void __launch_bounds__(256) rmsnorm_rows_f16_kernel(const float* x, const float* w, int n, __half* out) {
     __shared__ float red[8];
+    pdl_wait();
+    pdl_launch_dependents();
     const int i = blockIdx.x, tid = threadIdx.x;
     if (i >= n) return;
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)i * H);
@@ -75,6 +81,8 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(const float* qkv, int n
     for (int e = 0; e < 4; ++e) cs4[e] = rope[(size_t)pos * 64 + 4 * (lane & 15) + e];
     const float4 qn = reinterpret_cast<const float4*>(q_norm)[lane];
     const float4 kn = reinterpret_cast<const float4*>(k_norm)[lane];
+    pdl_wait();  // the norm weights and the RoPE table do not depend on the previous kernel
+    pdl_launch_dependents();
 #pragma unroll 1
     for (int vi = warp; vi < 32; vi += 8) {
         const float4 x4 = reinterpret_cast<const float4*>(row + vi * HD)[lane];
@@ -137,6 +145,8 @@ __global__ void __launch_bounds__(PA_THREADS) prefill_attn_kernel(const float* q
     extern __shared__ __align__(128) uint8_t smem[];
     using S = PrefillAttnSmem<KVT>;
     constexpr int RB = S::row_bytes;
+    pdl_wait();
+    pdl_launch_dependents();
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bars_off);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int h = blockIdx.y;
