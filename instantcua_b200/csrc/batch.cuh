@@ -28,7 +28,7 @@ __global__ void batch_embed_kernel(const int* rows_sess, const DevState* st_all,
 // ties) and commits the token to its session exactly as the batch-1 commit does.  One CTA per row.
 __global__ void __launch_bounds__(256) batch_commit_kernel(const float* best_v, const int* best_i, int n_tiles,
                                                            int n_rows, const int* rows_sess, DevState* st_all,
-                                                           int* out_all, int out_stride) {
+                                                           int* out_all, int out_stride, int vocab) {
     pdl_wait();
     pdl_launch_dependents();
     const int r = blockIdx.x;
@@ -50,6 +50,11 @@ __global__ void __launch_bounds__(256) batch_commit_kernel(const float* best_v, 
     if (threadIdx.x == 0) {
         for (int w2 = 1; w2 < (int)(blockDim.x >> 5); ++w2) argmax_merge(sv[0], si[0], sv[w2], si[w2]);
         const int tok = si[0];
+        if ((unsigned)tok >= (unsigned)vocab) {  // no finite logit: stop this session
+            atomicOr(&st->error, ERR_BAD_TOKEN);
+            st->done = 1;
+            return;
+        }
         st->pos += 1;
         out_all[(size_t)rows_sess[r] * out_stride + st->step] = tok;
         st->step += 1;

@@ -247,6 +247,8 @@ template <>
 __device__ __forceinline__ __nv_bfloat16 float_to_kv<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 
 // Error flags written to DevState::error.
-enum : int { ERR_WAIT_GEMV = 1, ERR_WAIT_ATTN = 2, ERR_WAIT_PREFILL = 4 };
+// ERR_BAD_TOKEN: a commit found no finite logit (NaN rows leave the argmax without a winner); the
+// session stops instead of embedding an id outside the vocabulary on its next step.
+enum : int { ERR_WAIT_GEMV = 1, ERR_WAIT_ATTN = 2, ERR_WAIT_PREFILL = 4, ERR_BAD_TOKEN = 8 };
 
 }  // namespace icua

@@ -672,7 +672,7 @@ cudaError_t record_head(icua_engine* e, Session& S) {
     GrammarRule rule = e->rule;
     if (!e->grammar) rule.n_action = -1;  // the commit never applies the rule
     return launch(commit_kernel, 1, 256, 0, e->stream, true, (const float*)e->cta_best_v, (const int*)e->cta_best_i,
-                  e->embed.grid, S.out_tokens, S.st, rule);
+                  e->embed.grid, S.out_tokens, S.st, rule, e->cfg.vocab);
 }
 
 icua_status build_graph(icua_engine* eng, Session& S, int kind, cudaGraphExec_t* out) {
@@ -766,6 +766,9 @@ icua_status sync_and_check(icua_engine* eng, Session& S) {
     S.done = hs.done;
     if (hs.error) {
         eng->failed = true;
+        if (hs.error == ERR_BAD_TOKEN)
+            return fail(eng, ICUA_ERR_STATE, "no finite logit at step %d (NaN/inf activations); the session stopped",
+                        hs.step);
         return fail(eng, ICUA_ERR_TIMEOUT, "a bounded device wait gave up (flags 0x%x)", hs.error);
     }
     return ICUA_OK;
@@ -1122,7 +1125,7 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
     if (err != cudaSuccess) return err;
     return launch(batch_commit_kernel, n_rows, 256, 0, st, true, (const float*)e->batch_best_v,
                   (const int*)e->batch_best_i, e->cfg.vocab / TC_BM, n_rows, (const int*)e->batch_rows, e->st_all,
-                  e->out_all, e->out_stride);
+                  e->out_all, e->out_stride, e->cfg.vocab);
 }
 
 void drop_batch_graphs(icua_engine* e) {

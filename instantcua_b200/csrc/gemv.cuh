@@ -673,7 +673,7 @@ __global__ void __launch_bounds__(256) argmax_parts_kernel(const float* best_v, 
 // appended after ',' and after a first-output action word; the next pass then carries both tokens
 // (n_tok = 2) and advances the position by two.
 __global__ void __launch_bounds__(256) commit_kernel(const float* cta_best_v, const int* cta_best_i, int n_parts,
-                                                     int* out_tokens, DevState* st, GrammarRule rule) {
+                                                     int* out_tokens, DevState* st, GrammarRule rule, int vocab) {
     pdl_wait();
     pdl_launch_dependents();
     if (st->done) return;
@@ -692,6 +692,11 @@ __global__ void __launch_bounds__(256) commit_kernel(const float* cta_best_v, co
     if (threadIdx.x == 0) {
         for (int w2 = 1; w2 < (int)(blockDim.x >> 5); ++w2) argmax_merge(sv[0], si[0], sv[w2], si[w2]);
         const int tok = si[0];
+        if ((unsigned)tok >= (unsigned)vocab) {
+            atomicOr(&st->error, ERR_BAD_TOKEN);
+            st->done = 1;
+            return;
+        }
         const bool gram = rule.n_action >= 0 && st->grammar;
         st->pos += gram ? st->n_tok : 1;
         if (st->prompt_idx < st->prompt_len) st->prompt_idx += 1;
