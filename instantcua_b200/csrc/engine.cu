@@ -339,7 +339,7 @@ int g_n_sm_cache = 0;
 // dequant_q4s_f16_kernel), brought in by TMA as well.
 template <int EPI, int FMT = FMT_Q4S>
 cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaStream_t s, const __half* w16 = nullptr,
-                           int ksplit = 1, bool pdl = false) {
+                           int ksplit = 1, bool pdl = false, int max_stages = 8) {
     if (p.n_rows % TC_BM || p.k % TC_BK || p.m_tok < 1 || p.m_tok > rows_alloc) return cudaErrorInvalidValue;
     if (!g_n_sm_cache) {
         int dev = 0;
@@ -359,7 +359,8 @@ cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaSt
     if (ksplit > 1 && (EPI != TC_STORE || ksplit > p.k / TC_BK)) return cudaErrorInvalidValue;
     cfg.gridDim = dim3((p.m_tok + t.bn - 1) / t.bn, p.n_rows / (TC_BM * t.mh), ksplit);
     cfg.blockDim = dim3(TC_THREADS);
-    cfg.dynamicSmemBytes = TcLayout(t.bn, t.mh, FMT, EPI == TC_ARGMAX).alloc;
+    p.max_stages = max_stages;
+    cfg.dynamicSmemBytes = TcLayout(t.bn, t.mh, FMT, EPI == TC_ARGMAX, max_stages).alloc;
     cfg.stream = s;
     // programmatic dependent launch: only where the weights are not the previous kernel's output
     // (engine matrices); the kernel waits for the previous kernel before its activation loads
@@ -392,10 +393,10 @@ cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmPar
         constexpr int E = decltype(epi_tag)::value;
         if (m.fmt == FMT_F16)
             return launch_tc_gemm<E, FMT_F16>(x, e->cfg.max_pass, q, s, reinterpret_cast<const __half*>(m.dev), ksplit,
-                                              true);
-        if (m.fmt == FMT_Q8) return launch_tc_gemm<E, FMT_Q8>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true);
-        if (m.fmt == FMT_Q4A) return launch_tc_gemm<E, FMT_Q4A>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true);
-        return launch_tc_gemm<E, FMT_Q4S>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true);
+                                              true, 3);
+        if (m.fmt == FMT_Q8) return launch_tc_gemm<E, FMT_Q8>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, 3);
+        if (m.fmt == FMT_Q4A) return launch_tc_gemm<E, FMT_Q4A>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, 3);
+        return launch_tc_gemm<E, FMT_Q4S>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, 3);
     };
     if (ks < 2 || p.m_tok > SPLITK_MAX_ROWS) return run(std::integral_constant<int, EPI>{}, p, 1);
     TcGemmParams q = p;

@@ -1,5 +1,6 @@
 """CPU tests of the oracle against the committed golden fixtures (no GPU, no transformers)."""
 import hashlib
+import os
 
 import numpy as np
 import pytest
@@ -153,3 +154,39 @@ def test_grammar_generation_rule(tiny_dequant):
     rule["close"] = out[4]
     out2, _ = O.TextModel(wd).generate_grammar(prompt, 10, rule=rule)
     assert out2 == out[:out.index(out[4]) + 1]
+
+
+def test_vision_oracle_reproduces_pinned_fixture():
+    """The vision restatement on the narrow configuration that tests/golden/make_golden_vision.py
+    pinned against Hugging Face Qwen3VLVisionModel (max |d| stored in the fixture)."""
+    from golden.make_golden_vision import SEED, SMALL
+    from oracle import qwen3vl_vision as V
+
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden_vision.npz"))
+    assert float(g["hf_max_abs_diff"]) <= 1e-5
+    w = V.generate_weights(int(g["seed"]), SMALL)
+    patches, gh, gw = V.patchify(g["rgb"], SMALL)
+    pooler, ds = V.encode_vision(w, patches, gh, gw, SMALL)
+    assert np.allclose(pooler, g["pooler"], atol=1e-6, rtol=0)
+    assert np.allclose(np.stack(ds), g["deepstack"], atol=1e-6, rtol=0)
+
+
+def test_vision_patch_order_and_tables():
+    """Merge-block patch order, the position resampling at the grid corners, and the 2-D RoPE
+    angles (qwen3vl_ref.py:25-84) on hand-checkable inputs."""
+    from oracle import qwen3vl_vision as V
+
+    d = V.REFERENCE
+    rgb = np.zeros((64, 64, 3), np.uint8)
+    rgb[16:32, 0:16, 1] = 255  # patch (row 1, col 0), green channel
+    p, gh, gw = V.patchify(rgb, d)
+    assert (gh, gw) == (4, 4)
+    hot = np.nonzero((p > 0).any(axis=1))[0]
+    assert hot.tolist() == [2]  # block (0, 0) holds patches (0,0) (0,1) (1,0) (1,1)
+    assert np.all(p[2, 256:512] == 1.0) and np.all(p[2, :256] == -1.0)
+    table = np.random.default_rng(0).standard_normal((48 * 48, 8)).astype(np.float32)
+    pos = V.pos_embed_interp(table, 4, 4, d)
+    assert np.allclose(pos[0], table[0]) and np.allclose(pos[15], table[48 * 48 - 1])
+    cos, sin = V.vision_rope(4, 4, d)
+    # patch 3 of block 0 is (row 1, col 1): first-frequency angle 1 for both halves
+    assert np.isclose(cos[3, 0], np.cos(1.0)) and np.isclose(cos[3, 16], np.cos(1.0)) and cos[0, 0] == 1.0
