@@ -89,7 +89,8 @@ typedef struct {
 } icua_timing;
 
 /* Optional visual inputs for a prompt (replace the ViT outputs poolerBuf / deepstackBufs,
- * Engine.swift:20-21).  Host fp32 arrays, row-major [n_vis, 2048]; deepstack[i] may be NULL. */
+ * Engine.swift:20-21).  Host fp32 arrays, row-major [n_vis, 2048]; deepstack[i] may be NULL.
+ * pooler == NULL takes the rows that the last icua_encode_vision left on the device. */
 typedef struct {
     const float* pooler;
     const float* deepstack[3];
@@ -182,6 +183,24 @@ icua_status icua_set_grammar_commit(icua_engine* eng, int32_t enable, const icua
 icua_status icua_generate(icua_engine* eng, int32_t session, const int32_t* tokens, int32_t n,
                           const icua_visual* visual, int32_t max_new, int32_t write_first_logits,
                           int32_t* out_tokens, int32_t* n_out);
+
+/* ---- vision encoder (reference encodeVision, Engine.swift:317-473) -------------------------
+ * Needs the vision tensors of the model file (ids 0..ICUA_VIT_TENSORS-1: fp16 matrices, fp32
+ * biases / norms / position table, Convert.swift:99-152); icua_engine_load_file takes them from
+ * the file when present, icua_engine_set_tensor at any time.  rgb is RGB8 [height][width][3] with
+ * width and height multiples of 32 (16-pixel patches, 2x2 merge) and at most 4 * max_pass patches.
+ * The outputs stay on the device as the next prompt's visual rows (use icua_generate_rgb, or pass
+ * an icua_visual whose pooler is NULL and whose n_vis, llm_h, llm_w match); pooler_out [n_vis][2048]
+ * and deepstack_out [3][n_vis][2048] receive host copies when not NULL.  *n_vis_out = patches / 4. */
+enum { ICUA_VIT_TENSORS = 315 };
+icua_status icua_encode_vision(icua_engine* eng, const uint8_t* rgb, int32_t width, int32_t height,
+                               float* pooler_out, float* deepstack_out, int32_t* n_vis_out);
+/* reference generateVision(rgbBytes:width:height:tokens:maxNewTokens:writeFirstLogits:)
+ * (Engine.swift:696-827): vision encoder, then icua_generate with the prompt's IMAGE_PAD block
+ * (n_vis = width * height / 1024 tokens) taking the encoder's rows. */
+icua_status icua_generate_rgb(icua_engine* eng, int32_t session, const uint8_t* rgb, int32_t width, int32_t height,
+                              const int32_t* tokens, int32_t n, int32_t max_new, int32_t write_first_logits,
+                              int32_t* out_tokens, int32_t* n_out);
 
 /* Resets a session to position 0 (empty KV). */
 icua_status icua_reset_session(icua_engine* eng, int32_t session);

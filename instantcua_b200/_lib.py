@@ -67,6 +67,8 @@ PROTOTYPES = {
     "icua_decode": (_I, [_P, _I, _I, _IP, _IP]),
     "icua_decode_step": (_I, [_P, _I, _I, _IP]),
     "icua_generate": (_I, [_P, _I, _IP, _I, C.POINTER(IcuaVisual), _I, _I, _IP, _IP]),
+    "icua_encode_vision": (_I, [_P, C.c_void_p, _I, _I, C.c_void_p, C.c_void_p, _IP]),
+    "icua_generate_rgb": (_I, [_P, _I, C.c_void_p, _I, _I, _IP, _I, _I, _I, _IP, _IP]),
     "icua_reset_session": (_I, [_P, _I]),
     "icua_inject_kv": (_I, [_P, _I, _FP, _FP, _I]),
     "icua_inject_kv_random": (_I, [_P, _I, _I, C.c_uint64]),

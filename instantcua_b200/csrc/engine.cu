@@ -35,6 +35,7 @@
 #include "gemv.cuh"
 #include "misc.cuh"
 #include "prefill.cuh"
+#include "vision.cuh"
 
 namespace icua_host {
 uint16_t f32_to_f16_bits(float f);
@@ -149,6 +150,17 @@ struct icua_engine {
     float* batch_logits = nullptr;  // [rows][vocab] of the last batched step, when requested
     float* batch_logits_host = nullptr;
     int batch_logits_rows = 0;
+    // vision encoder: weights by reference tensor id (fp16 matrices, fp32 vectors), activations
+    // for up to vit_np_max patches (allocated at the first encode), the visual rows it left in
+    // pooler / deepstack (vis_rows, -1 when none)
+    void* vit[ICUA_VIT_TENSORS] = {};
+    int vit_count = 0;
+    int vit_np_max = 0;
+    uint8_t* vrgb = nullptr;
+    __half *vpatch = nullptr, *vxn = nullptr, *vq = nullptr, *vk = nullptr, *vv = nullptr, *vattn = nullptr,
+           *vh = nullptr;
+    float *vx = nullptr, *vqkv = nullptr;
+    int vis_rows = -1;
 };
 
 namespace {
@@ -497,7 +509,8 @@ cudaError_t set_smem_attrs() {
           (const void*)tc_gemm_kernel<TC_RESID, FMT_Q4A, 1>, (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q4A, 1>,
           (const void*)tc_gemm_kernel<TC_STORE, FMT_Q4A, 2>, (const void*)tc_gemm_kernel<TC_RESID, FMT_Q4A, 2>,
           (const void*)tc_gemm_kernel<TC_SWIGLU, FMT_Q4A, 2>, (const void*)tc_gemm_kernel<TC_ARGMAX, FMT_Q4A, 1>,
-          (const void*)tc_gemm_kernel<TC_ARGMAX, FMT_F16, 1>}) {
+          (const void*)tc_gemm_kernel<TC_ARGMAX, FMT_F16, 1>, (const void*)tc_gemm_kernel<TC_GELU, FMT_F16, 1>,
+          (const void*)tc_gemm_kernel<TC_GELU, FMT_F16, 2>}) {
         if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)) != cudaSuccess)
             return e;
     }
@@ -1349,11 +1362,55 @@ void icua_engine_destroy(icua_engine* eng) {
     delete eng;
 }
 
+// Bytes of vision tensor `id` (reference TensorID 0..314, ModelFile.swift:73-99; storage types of
+// Convert.swift:99-152): fp16 matrices [out][in], fp32 vectors and position table.
+static size_t vit_tensor_bytes(int id) {
+    if (id == 0) return (size_t)VIT_HIDDEN * VIT_PATCH_DIM * 2;
+    if (id == 1) return VIT_HIDDEN * 4;
+    if (id == 2) return (size_t)VIT_POS_SIDE * VIT_POS_SIDE * VIT_HIDDEN * 4;
+    if (id < 3 + VIT_LAYERS * 12) {
+        switch ((id - 3) % 12) {
+            case 2: return (size_t)VIT_QKV * VIT_HIDDEN * 2;
+            case 3: return VIT_QKV * 4;
+            case 4: return (size_t)VIT_HIDDEN * VIT_HIDDEN * 2;
+            case 8: return (size_t)VIT_FF * VIT_HIDDEN * 2;
+            case 9: return VIT_FF * 4;
+            case 10: return (size_t)VIT_HIDDEN * VIT_FF * 2;
+            default: return VIT_HIDDEN * 4;  // norms, proj / fc2 biases
+        }
+    }
+    const int m = (id - 3 - VIT_LAYERS * 12) / 6, k = (id - 3 - VIT_LAYERS * 12) % 6;
+    switch (k) {
+        case 0:
+        case 1: return (m < 3 ? VIT_MERGED : VIT_HIDDEN) * 4;  // the final merger normalises patches
+        case 2: return (size_t)VIT_MERGED * VIT_MERGED * 2;
+        case 3: return VIT_MERGED * 4;
+        case 4: return (size_t)H * VIT_MERGED * 2;
+        default: return H * 4;
+    }
+}
+
+static icua_status set_vit_tensor(icua_engine* eng, int id, const void* data, uint64_t bytes) {
+    const size_t want = vit_tensor_bytes(id);
+    if (bytes != want)
+        return fail(eng, ICUA_ERR_FORMAT, "vision tensor %d: %llu bytes, expected %zu", id, (unsigned long long)bytes,
+                    want);
+    CK(cudaSetDevice(eng->cfg.device));
+    if (!eng->vit[id]) {
+        icua_status s = dalloc(eng, &eng->vit[id], want);
+        if (s != ICUA_OK) return s;
+        eng->vit_count += 1;
+    }
+    CK(cudaMemcpy(eng->vit[id], data, want, cudaMemcpyHostToDevice));
+    return ICUA_OK;
+}
+
 icua_status icua_engine_set_tensor(icua_engine* eng, int32_t id, const void* data, uint64_t bytes) {
     if (!eng || !data) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    if (id >= 0 && id < ICUA_VIT_TENSORS) return set_vit_tensor(eng, id, data, bytes);
     if (eng->uploaded) return fail(eng, ICUA_ERR_STATE, "weights already uploaded");
     if (id < 0 || id >= ICUA_TENSOR_COUNT) return fail(eng, ICUA_ERR_INVALID, "tensor id %d out of range", id);
-    if (!id_used(eng, id)) return ICUA_OK;  // vision tensors and unused slots are ignored
+    if (!id_used(eng, id)) return ICUA_OK;  // unused slots (f16 files' scale slots) are ignored
     const size_t want = expected_bytes(eng, id);
     if (bytes != want)
         return fail(eng, ICUA_ERR_FORMAT, "tensor %d: %llu bytes, expected %zu", id, (unsigned long long)bytes, want);
@@ -1396,10 +1453,12 @@ icua_status icua_engine_load_file(icua_engine* eng, const char* path) {
     else if (hdr[3] != (uint32_t)ICUA_TENSOR_COUNT)
         s = fail(eng, ICUA_ERR_FORMAT, "%s: tensor table mismatch", path);
     for (int id = 0; s == ICUA_OK && id < ICUA_TENSOR_COUNT; ++id) {
-        if (!id_used(eng, id)) continue;
+        const bool vit = id < ICUA_VIT_TENSORS;
+        if (!vit && !id_used(eng, id)) continue;
         uint64_t off, sz;
         memcpy(&off, base + 16 + 16 * id, 8);
         memcpy(&sz, base + 16 + 16 * id + 8, 8);
+        if (vit && sz == 0) continue;  // a file without the vision encoder
         if (off + sz > size) {
             s = fail(eng, ICUA_ERR_FORMAT, "%s: tensor %d outside the file", path, id);
             break;
@@ -1580,8 +1639,9 @@ static icua_status prepare_prefill(icua_engine* eng, Session& S, int session, co
             return fail(eng, ICUA_ERR_INVALID, "token %d at %d out of range", tokens[i], i);
         if (tokens[i] == IMAGE_PAD_ID && vis_off < 0) vis_off = i;
     }
-    if (vis_off >= 0 && (!vis || !vis->pooler))
-        return fail(eng, ICUA_ERR_INVALID, "IMAGE_PAD tokens without visual inputs");
+    if (vis_off >= 0 && (!vis || (!vis->pooler && eng->vis_rows != vis->n_vis)))
+        return fail(eng, ICUA_ERR_INVALID, "IMAGE_PAD tokens without visual inputs (host rows, or %d encoder rows)",
+                    eng->vis_rows);
     CK(cudaMemcpyAsync(S.prompt, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, eng->stream));
     std::vector<float2> tab((size_t)C * 64);
     CK(cudaMemcpy(tab.data(), S.rope, tab.size() * sizeof(float2), cudaMemcpyDeviceToHost));
@@ -1593,13 +1653,16 @@ static icua_status prepare_prefill(icua_engine* eng, Session& S, int session, co
                         vis->llm_h, vis->llm_w);
         for (int i = vis_off; i < vis_off + n_vis; ++i)
             if (tokens[i] != IMAGE_PAD_ID) return fail(eng, ICUA_ERR_INVALID, "visual block is not contiguous");
-        CK(cudaMemcpyAsync(eng->pooler, vis->pooler, (size_t)n_vis * H * 4, cudaMemcpyHostToDevice, eng->stream));
-        for (int d = 0; d < 3; ++d) {
-            if (vis->deepstack[d])
-                CK(cudaMemcpyAsync(eng->deepstack[d], vis->deepstack[d], (size_t)n_vis * H * 4, cudaMemcpyHostToDevice,
-                                   eng->stream));
-            else
-                CK(cudaMemsetAsync(eng->deepstack[d], 0, (size_t)n_vis * H * 4, eng->stream));
+        if (vis->pooler) {  // host rows; else the vision encoder's rows are already in place
+            CK(cudaMemcpyAsync(eng->pooler, vis->pooler, (size_t)n_vis * H * 4, cudaMemcpyHostToDevice, eng->stream));
+            for (int d = 0; d < 3; ++d) {
+                if (vis->deepstack[d])
+                    CK(cudaMemcpyAsync(eng->deepstack[d], vis->deepstack[d], (size_t)n_vis * H * 4,
+                                       cudaMemcpyHostToDevice, eng->stream));
+                else
+                    CK(cudaMemsetAsync(eng->deepstack[d], 0, (size_t)n_vis * H * 4, eng->stream));
+            }
+            eng->vis_rows = -1;  // overwritten
         }
         const int vis_abs = S.pos + vis_off;
         S.rope_delta = std::max(vis->llm_h, vis->llm_w) - n_vis;
@@ -2242,6 +2305,162 @@ icua_status icua_dequant(int32_t fmt, int32_t n_rows, int32_t k, const void* pac
         dequant_kernel<FMT_Q8><<<1184, 256, 0, s>>>((const uint8_t*)packed, n_rows, k, out);
     CK(cudaGetLastError());
     return ICUA_OK;
+}
+
+// ---- vision encoder ------------------------------------------------------------------------
+
+static cudaError_t vit_gemm(icua_engine* e, int epi, const void* x, int rows_alloc, int m, int n_rows, int k,
+                            const void* w16, const void* bias, float* out, int ldo, __half* out_h, int ldh,
+                            int gelu_erf) {
+    TcGemmParams p{};
+    p.n_rows = n_rows;
+    p.k = k;
+    p.n_tiles = n_rows / 16;
+    p.upt = k / 64;
+    p.m_tok = m;
+    p.out = out;
+    p.ldo = ldo;
+    p.out_h = out_h;
+    p.ldh = ldh;
+    p.bias = static_cast<const float*>(bias);
+    p.gelu_erf = gelu_erf;
+    p.err = e->gemm_err;
+    const __half* w = static_cast<const __half*>(w16);
+    if (epi == TC_STORE) return launch_tc_gemm<TC_STORE, FMT_F16>(x, rows_alloc, p, e->stream, w);
+    if (epi == TC_RESID) return launch_tc_gemm<TC_RESID, FMT_F16>(x, rows_alloc, p, e->stream, w);
+    return launch_tc_gemm<TC_GELU, FMT_F16>(x, rows_alloc, p, e->stream, w);
+}
+
+// Records the encoder for np patches (grid gh x gw) on the engine stream: patchify, position rows,
+// patch embedding, 24 blocks (the DeepStack mergers after blocks 5, 11, 17), final merger.
+static cudaError_t record_vision(icua_engine* e, int gh, int gw) {
+    const int np = gh * gw, nv = np / 4, NP = e->vit_np_max, NV = NP / 4;
+    cudaStream_t st = e->stream;
+    cudaError_t err;
+    auto T = [&](int id) { return e->vit[id]; };
+    auto F = [&](int id) { return static_cast<const float*>(e->vit[id]); };
+#define VK(...)                                        \
+    do {                                               \
+        if ((err = (__VA_ARGS__)) != cudaSuccess) return err; \
+    } while (0)
+    VK(launch(vit_patchify_kernel, np, 256, 0, st, false, (const uint8_t*)e->vrgb, gh, gw, e->vpatch));
+    VK(launch(vit_pos_init_kernel, np, 256, 0, st, false, F(2), gh, gw, e->vx));
+    VK(vit_gemm(e, TC_RESID, e->vpatch, NP, np, VIT_HIDDEN, VIT_PATCH_DIM, T(0), T(1), e->vx, VIT_HIDDEN, nullptr, 0, 0));
+    const int ds_layer[3] = {5, 11, 17};
+    for (int l = 0; l < VIT_LAYERS; ++l) {
+        const int b = 3 + l * 12;
+        VK(launch(vit_layernorm_kernel, np, 256, 0, st, false, (const float*)e->vx, F(b + 0), F(b + 1), VIT_HIDDEN,
+                  e->vxn));
+        VK(vit_gemm(e, TC_STORE, e->vxn, NP, np, VIT_QKV, VIT_HIDDEN, T(b + 2), T(b + 3), e->vqkv, VIT_QKV, nullptr, 0, 0));
+        VK(launch(vit_qkv_rope_kernel, np, 256, 0, st, false, (const float*)e->vqkv, np, gw, e->vq, e->vk, e->vv));
+        {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((np + VA_BQ - 1) / VA_BQ, VIT_HEADS);
+            cfg.blockDim = dim3(VA_THREADS);
+            cfg.stream = st;
+            VK(cudaLaunchKernelEx(&cfg, vit_attn_kernel, (const __half*)e->vq, (const __half*)e->vk,
+                                  (const __half*)e->vv, np, e->vattn));
+        }
+        VK(vit_gemm(e, TC_RESID, e->vattn, NP, np, VIT_HIDDEN, VIT_HIDDEN, T(b + 4), T(b + 5), e->vx, VIT_HIDDEN, nullptr,
+                    0, 0));
+        VK(launch(vit_layernorm_kernel, np, 256, 0, st, false, (const float*)e->vx, F(b + 6), F(b + 7), VIT_HIDDEN,
+                  e->vxn));
+        VK(vit_gemm(e, TC_GELU, e->vxn, NP, np, VIT_FF, VIT_HIDDEN, T(b + 8), T(b + 9), nullptr, 0, e->vh, VIT_FF, 0));
+        VK(vit_gemm(e, TC_RESID, e->vh, NP, np, VIT_HIDDEN, VIT_FF, T(b + 10), T(b + 11), e->vx, VIT_HIDDEN, nullptr, 0, 0));
+        for (int d = 0; d < 3; ++d) {
+            if (l != ds_layer[d]) continue;
+            // DeepStack merger d: LayerNorm over the 2x2 merged rows [nv][4096] (views of [np][1024])
+            const int m = 3 + VIT_LAYERS * 12 + d * 6;
+            VK(launch(vit_layernorm_kernel, nv, 256, 0, st, false, (const float*)e->vx, F(m + 0), F(m + 1), VIT_MERGED,
+                      e->vxn));
+            VK(vit_gemm(e, TC_GELU, e->vxn, NV, nv, VIT_MERGED, VIT_MERGED, T(m + 2), T(m + 3), nullptr, 0, e->vh,
+                        VIT_MERGED, 1));
+            VK(vit_gemm(e, TC_STORE, e->vh, NV, nv, H, VIT_MERGED, T(m + 4), T(m + 5), e->deepstack[d], H, nullptr, 0, 0));
+        }
+    }
+    // final merger: LayerNorm per patch, then the merged rows [nv][4096]
+    const int m = 3 + VIT_LAYERS * 12 + 3 * 6;
+    VK(launch(vit_layernorm_kernel, np, 256, 0, st, false, (const float*)e->vx, F(m + 0), F(m + 1), VIT_HIDDEN, e->vxn));
+    VK(vit_gemm(e, TC_GELU, e->vxn, NV, nv, VIT_MERGED, VIT_MERGED, T(m + 2), T(m + 3), nullptr, 0, e->vh, VIT_MERGED, 1));
+    VK(vit_gemm(e, TC_STORE, e->vh, NV, nv, H, VIT_MERGED, T(m + 4), T(m + 5), e->pooler, H, nullptr, 0, 0));
+#undef VK
+    return cudaSuccess;
+}
+
+icua_status icua_encode_vision(icua_engine* eng, const uint8_t* rgb, int32_t width, int32_t height, float* pooler_out,
+                               float* deepstack_out, int32_t* n_vis_out) {
+    if (!eng || !rgb) return fail(eng, ICUA_ERR_INVALID, "null argument");
+    if (eng->failed) return fail(eng, ICUA_ERR_STATE, "engine failed earlier: %s", eng->err.c_str());
+    if (eng->vit_count < ICUA_VIT_TENSORS)
+        return fail(eng, ICUA_ERR_STATE, "vision encoder tensors missing (%d of %d)", eng->vit_count, ICUA_VIT_TENSORS);
+    if (width < 32 || height < 32 || width % 32 || height % 32)
+        return fail(eng, ICUA_ERR_INVALID, "image %dx%d: sides must be positive multiples of 32", width, height);
+    const int gh = height / 16, gw = width / 16, np = gh * gw, nv = np / 4;
+    if (nv > eng->cfg.max_pass)
+        return fail(eng, ICUA_ERR_CAPACITY, "%d visual tokens exceed max_pass %d", nv, eng->cfg.max_pass);
+    CK(cudaSetDevice(eng->cfg.device));
+    if (!eng->vit_np_max) {
+        const size_t NP = (size_t)eng->cfg.max_pass * 4;
+        icua_status s;
+        if ((s = dalloc_t(eng, &eng->vrgb, NP * VIT_PATCH_DIM)) != ICUA_OK ||
+            (s = dalloc_t(eng, &eng->vpatch, NP * VIT_PATCH_DIM)) != ICUA_OK ||
+            (s = dalloc_t(eng, &eng->vx, NP * VIT_HIDDEN)) != ICUA_OK ||
+            (s = dalloc_t(eng, &eng->vxn, NP * VIT_HIDDEN)) != ICUA_OK ||
+            (s = dalloc_t(eng, &eng->vqkv, NP * VIT_QKV)) != ICUA_OK ||
+            (s = dalloc_t(eng, &eng->vq, NP * VIT_HIDDEN)) != ICUA_OK ||
+            (s = dalloc_t(eng, &eng->vk, NP * VIT_HIDDEN)) != ICUA_OK ||
+            (s = dalloc_t(eng, &eng->vv, NP * VIT_HIDDEN)) != ICUA_OK ||
+            (s = dalloc_t(eng, &eng->vattn, NP * VIT_HIDDEN)) != ICUA_OK ||
+            (s = dalloc_t(eng, &eng->vh, NP * VIT_FF)) != ICUA_OK)
+            return s;
+        cudaMemset(eng->vxn, 0, NP * VIT_HIDDEN * sizeof(__half));  // rows past a call's patches read by TMA
+        cudaMemset(eng->vh, 0, NP * VIT_FF * sizeof(__half));
+        cudaMemset(eng->vattn, 0, NP * VIT_HIDDEN * sizeof(__half));
+        cudaMemset(eng->vpatch, 0, NP * VIT_PATCH_DIM * sizeof(__half));
+        eng->vit_np_max = (int)NP;
+    }
+    CK(cudaMemcpyAsync(eng->vrgb, rgb, (size_t)np * VIT_PATCH_DIM, cudaMemcpyHostToDevice, eng->stream));
+    const int zero = 0;
+    CK(cudaMemcpyAsync(eng->gemm_err, &zero, 4, cudaMemcpyHostToDevice, eng->stream));
+    CK(cudaEventRecord(eng->ev[0], eng->stream));
+    const cudaError_t e2 = record_vision(eng, gh, gw);
+    if (e2 != cudaSuccess) return fail(eng, ICUA_ERR_CUDA, "vision launch: %s", cudaGetErrorString(e2));
+    CK(cudaEventRecord(eng->ev[1], eng->stream));
+    CK(cudaStreamSynchronize(eng->stream));
+    int gerr = 0;
+    CK(cudaMemcpy(&gerr, eng->gemm_err, 4, cudaMemcpyDeviceToHost));
+    if (gerr) {
+        eng->failed = true;
+        return fail(eng, ICUA_ERR_TIMEOUT, "a bounded device wait gave up in the vision encoder (flags 0x%x)", gerr);
+    }
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, eng->ev[0], eng->ev[1]);
+    eng->timing.vision_ms = ms;
+    eng->vis_rows = nv;
+    if (pooler_out) CK(cudaMemcpy(pooler_out, eng->pooler, (size_t)nv * H * 4, cudaMemcpyDeviceToHost));
+    if (deepstack_out)
+        for (int d = 0; d < 3; ++d)
+            CK(cudaMemcpy(deepstack_out + (size_t)d * nv * H, eng->deepstack[d], (size_t)nv * H * 4,
+                          cudaMemcpyDeviceToHost));
+    if (n_vis_out) *n_vis_out = nv;
+    return ICUA_OK;
+}
+
+icua_status icua_generate_rgb(icua_engine* eng, int32_t session, const uint8_t* rgb, int32_t width, int32_t height,
+                              const int32_t* tokens, int32_t n, int32_t max_new, int32_t write_first_logits,
+                              int32_t* out_tokens, int32_t* n_out) {
+    int32_t nv = 0;
+    icua_status s = icua_encode_vision(eng, rgb, width, height, nullptr, nullptr, &nv);
+    if (s != ICUA_OK) return s;
+    const float vision_ms = (float)eng->timing.vision_ms;
+    icua_visual v{};
+    v.pooler = nullptr;
+    v.n_vis = nv;
+    v.llm_h = height / 32;
+    v.llm_w = width / 32;
+    s = icua_generate(eng, session, tokens, n, &v, max_new, write_first_logits, out_tokens, n_out);
+    eng->timing.vision_ms = vision_ms;
+    return s;
 }
 
 }  // extern "C"

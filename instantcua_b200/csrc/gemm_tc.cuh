@@ -37,7 +37,9 @@ constexpr int TC_BK = 64;       // columns per stage: one 128-byte swizzle row o
 constexpr int TC_THREADS = 320; // producer warp, MMA warp, 8 dequant / epilogue warps
 constexpr int TC_SMEM_BUDGET = 225 * 1024;
 
-enum TcEpi { TC_STORE = 0, TC_RESID = 1, TC_SWIGLU = 2, TC_ARGMAX = 3 };
+// TC_GELU (fp16 weights only): out_h[tok * ldh + row] = half(gelu(y)), tanh form or, with
+// gelu_erf, the exact erf form (the vision MLP and mergers).
+enum TcEpi { TC_STORE = 0, TC_RESID = 1, TC_SWIGLU = 2, TC_ARGMAX = 3, TC_GELU = 4 };
 
 struct TcGemmParams {
     const uint8_t* w;          // weights in the device tile layout [n_rows, k] (q4s, q4a or q8)
@@ -57,6 +59,8 @@ struct TcGemmParams {
     int* err;                  // error flags (bounded waits that gave up)
     long long out_zstride;     // split K (gridDim.z > 1, TC_STORE only): slice z covers k-blocks
                                //   [z nk / Z, (z+1) nk / Z) and stores to out + z * out_zstride
+    const float* bias;         // fp16-weight GEMMs: per weight row, added to y before the epilogue
+    int gelu_erf;              // TC_GELU: 1 = exact erf GELU, 0 = tanh approximation
     int max_stages;            // pipeline depth cap (TcLayout), set by the launcher
     int pdl;                   // launched as a programmatic dependent: all S stages' quantised
                                //   weights are requested before griddepcontrol.wait (else only the
@@ -472,6 +476,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                     tmem_ld32(taddr, v);
                 else
                     tmem_ld16(taddr, v);
+                if (FMT == FMT_F16 && p.bias != nullptr) {
+                    const float b = p.bias[row];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] += b;
+                }
+                if (EPI == TC_GELU) {
+                    // one weight row per thread, 32 tokens: fp16 stores strided by ldh
+                    const int nj = min(ncol, p.m_tok - (tok0 + c * 32));
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (j < nj) {
+                            const float x = v[j];
+                            const float g = p.gelu_erf ? 0.5f * x * (1.0f + erff(x * 0.70710678118654752f))
+                                                       : 0.5f * x * (1.0f + tanhf(0.79788456080286536f *
+                                                                                  (x + 0.044715f * x * x * x)));
+                            p.out_h[(size_t)(tok0 + c * 32 + j) * p.ldh + row] = __float2half_rn(g);
+                        }
+                    }
+                    continue;
+                }
                 if (EPI == TC_RESID) {
                     // residual rows: the chunk's loads first (independent, in flight together),
                     // then the adds and stores; DeepStack rows (three layers of a visual prefill)

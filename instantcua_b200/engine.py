@@ -1,8 +1,9 @@
 """Python mirror of the reference ``Engine`` (Sources/Engine/Engine.swift) over the C ABI.
 
 Same names and meaning as the Swift class where the path overlaps:
-``Engine(model_path, max_context, max_pass, max_steps)``, ``generate_vision`` (generateVision
-without the ViT: visual rows are inputs), ``last_timing`` (Engine.Timing), ``eos``.  Errors
+``Engine(model_path, max_context, max_pass, max_steps)``, ``generate_rgb`` (generateVision: vision
+encoder on an RGB image, then the token loop), ``generate_vision`` (the same with the visual rows as
+inputs), ``encode_vision`` (encodeVision), ``last_timing`` (Engine.Timing), ``eos``.  Errors
 raise :class:`IcuaError` carrying the engine's message (the reference throws EngineError).
 """
 from __future__ import annotations
@@ -129,6 +130,34 @@ class Engine:
                                         C.byref(vis) if vis is not None else None, max_new_tokens,
                                         int(write_first_logits), out.ctypes.data_as(L._IP), C.byref(n)), self._h)
         del keep
+        return out[: n.value].tolist()
+
+    def encode_vision(self, rgb) -> tuple:
+        """Vision encoder + mergers on an RGB8 image [height, width, 3] (reference encodeVision,
+        Engine.swift:317-473).  Returns (pooler [n_vis, 2048], deepstack [3, n_vis, 2048]) as host
+        copies; the rows also stay on the device for the next prompt (``generate_rgb``)."""
+        img = np.ascontiguousarray(rgb, np.uint8)
+        h, w = img.shape[:2]
+        nv = (h // 32) * (w // 32)
+        pooler = np.zeros((max(nv, 1), 2048), np.float32)
+        ds = np.zeros((3, max(nv, 1), 2048), np.float32)
+        n = C.c_int32()
+        L.check(self._lib.icua_encode_vision(self._h, img.ctypes.data, w, h, pooler.ctypes.data, ds.ctypes.data,
+                                             C.byref(n)), self._h)
+        return pooler[: n.value], ds[:, : n.value]
+
+    def generate_rgb(self, rgb, tokens, max_new_tokens: int = 64, write_first_logits: bool = False,
+                     session: int = 0) -> list:
+        """Engine.generateVision(rgbBytes:width:height:tokens:...): vision encoder on the image, then
+        prefill (the prompt's IMAGE_PAD block takes the encoder's rows) and greedy decode."""
+        img = np.ascontiguousarray(rgb, np.uint8)
+        h, w = img.shape[:2]
+        toks = np.ascontiguousarray(tokens, np.int32)
+        out = np.zeros(max(max_new_tokens, 1), np.int32)
+        n = C.c_int32()
+        L.check(self._lib.icua_generate_rgb(self._h, session, img.ctypes.data, w, h, toks.ctypes.data_as(L._IP),
+                                            len(toks), max_new_tokens, int(write_first_logits),
+                                            out.ctypes.data_as(L._IP), C.byref(n)), self._h)
         return out[: n.value].tolist()
 
     def reset(self, session: int = 0) -> None:

@@ -126,6 +126,25 @@ def quantize_stream(fp32_stream, keep_fp32: bool = False, fmt: int = L.FMT_Q4S):
     return (out, raw) if keep_fp32 else out
 
 
+VISION_TENSORS = 315  # reference TensorID 0..314 (ModelFile.swift:73-99)
+
+
+def vision_tensors(named: dict) -> dict:
+    """Vision encoder tensors in the file's storage types (Convert.swift:99-152) keyed by reference
+    tensor id: the matrices (patch embedding [1024, 768] with the temporal frames folded, QKV,
+    projection, MLP, merger layers) as fp16 [out, in], biases, norms and the position table fp32.
+    ``named``: fp32 arrays under the names of ``oracle.qwen3vl_vision.weight_names`` order, which
+    is the id order."""
+    mats = ("patch_w", "qkv_w", "proj_w", "fc1_w", "fc2_w")
+    out = {}
+    for tid, (name, arr) in enumerate(named.items()):
+        a = np.asarray(arr)
+        short = name.split(".")[-1]
+        out[tid] = np.ascontiguousarray(a, np.float16 if short in mats else np.float32).tobytes()
+    assert len(out) == VISION_TENSORS, len(out)
+    return out
+
+
 def write_icua(path: str, tensors: dict, fmt: int = L.FMT_Q4S) -> None:
     """Writes an .icua file (ModelFile.swift:164-195 layout): 16 KiB header with magic, version 1,
     format, tensor count and an (offset, size) u64 table; tensors 256-byte aligned; the file
