@@ -448,6 +448,66 @@ def run_gemm(args):
 
 
 N_VIS, LLM_H, LLM_W, N_TEXT, PREFILL_DECODE = 1000, 25, 40, 256, 32
+VIS_H, VIS_W = LLM_H * 32, LLM_W * 32  # the config-3 image: 800 x 1280 pixels, 50 x 80 patches
+
+
+def vision_flops(n_patch: int) -> int:
+    """Algorithmic FLOPs of one encode: 24 blocks of QKV / projection / MLP GEMMs (2 x 12.58 M
+    weights per patch) and bidirectional attention (QK^T and PV: 4 n^2 x 1024), the patch
+    embedding, and the four mergers (2 x 25.2 M weights per merged row)."""
+    nv = n_patch // 4
+    blocks = 24 * (2 * (3072 * 1024 + 1024 * 1024 + 4096 * 1024 + 1024 * 4096) * n_patch + 4 * n_patch * n_patch * 1024)
+    return blocks + 2 * n_patch * 1024 * 768 + 4 * nv * 2 * (4096 * 4096 + 2048 * 4096)
+
+
+def run_vision(args):
+    """The vision encoder + mergers on a config-3 sized image (800 x 1280, 4000 patches, 1000 visual
+    tokens) with seeded synthetic fp16 weights: value = patches per second of device time
+    (CUDA events around the encode), roofline = algorithmic TFLOP/s against the measured
+    sustained bf16 peak; e2e = icua_encode_vision from host RGB to host pooler / DeepStack rows."""
+    import numpy as np
+    import torch
+
+    from instantcua_b200 import Engine, model
+
+    torch.cuda.set_device(0)
+    eng = Engine(max_context=64, max_pass=N_VIS, max_steps=8, kv_dtype="bf16")
+    eng.set_tensors(model.synthetic_vision_fast(seed=7), ready=False)
+    rgb = np.random.default_rng(5).integers(0, 256, (VIS_H, VIS_W, 3), dtype=np.uint8)
+    K, W = args.steps, args.warmup
+    for _ in range(max(W, 1)):
+        eng.encode_vision(rgb)
+    dev_ms, wall_ms = [], []
+    with Clocks(0) as clk:
+        for _ in range(K):
+            t0 = time.perf_counter()
+            pooler, ds = eng.encode_vision(rgb)
+            wall_ms.append((time.perf_counter() - t0) * 1e3)
+            dev_ms.append(eng.last_timing.vision_ms)
+    eng.close()
+    n_patch = (VIS_H // 16) * (VIS_W // 16)
+    med = statistics.median(dev_ms)
+    fl = vision_flops(n_patch)
+    peaks_d = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    tpk = float(peaks_d.get("bf16_tflops_sustained", 1400.0))
+    ach = fl / (med / 1e3) / 1e12
+    print(json.dumps({
+        "metric": "vision encoder patches/s (config 3 image, 800x1280)", "value": round(n_patch / (med / 1e3), 1),
+        "unit": "patches/s", "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": round(med, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp16 operands, fp32 accumulate (fp16 q/k/v, probabilities, GEMM inputs)",
+        "data": "synthetic (seeded fp16 weights, uniform RGB8 image)",
+        "config": {"workload": f"vision encoder + 3 DeepStack mergers + final merger, {n_patch} patches -> "
+                               f"{n_patch // 4} visual rows", "image": [VIS_H, VIS_W]},
+        "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": tpk, "unit": "TFLOP/s",
+                     "frac": round(ach / tpk, 4), "traffic": None,
+                     "note": f"{fl / 1e12:.3f} TFLOP per encode (GEMMs + attention + mergers); peak: measured sustained bf16"},
+        "e2e": {"value": round(statistics.median(wall_ms), 2), "unit": "ms per image",
+                "h2d_bytes_per_step": int(VIS_H * VIS_W * 3), "d2h_bytes_per_step": int(4 * pooler.size + 4 * ds.size),
+                "api": "icua_encode_vision (host RGB8 in, host pooler + DeepStack rows out)"},
+        "clocks": clk.summary(),
+    }))
 LAYER_PARAMS = {"qkv": 4096 * 2048, "o": 2048 * 2048, "gu": 12288 * 2048, "d": 2048 * 6144}
 
 
@@ -640,10 +700,11 @@ def main():
     ap.add_argument("--prefill", action="store_true", help="config 3: multimodal prefill through the GEMM path")
     ap.add_argument("--batched", action="store_true", help="config 4: 64 sessions decoded together")
     ap.add_argument("--gemm", action="store_true", help="the prefill GEMMs alone (config 3 shapes)")
+    ap.add_argument("--vision", action="store_true", help="the vision encoder on a config-3 sized image")
     ap.add_argument("--batch-ctx", type=int, default=BATCH_CTX,
                     help="--batched: KV positions per session (config 4: 2048; smaller for ncu captures)")
     args = ap.parse_args()
-    if args.warmup < 3 and not (args.prefill or args.batched or args.micro or args.gemm):
+    if args.warmup < 3 and not (args.prefill or args.batched or args.micro or args.gemm or args.vision):
         args.warmup = 3  # the headline bench always warms up; the side modes allow short profiling runs
     if args.impl == "reference":
         run_reference(args)
@@ -655,6 +716,8 @@ def main():
         run_batched(args)
     elif args.gemm:
         run_gemm(args)
+    elif args.vision:
+        run_vision(args)
     else:
         run_ours(args)
 

@@ -160,6 +160,7 @@ struct icua_engine {
     __half *vpatch = nullptr, *vxn = nullptr, *vq = nullptr, *vk = nullptr, *vv = nullptr, *vattn = nullptr,
            *vh = nullptr;
     float *vx = nullptr, *vqkv = nullptr;
+    float2* vrope = nullptr;
     int vis_rows = -1;
 };
 
@@ -2345,6 +2346,7 @@ static cudaError_t record_vision(icua_engine* e, int gh, int gw) {
     } while (0)
     VK(launch(vit_patchify_kernel, np, 256, 0, st, false, (const uint8_t*)e->vrgb, gh, gw, e->vpatch));
     VK(launch(vit_pos_init_kernel, np, 256, 0, st, false, F(2), gh, gw, e->vx));
+    VK(launch(vit_rope_table_kernel, (np * 32 + 255) / 256, 256, 0, st, false, np, gw, e->vrope));
     VK(vit_gemm(e, TC_RESID, e->vpatch, NP, np, VIT_HIDDEN, VIT_PATCH_DIM, T(0), T(1), e->vx, VIT_HIDDEN, nullptr, 0, 0));
     const int ds_layer[3] = {5, 11, 17};
     for (int l = 0; l < VIT_LAYERS; ++l) {
@@ -2352,7 +2354,8 @@ static cudaError_t record_vision(icua_engine* e, int gh, int gw) {
         VK(launch(vit_layernorm_kernel, np, 256, 0, st, false, (const float*)e->vx, F(b + 0), F(b + 1), VIT_HIDDEN,
                   e->vxn));
         VK(vit_gemm(e, TC_STORE, e->vxn, NP, np, VIT_QKV, VIT_HIDDEN, T(b + 2), T(b + 3), e->vqkv, VIT_QKV, nullptr, 0, 0));
-        VK(launch(vit_qkv_rope_kernel, np, 256, 0, st, false, (const float*)e->vqkv, np, gw, e->vq, e->vk, e->vv));
+        VK(launch(vit_qkv_rope_kernel, np, 256, 0, st, false, (const float*)e->vqkv, (const float2*)e->vrope, np,
+                  e->vq, e->vk, e->vv));
         {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3((np + VA_BQ - 1) / VA_BQ, VIT_HEADS);
@@ -2411,7 +2414,8 @@ icua_status icua_encode_vision(icua_engine* eng, const uint8_t* rgb, int32_t wid
             (s = dalloc_t(eng, &eng->vk, NP * VIT_HIDDEN)) != ICUA_OK ||
             (s = dalloc_t(eng, &eng->vv, NP * VIT_HIDDEN)) != ICUA_OK ||
             (s = dalloc_t(eng, &eng->vattn, NP * VIT_HIDDEN)) != ICUA_OK ||
-            (s = dalloc_t(eng, &eng->vh, NP * VIT_FF)) != ICUA_OK)
+            (s = dalloc_t(eng, &eng->vh, NP * VIT_FF)) != ICUA_OK ||
+            (s = dalloc_t(eng, &eng->vrope, NP * 32)) != ICUA_OK)
             return s;
         cudaMemset(eng->vxn, 0, NP * VIT_HIDDEN * sizeof(__half));  // rows past a call's patches read by TMA
         cudaMemset(eng->vh, 0, NP * VIT_FF * sizeof(__half));

@@ -124,23 +124,32 @@ __global__ void __launch_bounds__(256) vit_layernorm_kernel(const float* x, cons
         }
 }
 
-// qkv [n][3072] fp32 (bias added by the GEMM) -> head-major fp16 q, k, v [16][n][64], q and k
-// rotated by the 2-D RoPE (rotate-half pairs d, d + 32 share the angle: frequencies 0..7 of the
-// patch row, 8..15 of the column, qwen3vl_ref.py:71-84, 184-186).  One CTA per patch; thread
-// (head, pair) for q and k, plain copies for v.
-__global__ void __launch_bounds__(256) vit_qkv_rope_kernel(const float* qkv, int n, int gw, __half* q, __half* k,
-                                                           __half* v) {
-    const int p = blockIdx.x;
+// 2-D RoPE table of an image: rope[p][d] = (cos, sin) of angle d of patch p for the rotate-half
+// pairs (d, d + 32), d < 32: frequencies 0..15 (1 / 10000^(2f/32)) times the patch row for
+// d < 16, times the column for d >= 16 (qwen3vl_ref.py:71-84).  Computed once per image.
+__global__ void __launch_bounds__(256) vit_rope_table_kernel(int n, int gw, float2* rope) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * 32) return;
+    const int p = i >> 5, d = i & 31, f = d & 15;
     int r, c;
     vit_patch_rc(p, gw, r, c);
+    const float inv = powf(10000.0f, -(float)(2 * f) / 32.0f);
+    float sn, cs;
+    sincosf((float)(d < 16 ? r : c) * inv, &sn, &cs);
+    rope[i] = make_float2(cs, sn);
+}
+
+// qkv [n][3072] fp32 (bias added by the GEMM) -> head-major fp16 q, k, v [16][n][64], q and k
+// rotated by the 2-D RoPE table (qwen3vl_ref.py:184-186).  One CTA per patch; thread
+// (head, pair) for q and k, plain copies for v.
+__global__ void __launch_bounds__(256) vit_qkv_rope_kernel(const float* qkv, const float2* rope, int n, __half* q,
+                                                           __half* k, __half* v) {
+    const int p = blockIdx.x;
     const float* row = qkv + (size_t)p * VIT_QKV;
     for (int i = threadIdx.x; i < 2 * VIT_HEADS * 32; i += blockDim.x) {
         const int which = i >> 9, h = (i >> 5) & 15, d = i & 31;  // which: 0 q, 1 k
-        const int f = d & 15;                                     // frequency index
-        const float inv = powf(10000.0f, -(float)(2 * f) / 32.0f);
-        const float ang = (float)(d < 16 ? r : c) * inv;
-        float sn, cs;
-        sincosf(ang, &sn, &cs);
+        const float2 csn = rope[p * 32 + d];
+        const float cs = csn.x, sn = csn.y;
         const float* src = row + which * VIT_HIDDEN + h * VIT_HD;
         const float a = src[d], b = src[d + 32];
         __half* dst = (which ? k : q) + ((size_t)h * n + p) * VIT_HD;
@@ -154,7 +163,7 @@ __global__ void __launch_bounds__(256) vit_qkv_rope_kernel(const float* qkv, int
 }
 
 // ---- bidirectional attention ------------------------------------------------------------------
-constexpr int VA_BQ = 64;       // queries per CTA (4 warps x 16)
+constexpr int VA_BQ = 64;       // queries per CTA (4 warps x 16; 128 measured 6% slower)
 constexpr int VA_BK = 64;       // keys per block
 constexpr int VA_THREADS = 128;
 

@@ -67,12 +67,15 @@ class Engine:
             self.set_tensors(tensors)
 
     # -- weights ---------------------------------------------------------------------------------
-    def set_tensors(self, tensors: dict) -> None:
+    def set_tensors(self, tensors: dict, ready: bool = True) -> None:
+        """Uploads {tensor id: bytes}; ``ready`` then requires the language model to be complete
+        (False for vision tensors alone)."""
         for tid in sorted(tensors):
             data = tensors[tid]
             buf = C.create_string_buffer(data, len(data)) if isinstance(data, (bytes, bytearray)) else data
             L.check(self._lib.icua_engine_set_tensor(self._h, tid, buf, len(data)), self._h)
-        L.check(self._lib.icua_engine_ready(self._h), self._h)
+        if ready:
+            L.check(self._lib.icua_engine_ready(self._h), self._h)
 
     # -- reference properties ----------------------------------------------------------------------
     @property

@@ -129,19 +129,62 @@ def quantize_stream(fp32_stream, keep_fp32: bool = False, fmt: int = L.FMT_Q4S):
 VISION_TENSORS = 315  # reference TensorID 0..314 (ModelFile.swift:73-99)
 
 
+def vision_shapes():
+    """(shape, dtype) of each vision tensor by reference id (ModelFile.swift:73-99, storage types of
+    Convert.swift:99-152): patch matrix, patch bias, position table; 24 blocks of (norm1 w/b, qkv
+    w/b, proj w/b, norm2 w/b, fc1 w/b, fc2 w/b); 3 DeepStack mergers and the final merger of
+    (norm w/b, fc1 w/b, fc2 w/b)."""
+    f16, f32 = np.float16, np.float32
+    out = [((1024, 768), f16), ((1024,), f32), ((2304, 1024), f32)]
+    for _ in range(24):
+        out += [((1024,), f32), ((1024,), f32), ((3072, 1024), f16), ((3072,), f32), ((1024, 1024), f16),
+                ((1024,), f32), ((1024,), f32), ((1024,), f32), ((4096, 1024), f16), ((4096,), f32),
+                ((1024, 4096), f16), ((1024,), f32)]
+    for m in range(4):
+        norm = 1024 if m == 3 else 4096
+        out += [((norm,), f32), ((norm,), f32), ((4096, 4096), f16), ((4096,), f32), ((2048, 4096), f16),
+                ((2048,), f32)]
+    assert len(out) == VISION_TENSORS
+    return out
+
+
+def synthetic_vision_fast(seed: int = 0, device: int = 0, std: float = 0.02) -> dict:
+    """Seeded synthetic vision tensors drawn on the GPU (torch) in their storage types: matrices and
+    biases N(0, std), norm weights 1, norm biases 0, position table N(0, 0.5).  {id: bytes}."""
+    import torch
+
+    g = torch.Generator(device=f"cuda:{device}").manual_seed(seed)
+    out = {}
+    for tid, (shape, dt) in enumerate(vision_shapes()):
+        if tid == 2:
+            a = torch.randn(shape, generator=g, device=f"cuda:{device}") * 0.5
+        elif len(shape) == 1 and ((tid >= 3 and tid < 291 and (tid - 3) % 12 in (0, 6)) or
+                                  (tid >= 291 and (tid - 291) % 6 == 0)):
+            a = torch.ones(shape, device=f"cuda:{device}")
+        elif len(shape) == 1 and ((tid >= 3 and tid < 291 and (tid - 3) % 12 in (1, 7)) or
+                                  (tid >= 291 and (tid - 291) % 6 == 1)):
+            a = torch.zeros(shape, device=f"cuda:{device}")
+        else:
+            a = torch.randn(shape, generator=g, device=f"cuda:{device}") * std
+        a = a.half() if dt == np.float16 else a.float()
+        out[tid] = a.cpu().numpy().tobytes()
+    return out
+
+
 def vision_tensors(named: dict) -> dict:
     """Vision encoder tensors in the file's storage types (Convert.swift:99-152) keyed by reference
     tensor id: the matrices (patch embedding [1024, 768] with the temporal frames folded, QKV,
     projection, MLP, merger layers) as fp16 [out, in], biases, norms and the position table fp32.
     ``named``: fp32 arrays under the names of ``oracle.qwen3vl_vision.weight_names`` order, which
     is the id order."""
-    mats = ("patch_w", "qkv_w", "proj_w", "fc1_w", "fc2_w")
+    shapes = vision_shapes()
+    assert len(named) == VISION_TENSORS, len(named)
     out = {}
-    for tid, (name, arr) in enumerate(named.items()):
-        a = np.asarray(arr)
-        short = name.split(".")[-1]
-        out[tid] = np.ascontiguousarray(a, np.float16 if short in mats else np.float32).tobytes()
-    assert len(out) == VISION_TENSORS, len(out)
+    for tid, arr in enumerate(named.values()):
+        shape, dt = shapes[tid]
+        a = np.ascontiguousarray(arr, dt)
+        assert a.shape == shape, (tid, a.shape, shape)
+        out[tid] = a.tobytes()
     return out
 
 
