@@ -36,6 +36,7 @@
 #include "misc.cuh"
 #include "prefill.cuh"
 #include "vision.cuh"
+#include "attn_tc.cuh"
 
 namespace icua_host {
 uint16_t f32_to_f16_bits(float f);
@@ -157,10 +158,10 @@ struct icua_engine {
     int vit_count = 0;
     int vit_np_max = 0;
     uint8_t* vrgb = nullptr;
-    __half *vpatch = nullptr, *vxn = nullptr, *vq = nullptr, *vk = nullptr, *vv = nullptr, *vattn = nullptr,
-           *vh = nullptr;
+    __half *vpatch = nullptr, *vxn = nullptr, *vq = nullptr, *vk = nullptr, *vattn = nullptr, *vh = nullptr;
     float *vx = nullptr, *vqkv = nullptr;
     float2* vrope = nullptr;
+    __half* vvt = nullptr;  // V^T per head [16][64][vit_np_max + 8]
     int vis_rows = -1;
 };
 
@@ -515,6 +516,9 @@ cudaError_t set_smem_attrs() {
         if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)) != cudaSuccess)
             return e;
     }
+    if ((e = cudaFuncSetAttribute(vit_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  VitAttnSmem::alloc)) != cudaSuccess)
+        return e;
     for (const void* k : {(const void*)prefill_attn_kernel<__half>, (const void*)prefill_attn_kernel<__nv_bfloat16>}) {
         if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       PrefillAttnSmem<__half>::total)) != cudaSuccess)
@@ -2336,8 +2340,30 @@ static cudaError_t vit_gemm(icua_engine* e, int epi, const void* x, int rows_all
 // patch embedding, 24 blocks (the DeepStack mergers after blocks 5, 11, 17), final merger.
 static cudaError_t record_vision(icua_engine* e, int gh, int gw) {
     const int np = gh * gw, nv = np / 4, NP = e->vit_np_max, NV = NP / 4;
+    const int npad = (np + 7) / 8 * 8;  // V^T row length: 16-byte row stride for TMA
     cudaStream_t st = e->stream;
     cudaError_t err;
+    // per-head 3-D maps of q, k [16][np][64] and V^T [16][64][np (rows of npad)]; rows past np
+    // read as zeros
+    CUtensorMap qmap, kmap, vtmap;
+    {
+        auto enc = tensor_map_encoder();
+        if (!enc) return cudaErrorNotSupported;
+        const cuuint32_t es[3] = {1, 1, 1};
+        const cuuint64_t dq[3] = {VIT_HD, (cuuint64_t)np, VIT_HEADS};
+        const cuuint64_t sq[2] = {VIT_HD * 2, (cuuint64_t)np * VIT_HD * 2};
+        const cuuint32_t bq[3] = {VIT_HD, VT_BQ, 1}, bk[3] = {VIT_HD, VT_BK, 1};
+        const cuuint64_t dv[3] = {(cuuint64_t)np, VIT_HD, VIT_HEADS};
+        const cuuint64_t sv[2] = {(cuuint64_t)npad * 2, (cuuint64_t)npad * VIT_HD * 2};
+        const cuuint32_t bv[3] = {VT_BK, VIT_HD, 1};
+        auto make = [&](CUtensorMap* m, void* base, const cuuint64_t* d, const cuuint64_t* str, const cuuint32_t* b) {
+            return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, d, str, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        };
+        if (!make(&qmap, e->vq, dq, sq, bq) || !make(&kmap, e->vk, dq, sq, bk) || !make(&vtmap, e->vvt, dv, sv, bv))
+            return cudaErrorInvalidValue;
+    }
     auto T = [&](int id) { return e->vit[id]; };
     auto F = [&](int id) { return static_cast<const float*>(e->vit[id]); };
 #define VK(...)                                        \
@@ -2355,14 +2381,21 @@ static cudaError_t record_vision(icua_engine* e, int gh, int gw) {
                   e->vxn));
         VK(vit_gemm(e, TC_STORE, e->vxn, NP, np, VIT_QKV, VIT_HIDDEN, T(b + 2), T(b + 3), e->vqkv, VIT_QKV, nullptr, 0, 0));
         VK(launch(vit_qkv_rope_kernel, np, 256, 0, st, false, (const float*)e->vqkv, (const float2*)e->vrope, np,
-                  e->vq, e->vk, e->vv));
+                  e->vq, e->vk));
         {
             cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3((np + VA_BQ - 1) / VA_BQ, VIT_HEADS);
-            cfg.blockDim = dim3(VA_THREADS);
+            cfg.gridDim = dim3((np + 31) / 32, VIT_HIDDEN / 32);
+            cfg.blockDim = dim3(32, 8);
             cfg.stream = st;
-            VK(cudaLaunchKernelEx(&cfg, vit_attn_kernel, (const __half*)e->vq, (const __half*)e->vk,
-                                  (const __half*)e->vv, np, e->vattn));
+            VK(cudaLaunchKernelEx(&cfg, vit_vt_kernel, (const float*)e->vqkv, np, npad, e->vvt));
+        }
+        {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((np + VT_BQ - 1) / VT_BQ, VIT_HEADS);
+            cfg.blockDim = dim3(VT_THREADS);
+            cfg.dynamicSmemBytes = VitAttnSmem::alloc;
+            cfg.stream = st;
+            VK(cudaLaunchKernelEx(&cfg, vit_attn_tc_kernel, qmap, kmap, vtmap, np, e->vattn, e->gemm_err));
         }
         VK(vit_gemm(e, TC_RESID, e->vattn, NP, np, VIT_HIDDEN, VIT_HIDDEN, T(b + 4), T(b + 5), e->vx, VIT_HIDDEN, nullptr,
                     0, 0));
@@ -2412,10 +2445,10 @@ icua_status icua_encode_vision(icua_engine* eng, const uint8_t* rgb, int32_t wid
             (s = dalloc_t(eng, &eng->vqkv, NP * VIT_QKV)) != ICUA_OK ||
             (s = dalloc_t(eng, &eng->vq, NP * VIT_HIDDEN)) != ICUA_OK ||
             (s = dalloc_t(eng, &eng->vk, NP * VIT_HIDDEN)) != ICUA_OK ||
-            (s = dalloc_t(eng, &eng->vv, NP * VIT_HIDDEN)) != ICUA_OK ||
             (s = dalloc_t(eng, &eng->vattn, NP * VIT_HIDDEN)) != ICUA_OK ||
             (s = dalloc_t(eng, &eng->vh, NP * VIT_FF)) != ICUA_OK ||
-            (s = dalloc_t(eng, &eng->vrope, NP * 32)) != ICUA_OK)
+            (s = dalloc_t(eng, &eng->vrope, NP * 32)) != ICUA_OK ||
+            (s = dalloc_t(eng, &eng->vvt, (NP + 8) * VIT_HIDDEN)) != ICUA_OK)
             return s;
         cudaMemset(eng->vxn, 0, NP * VIT_HIDDEN * sizeof(__half));  // rows past a call's patches read by TMA
         cudaMemset(eng->vh, 0, NP * VIT_FF * sizeof(__half));

@@ -1,18 +1,15 @@
 // Vision encoder row kernels around the tensor-core GEMM (fp16 weights): patchify, position
-// resampling, LayerNorm into fp16 GEMM inputs, QKV bias-free split with 2-D RoPE into head-major
-// fp16, and bidirectional multi-head attention.
+// resampling, LayerNorm into fp16 GEMM inputs, and the split of q / k with 2-D RoPE into
+// head-major fp16.
 //
 // Replaces the reference's k_vit_patchify_rgb (Shaders.swift:82-110), k_vit_ln1024 / k_vit_ln4096
-// (112-200), the epilogue of k_vit_qkv (202-290: bias, 2-D RoPE, head-major fp16 q / k / v) and
-// k_vit_attn (292-395, scores and probabilities in threadgroup memory); the GEMMs themselves
-// (patch embedding, QKV, projection, MLP, mergers; k_vit_gemm_T 396-454) run on tc_gemm_kernel
-// with fp16 weights and the store / residual / GELU epilogues.
+// (112-200) and the epilogue of k_vit_qkv (202-290: bias, 2-D RoPE, head-major fp16 q / k / v);
+// the GEMMs themselves (patch embedding, QKV, projection, MLP, mergers; k_vit_gemm_T 396-454) run
+// on tc_gemm_kernel with fp16 weights and the store / residual / GELU epilogues, the attention
+// (k_vit_attn 292-395) on vit_attn_tc_kernel (attn_tc.cuh).
 //
-// Design (B200): one CTA per row for the row kernels; attention is a flash kernel on the tensor
-// cores (mma.sync m16n8k16, fp16 operands, fp32 accumulation, online softmax in registers, K / V
-// tiles double-buffered through cp.async), 64 queries x one head per CTA, the score matrix never
-// leaves registers.  Patches are kept in the 2x2 merge-block order throughout, so the mergers'
-// [n / 4, 4096] inputs are views of the [n, 1024] rows.
+// Design (B200): one CTA per row for the row kernels.  Patches are kept in the 2x2 merge-block
+// order throughout, so the mergers' [n / 4, 4096] inputs are views of the [n, 1024] rows.
 #pragma once
 #include "common.cuh"
 
@@ -139,11 +136,11 @@ __global__ void __launch_bounds__(256) vit_rope_table_kernel(int n, int gw, floa
     rope[i] = make_float2(cs, sn);
 }
 
-// qkv [n][3072] fp32 (bias added by the GEMM) -> head-major fp16 q, k, v [16][n][64], q and k
-// rotated by the 2-D RoPE table (qwen3vl_ref.py:184-186).  One CTA per patch; thread
-// (head, pair) for q and k, plain copies for v.
+// qkv [n][3072] fp32 (bias added by the GEMM) -> head-major fp16 q, k [16][n][64] rotated by the
+// 2-D RoPE table (qwen3vl_ref.py:184-186); v goes to V^T (vit_vt_kernel).  One CTA per patch,
+// thread (head, pair).
 __global__ void __launch_bounds__(256) vit_qkv_rope_kernel(const float* qkv, const float2* rope, int n, __half* q,
-                                                           __half* k, __half* v) {
+                                                           __half* k) {
     const int p = blockIdx.x;
     const float* row = qkv + (size_t)p * VIT_QKV;
     for (int i = threadIdx.x; i < 2 * VIT_HEADS * 32; i += blockDim.x) {
@@ -155,184 +152,6 @@ __global__ void __launch_bounds__(256) vit_qkv_rope_kernel(const float* qkv, con
         __half* dst = (which ? k : q) + ((size_t)h * n + p) * VIT_HD;
         dst[d] = __float2half_rn(a * cs - b * sn);
         dst[d + 32] = __float2half_rn(b * cs + a * sn);
-    }
-    for (int i = threadIdx.x; i < VIT_HIDDEN; i += blockDim.x) {
-        const int h = i >> 6, d = i & 63;
-        v[((size_t)h * n + p) * VIT_HD + d] = __float2half_rn(row[2 * VIT_HIDDEN + i]);
-    }
-}
-
-// ---- bidirectional attention ------------------------------------------------------------------
-constexpr int VA_BQ = 64;       // queries per CTA (4 warps x 16; 128 measured 6% slower)
-constexpr int VA_BK = 64;       // keys per block
-constexpr int VA_THREADS = 128;
-
-__device__ __forceinline__ void va_ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
-}
-__device__ __forceinline__ void va_ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(addr));
-}
-__device__ __forceinline__ void va_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void va_cp16(uint32_t dst, const void* src, bool valid) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
-}
-// 16-byte chunk j of a 128-byte tile row r, XOR-swizzled so ldmatrix rows hit distinct banks
-__device__ __forceinline__ int va_swz(int r, int j) { return r * 128 + ((j ^ (r & 7)) << 4); }
-
-// Scaled dot-product attention over all n patches (no mask), softmax in fp32, probabilities
-// rounded to fp16 for the PV product (as the reference's fp16 vprobs).  Grid (ceil(n / 64), 16).
-__global__ void __launch_bounds__(VA_THREADS) vit_attn_kernel(const __half* q, const __half* k, const __half* v, int n,
-                                                              __half* out) {
-    __shared__ __align__(128) uint8_t sm[VA_BQ * 128 + 2 * 2 * VA_BK * 128];  // Q, then K / V double buffers
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int h = blockIdx.y, q0 = blockIdx.x * VA_BQ;
-    const __half* qh = q + (size_t)h * n * VIT_HD;
-    const __half* kh = k + (size_t)h * n * VIT_HD;
-    const __half* vh = v + (size_t)h * n * VIT_HD;
-    const uint32_t sq = smem_u32(sm), skv = sq + VA_BQ * 128;
-    auto kbuf = [&](int b) { return skv + b * 2 * VA_BK * 128; };
-    auto vbuf = [&](int b) { return skv + b * 2 * VA_BK * 128 + VA_BK * 128; };
-    // Q tile (rows past n read as zeros)
-    for (int i = threadIdx.x; i < VA_BQ * 8; i += VA_THREADS) {
-        const int r = i >> 3, j = i & 7;
-        const bool ok = q0 + r < n;
-        va_cp16(sq + va_swz(r, j), qh + (size_t)(ok ? q0 + r : 0) * VIT_HD + j * 8, ok);
-    }
-    auto load_kv = [&](int blk, int b) {
-        const int k0 = blk * VA_BK;
-        for (int i = threadIdx.x; i < VA_BK * 8; i += VA_THREADS) {
-            const int r = i >> 3, j = i & 7;
-            const bool ok = k0 + r < n;
-            const size_t off = (size_t)(ok ? k0 + r : 0) * VIT_HD + j * 8;
-            va_cp16(kbuf(b) + va_swz(r, j), kh + off, ok);
-            va_cp16(vbuf(b) + va_swz(r, j), vh + off, ok);
-        }
-    };
-    const int nblk = (n + VA_BK - 1) / VA_BK;
-    load_kv(0, 0);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    // Q fragments of this warp's 16 rows: 4 k-steps of 16 dims
-    uint32_t qa[4][4];
-    float o[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows g and g + 8
-    const float sl2 = 0.125f * 1.4426950408889634f;             // 1/sqrt(64) * log2(e)
-    for (int blk = 0; blk < nblk; ++blk) {
-        const int b = blk & 1;
-        if (blk + 1 < nblk) load_kv(blk + 1, b ^ 1);
-        asm volatile("cp.async.commit_group;" ::: "memory");
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-        __syncthreads();
-        if (blk == 0) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const int r = warp * 16 + (lane & 15), j = 2 * kk + (lane >> 4);
-                va_ldsm_x4(qa[kk], sq + va_swz(r, j));
-            }
-        }
-        // S = Q K^T for 64 keys: 8 n-tiles of 8 keys
-        float s[8][4];
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-#pragma unroll
-        for (int nt = 0; nt < 8; nt += 2) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                // keys nt*8 .. nt*8+15 (two n-tiles), dims kk*16 .. +15
-                uint32_t kb[4];
-                const int r = nt * 8 + (lane & 7) + ((lane >> 4) << 3), j = 2 * kk + ((lane >> 3) & 1);
-                va_ldsm_x4(kb, kbuf(b) + va_swz(r, j));
-                va_mma(s[nt], qa[kk], kb[0], kb[1]);
-                va_mma(s[nt + 1], qa[kk], kb[2], kb[3]);
-            }
-        }
-        // mask keys past n, online softmax (base 2)
-        const int k0 = blk * VA_BK;
-        float bm0 = -INFINITY, bm1 = -INFINITY;
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int key = k0 + nt * 8 + 2 * t + (e & 1);
-                s[nt][e] = key < n ? s[nt][e] * sl2 : -INFINITY;
-            }
-            bm0 = fmaxf(bm0, fmaxf(s[nt][0], s[nt][1]));
-            bm1 = fmaxf(bm1, fmaxf(s[nt][2], s[nt][3]));
-        }
-        bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, 1));
-        bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, 2));
-        bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, 1));
-        bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, 2));
-        const float nm0 = fmaxf(m0, bm0), nm1 = fmaxf(m1, bm1);
-        const float c0 = exp2f(m0 - nm0), c1 = exp2f(m1 - nm1);  // m = -inf at first: 0
-        m0 = nm0;
-        m1 = nm1;
-        float rs0 = 0.f, rs1 = 0.f;
-        uint32_t pa[4][4];  // P as the A operand: k-step kk covers keys kk*16 .. +15 (n-tiles 2kk, 2kk+1)
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            const float p0 = exp2f(s[nt][0] - m0), p1 = exp2f(s[nt][1] - m0);
-            const float p2 = exp2f(s[nt][2] - m1), p3 = exp2f(s[nt][3] - m1);
-            const __half2 h01 = __floats2half2_rn(p0, p1), h23 = __floats2half2_rn(p2, p3);
-            // the row sums use the fp16 probabilities that enter the PV product
-            rs0 += __low2float(h01) + __high2float(h01);
-            rs1 += __low2float(h23) + __high2float(h23);
-            const int kk = nt >> 1, hi = nt & 1;
-            pa[kk][hi * 2 + 0] = *reinterpret_cast<const uint32_t*>(&h01);
-            pa[kk][hi * 2 + 1] = *reinterpret_cast<const uint32_t*>(&h23);
-        }
-        l0 = l0 * c0 + rs0;
-        l1 = l1 * c1 + rs1;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            o[j][0] *= c0;
-            o[j][1] *= c0;
-            o[j][2] *= c1;
-            o[j][3] *= c1;
-        }
-        // O += P V: 8 n-tiles of 8 dims, 4 k-steps of 16 keys; V^T fragments by ldmatrix.trans
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-            for (int j = 0; j < 8; j += 2) {
-                uint32_t vb[4];
-                const int r = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), c = j + (lane >> 4);
-                va_ldsm_x4_t(vb, vbuf(b) + va_swz(r, c));
-                va_mma(o[j], pa[kk], vb[0], vb[1]);
-                va_mma(o[j + 1], pa[kk], vb[2], vb[3]);
-            }
-        }
-        __syncthreads();  // the buffer is refilled two blocks later
-    }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    // row sums over the quad, normalise, store fp16 [n][1024] at column h * 64
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    const float i0 = 1.0f / l0, i1 = 1.0f / l1;
-    const int ra = q0 + warp * 16 + g, rb = ra + 8;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int d = j * 8 + 2 * t;
-        if (ra < n)
-            *reinterpret_cast<__half2*>(out + (size_t)ra * VIT_HIDDEN + h * VIT_HD + d) =
-                __floats2half2_rn(o[j][0] * i0, o[j][1] * i0);
-        if (rb < n)
-            *reinterpret_cast<__half2*>(out + (size_t)rb * VIT_HIDDEN + h * VIT_HD + d) =
-                __floats2half2_rn(o[j][2] * i1, o[j][3] * i1);
     }
 }
 
