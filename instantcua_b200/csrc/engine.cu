@@ -37,6 +37,7 @@
 #include "prefill.cuh"
 #include "vision.cuh"
 #include "attn_tc.cuh"
+#include "prefill_tc.cuh"
 
 namespace icua_host {
 uint16_t f32_to_f16_bits(float f);
@@ -125,7 +126,10 @@ struct icua_engine {
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     float inv_freq[64];
     // prefill rows through the tensor-core GEMM (max_pass rows each)
-    float *px = nullptr, *pqkv = nullptr, *pq = nullptr;
+    float *px = nullptr, *pqkv = nullptr;
+    void* pq = nullptr;   // prompt-row q in the cache type [max_pass][16][128]
+    void* pvt = nullptr;  // V^T of the session's cache slots [8][128][pvt_stride], cache type
+    int pvt_stride = 0;
     __half *pxn = nullptr, *pattn = nullptr, *ph = nullptr;
     int* gemm_err = nullptr;                     // error flags of the batched kernels
     float* splitk_part = nullptr;                // split-K partial products of the batched GEMMs
@@ -519,9 +523,8 @@ cudaError_t set_smem_attrs() {
     if ((e = cudaFuncSetAttribute(vit_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   VitAttnSmem::alloc)) != cudaSuccess)
         return e;
-    for (const void* k : {(const void*)prefill_attn_kernel<__half>, (const void*)prefill_attn_kernel<__nv_bfloat16>}) {
-        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      PrefillAttnSmem<__half>::total)) != cudaSuccess)
+    for (const void* k : {(const void*)prefill_attn_tc_kernel<__half>, (const void*)prefill_attn_tc_kernel<__nv_bfloat16>}) {
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PrefillTcSmem::alloc)) != cudaSuccess)
             return e;
     }
     done = true;
@@ -937,6 +940,62 @@ icua_status try_finalize(icua_engine* eng) {
 // SwiGLU -> down GEMM + residual (+ DeepStack rows after layers 0..2).  The last layer only
 // appends K/V: the prompt's final row, whose logits are needed, runs through the decode step
 // afterwards (the reference's last-layer shortcut, Engine.swift:525-528).
+// Causal attention of prompt rows [0, n_rows) (cache slots pos0 ..) over slots [0, pos0 + n_rows):
+// V^T of the slots (the prompt rows from the projection, earlier slots gathered from the cache),
+// then the tensor-core kernel with this layer's TMA maps.
+template <typename KVT>
+cudaError_t record_prefill_attention(icua_engine* e, const KVT* kc, const KVT* vc, int n_rows, int pos0, int* errp) {
+    cudaStream_t st = e->stream;
+    cudaError_t err;
+    KVT* vt = static_cast<KVT*>(e->pvt);
+    const int vs = e->pvt_stride;
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((n_rows + 31) / 32, NKV * HD / 32);
+        cfg.blockDim = dim3(32, 8);
+        cfg.stream = st;
+        if ((err = cudaLaunchKernelEx(&cfg, prefill_vt_kernel<KVT>, (const float*)e->pqkv, n_rows, pos0, vt, vs)) !=
+            cudaSuccess)
+            return err;
+        if (pos0 > 0) {
+            cfg.gridDim = dim3((pos0 + 31) / 32, NKV * HD / 32);
+            if ((err = cudaLaunchKernelEx(&cfg, prefill_vt_gather_kernel<KVT>, vc, e->cfg.max_context, pos0, vt, vs)) !=
+                cudaSuccess)
+                return err;
+        }
+    }
+    auto enc = tensor_map_encoder();
+    if (!enc) return cudaErrorNotSupported;
+    const CUtensorMapDataType dt =
+        std::is_same<KVT, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUtensorMap qmap, kmap, vtmap;
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    const cuuint64_t qd[4] = {64, 2, NQ, (cuuint64_t)n_rows};
+    const cuuint64_t qs[3] = {128, 256, (cuuint64_t)NQ * 256};
+    const cuuint32_t qb[4] = {64, 1, 1, PT_BQ};
+    const cuuint64_t kd[4] = {64, 2, (cuuint64_t)e->cfg.max_context, NKV};
+    const cuuint64_t ks[3] = {128, 256, (cuuint64_t)e->cfg.max_context * 256};
+    const cuuint32_t kb[4] = {64, 1, PT_BK, 1};
+    const cuuint64_t vd[3] = {(cuuint64_t)vs, HD, NKV};
+    const cuuint64_t vsd[2] = {(cuuint64_t)vs * 2, (cuuint64_t)vs * HD * 2};
+    const cuuint32_t vb[3] = {PT_BK, HD, 1};
+    if (enc(&qmap, dt, 4, e->pq, qd, qs, qb, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        // the cache rows are stored swizzled already: a plain copy lands them in the 128-byte swizzle
+        enc(&kmap, dt, 4, const_cast<KVT*>(kc), kd, ks, kb, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+            CUDA_SUCCESS ||
+        enc(&vtmap, dt, 3, vt, vd, vsd, vb, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((n_rows + PT_BQ - 1) / PT_BQ, NQ);
+    cfg.blockDim = dim3(PT_THREADS);
+    cfg.dynamicSmemBytes = PrefillTcSmem::alloc;
+    cfg.stream = st;
+    return cudaLaunchKernelEx(&cfg, prefill_attn_tc_kernel<KVT>, qmap, kmap, vtmap, n_rows, pos0, e->pattn, errp);
+}
+
 template <typename KVT>
 cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_off, int n_vis) {
     cudaError_t err;
@@ -1008,19 +1067,10 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
         if ((err = gemm_issued()) != cudaSuccess) return err;
         if ((err = launch(qk_rope_kv_kernel<KVT>, n_rows, 256, 0, st, false, (const float*)e->pqkv, n_rows,
                           (const float*)ly.q_norm, (const float*)ly.k_norm, (const float2*)S.rope, pos0, kc, vc,
-                          e->cfg.max_context, e->pq)) != cudaSuccess)
+                          e->cfg.max_context, (KVT*)e->pq)) != cudaSuccess)
             return err;
         if (l == L - 1) break;
-        {
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3((n_rows + PA_BQ - 1) / PA_BQ, NKV);
-            cfg.blockDim = dim3(PA_THREADS);
-            cfg.dynamicSmemBytes = PrefillAttnSmem<KVT>::total;
-            cfg.stream = st;
-            if ((err = cudaLaunchKernelEx(&cfg, prefill_attn_kernel<KVT>, (const float*)e->pq, (const KVT*)kc,
-                                          (const KVT*)vc, e->cfg.max_context, n_rows, pos0, e->pattn, errp)) != cudaSuccess)
-                return err;
-        }
+        if ((err = record_prefill_attention<KVT>(e, kc, vc, n_rows, pos0, errp)) != cudaSuccess) return err;
         p = tc_params(ly.o, n_rows, errp);
         p.out = e->px;
         p.ldo = H;
@@ -1284,7 +1334,10 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
         const size_t P = (size_t)cfg->max_pass;
         TRY(dalloc_t(eng, &eng->px, P * H));
         TRY(dalloc_t(eng, &eng->pqkv, P * QKV_ROWS));
-        TRY(dalloc_t(eng, &eng->pq, P * NQ * HD));
+        TRY(dalloc(eng, &eng->pq, P * NQ * HD * 2));
+        eng->pvt_stride = (cfg->max_context + 63) / 64 * 64 + 64;
+        TRY(dalloc(eng, &eng->pvt, (size_t)NKV * HD * eng->pvt_stride * 2));
+        cudaMemset(eng->pvt, 0, (size_t)NKV * HD * eng->pvt_stride * 2);  // slots past a call stay finite
         TRY(dalloc_t(eng, &eng->pxn, P * H));
         TRY(dalloc_t(eng, &eng->pattn, P * H));
         TRY(dalloc_t(eng, &eng->ph, P * FF));
