@@ -1337,7 +1337,7 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
         TRY(dalloc(eng, &eng->pq, P * NQ * HD * 2));
         eng->pvt_stride = (cfg->max_context + 63) / 64 * 64 + 64;
         TRY(dalloc(eng, &eng->pvt, (size_t)NKV * HD * eng->pvt_stride * 2));
-        cudaMemset(eng->pvt, 0, (size_t)NKV * HD * eng->pvt_stride * 2);  // slots past a call stay finite
+        cudaMemsetAsync(eng->pvt, 0, (size_t)NKV * HD * eng->pvt_stride * 2, eng->stream);  // slots past a call stay finite
         TRY(dalloc_t(eng, &eng->pxn, P * H));
         TRY(dalloc_t(eng, &eng->pattn, P * H));
         TRY(dalloc_t(eng, &eng->ph, P * FF));
@@ -1354,10 +1354,10 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
             cudaEventCreateWithFlags(&eng->ev_done[i], cudaEventDisableTiming);
         }
         cudaStreamCreateWithFlags(&eng->side, cudaStreamNonBlocking);
-        cudaMemset(eng->ph, 0, P * FF * sizeof(__half));
-        cudaMemset(eng->pxn, 0, P * H * sizeof(__half));
-        cudaMemset(eng->pattn, 0, P * H * sizeof(__half));
-        cudaMemset(eng->gemm_err, 0, sizeof(int));
+        cudaMemsetAsync(eng->ph, 0, P * FF * sizeof(__half), eng->stream);
+        cudaMemsetAsync(eng->pxn, 0, P * H * sizeof(__half), eng->stream);
+        cudaMemsetAsync(eng->pattn, 0, P * H * sizeof(__half), eng->stream);
+        cudaMemsetAsync(eng->gemm_err, 0, sizeof(int), eng->stream);
         CUtensorMap probe;
         if (!make_act_map(&probe, eng->pxn, (int)P, H, 16))
             TRY(fail(eng, ICUA_ERR_CUDA, "cuTensorMapEncodeTiled is not available"));
@@ -1376,7 +1376,9 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
     TRY(dalloc_t(eng, &eng->batch_rows, (size_t)cfg->max_pass));
     TRY(dalloc_t(eng, &eng->batch_best_v, (size_t)(cfg->vocab / TC_BM) * cfg->max_pass));
     TRY(dalloc_t(eng, &eng->batch_best_i, (size_t)(cfg->vocab / TC_BM) * cfg->max_pass));
-    cudaMemset(eng->st_all, 0, NS * sizeof(DevState));
+    cudaMemsetAsync(eng->st_all, 0, NS * sizeof(DevState), eng->stream);
+    // the zero fills are ordered on the engine stream; host-side copies below use the legacy stream
+    TRY(cudaStreamSynchronize(eng->stream) == cudaSuccess ? ICUA_OK : fail(eng, ICUA_ERR_CUDA, "zero fill failed"));
     for (size_t i = 0; i < NS; ++i) {
         Session& S = eng->sessions[i];
         S.st = eng->st_all + i;
@@ -2503,10 +2505,10 @@ icua_status icua_encode_vision(icua_engine* eng, const uint8_t* rgb, int32_t wid
             (s = dalloc_t(eng, &eng->vrope, NP * 32)) != ICUA_OK ||
             (s = dalloc_t(eng, &eng->vvt, (NP + 8) * VIT_HIDDEN)) != ICUA_OK)
             return s;
-        cudaMemset(eng->vxn, 0, NP * VIT_HIDDEN * sizeof(__half));  // rows past a call's patches read by TMA
-        cudaMemset(eng->vh, 0, NP * VIT_FF * sizeof(__half));
-        cudaMemset(eng->vattn, 0, NP * VIT_HIDDEN * sizeof(__half));
-        cudaMemset(eng->vpatch, 0, NP * VIT_PATCH_DIM * sizeof(__half));
+        cudaMemsetAsync(eng->vxn, 0, NP * VIT_HIDDEN * sizeof(__half), eng->stream);  // rows past a call's patches read by TMA
+        cudaMemsetAsync(eng->vh, 0, NP * VIT_FF * sizeof(__half), eng->stream);
+        cudaMemsetAsync(eng->vattn, 0, NP * VIT_HIDDEN * sizeof(__half), eng->stream);
+        cudaMemsetAsync(eng->vpatch, 0, NP * VIT_PATCH_DIM * sizeof(__half), eng->stream);
         eng->vit_np_max = (int)NP;
     }
     CK(cudaMemcpyAsync(eng->vrgb, rgb, (size_t)np * VIT_PATCH_DIM, cudaMemcpyHostToDevice, eng->stream));

@@ -68,6 +68,15 @@ struct TcGemmParams {
                                //   weight tiles)
 };
 
+// Epilogue activations on the hardware approximations (tanh.approx, ex2.approx through __expf,
+// __fdividef): their outputs are rounded to fp16 right after, well above the approximation error.
+__device__ __forceinline__ float tanh_approx(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 // Shared-memory layout of one CTA for a (BN, MH, format) choice; the same arithmetic runs on the
 // host (launch size) and the device (offsets).
 struct TcLayout {
@@ -489,7 +498,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                         if (j < nj) {
                             const float x = v[j];
                             const float g = p.gelu_erf ? 0.5f * x * (1.0f + erff(x * 0.70710678118654752f))
-                                                       : 0.5f * x * (1.0f + tanhf(0.79788456080286536f *
+                                                       : 0.5f * x * (1.0f + tanh_approx(0.79788456080286536f *
                                                                                   (x + 0.044715f * x * x * x)));
                             p.out_h[(size_t)(tok0 + c * 32 + j) * p.ldh + row] = __float2half_rn(g);
                         }
@@ -537,7 +546,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                         const float u = __shfl_xor_sync(0xffffffffu, v[j], 8);
                         if (!(lane & 8)) {
                             const float gv = v[j];
-                            const float hv = (gv / (1.0f + expf(-gv))) * u;
+                            const float hv = silu_fast(gv) * u;
                             p.out_h[(size_t)tok * p.ldh + (row >> 4) * 8 + (lane & 7)] = __float2half_rn(hv);
                         }
                     }
