@@ -290,6 +290,12 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
     __syncwarp();
 
     pdl_wait();
+    // the projection values are loaded before the stop-flag read so neither waits on the other
+    float4 x4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (prep) {
+        const int base = role < 2 ? (2 * h + role) * HD : (role == 2 ? 2048 + h * HD : 3072 + h * HD);
+        x4 = *reinterpret_cast<const float4*>(qkv + tk * QKV_ROWS + base + 4 * lane);
+    }
 
     if (*(volatile int*)&st->done) {  // uniform over the grid: no CTA reaches the cluster barriers
         pdl_launch_dependents();
@@ -302,9 +308,7 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
 
     // ---- q/k norm + RoPE for the new position: warp 0/1 -> q heads 2h, 2h+1, warp 2 -> k, 3 -> v ----
     if (prep) {
-        const int base = role < 2 ? (2 * h + role) * HD : (role == 2 ? 2048 + h * HD : 3072 + h * HD);
         const int tpos = pos + tk;
-        const float4 x4 = *reinterpret_cast<const float4*>(qkv + tk * QKV_ROWS + base + 4 * lane);
         float x[4] = {x4.x, x4.y, x4.z, x4.w};
         if (role < 3) {
             const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);

@@ -403,8 +403,11 @@ __device__ __forceinline__ void gemv_row_epilogue(const GemvParams& p, int r, fl
 // Shaders.swift:529-595).  Lane (g, t) accumulates token t & 1.  The lm_head (EPI_LOGITS) reads
 // only the pass's last row.  With one token the columns repeat it and the arithmetic is that of
 // the single-token kernel.
+//
+// 64 registers: the q4 kernels (512 threads) keep two CTAs per SM, the running one and the next
+// launch prefetching its weights, without spilling the hoisted unit constants.
 template <int FMT, int EPI, int KMAX, bool STREAM, int IN, bool DUAL = false>
-__global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParams p) {
+__global__ void __maxnreg__(64) gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NW = fmt_slices(FMT), NT = NW * 32;
     constexpr int KU = KMAX / 64 / NW;  // units of a tile per warp at K = KMAX
@@ -531,6 +534,8 @@ __global__ void __maxnreg__(FMT == FMT_Q8 ? 64 : 56) gemv_kernel(const GemvParam
         if (n_chunks > 0 && !mbar_wait_bounded(&bars[0], 0)) {
             if (lane == 0 && p.st) atomicOr(&p.st->error, ERR_WAIT_GEMV);
         }
+        // two tiles in flight: their unit MMA chains are independent
+#pragma unroll 2
         for (int j = 0; j < nt; ++j) {
             float acc0, acc1;
             tile_sum(ring + j * ku * UB, acc0, acc1);
