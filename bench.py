@@ -30,6 +30,7 @@ sys.path.insert(0, ROOT)
 CTX = 4096
 SEED = 0
 METRIC = "q4 decode tokens/s (batch 1, 4K ctx)"
+WORKLOAD = "config 2: batch-1 q4 decode, KV pre-filled to 4096 positions, CUDA graph of 8 steps"
 H, FF, V, NL = 2048, 6144, 151936, 28
 Q4_LAYER_BYTES = (4096 * 2048 + 2048 * 2048 + 12288 * 2048 + 2048 * 6144) * 9 // 16  # 0.5625 B / weight
 Q8_HEAD_BYTES = V * 2048 * 17 // 16                                                  # 1.0625 B / weight
@@ -208,7 +209,7 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "q4s/q8 weights, fp32 math, bf16 KV", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) KV)",
-            "config": {"workload": "config 2: batch-1 q4 decode, KV pre-filled to 4096 positions, CUDA graph of 8 steps",
+            "config": {"workload": WORKLOAD,
                        "model": "Qwen3-VL-2B text decoder (28 layers, random init)", "global_batch": world,
                        "seq_len": CTX, "context_range": [ctx0, ctx0 + K], "parallelism": f"replicas x{world}",
                        "l2": "inputs larger than L2 (1.59 GB streamed per step)"},
@@ -678,11 +679,13 @@ def run_reference(args):
     sample = (f"each step: 1 decode token through 4 of 28 layers + 1/7 of the lm_head rows at context {CTX}; "
               f"7 steps = 1 token; numpy fp32 oracle, BLAS on {cores} threads")
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": round(tok_s, 4), "unit": "tokens/s", "n_gpus": 0,
+        "impl": "reference", "metric": METRIC, "value": round(tok_s, 4), "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) KV)",
-        "config": {"workload": "config 2: batch-1 decode at 4K context (CPU reference path)", "seq_len": CTX},
+        "config": {"workload": WORKLOAD, "model": "Qwen3-VL-2B text decoder (28 layers, random init)",
+                   "seq_len": CTX, "parallelism": "the reference's CPU path on the host cores of rank 0",
+                   "l2": "n/a (host run)"},
         "cpu_baseline": {"value": round(tok_s, 4), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": round(tok_s, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
