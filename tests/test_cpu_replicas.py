@@ -59,3 +59,44 @@ def test_single_process_needs_no_group():
         assert bench.max_over_ranks(None, 3.5) == 3.5
     finally:
         os.environ.update(env)
+
+
+REQUIRED_KEYS = {"impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                 "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"}
+
+
+def _reference_line(env_extra, gpus):
+    import json
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ)
+    env.update(env_extra)
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--gpus", str(gpus), "--steps", "1",
+                        "--warmup", "0"], cwd=root, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    return [json.loads(l) for l in lines]
+
+
+def test_reference_arm_line_matches_the_measured_arm():
+    """`bench.py --impl reference` (the reference's CPU path, run on the host) prints one line with
+    the measured arm's metric, unit, direction and workload, the launch's GPU count, and its own
+    cpu_baseline / e2e blocks; warm-up is raised to the 3-step minimum."""
+    import bench
+
+    (line,) = _reference_line({"RANK": "0"}, 2)
+    assert REQUIRED_KEYS <= set(line)
+    assert line["impl"] == "reference" and line["metric"] == bench.METRIC and line["unit"] == "tokens/s"
+    assert line["higher_is_better"] is True and line["n_gpus"] == 2 and line["warmup"] >= 3
+    assert line["config"]["workload"] == bench.WORKLOAD
+    assert line["value"] > 0 and line["cpu_baseline"]["value"] == line["value"]
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"] == {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_other_ranks_print_nothing():
+    """Under torchrun only rank 0 runs the CPU reference; the other ranks exit 0 without output."""
+    assert _reference_line({"RANK": "1"}, 2) == []
