@@ -153,6 +153,8 @@ struct icua_engine {
     std::vector<int> batch_key;
     cudaGraphExec_t g_batch1 = nullptr, g_batchn = nullptr;
     float* batch_logits = nullptr;  // [rows][vocab] of the last batched step, when requested
+    float* batch_logits_buf = nullptr;  // its allocation, kept across disable / enable
+    int batch_logits_cap = 0;           // rows the allocation holds
     float* batch_logits_host = nullptr;
     int batch_logits_rows = 0;
     // vision encoder: weights by reference tensor id (fp16 matrices, fp32 vectors), activations
@@ -2076,8 +2078,20 @@ icua_status icua_capture_batch_logits(icua_engine* eng, float* host_out, int32_t
         return ICUA_OK;
     }
     if (n_rows > eng->cfg.max_pass) return fail(eng, ICUA_ERR_CAPACITY, "%d rows (max_pass %d)", n_rows, eng->cfg.max_pass);
-    icua_status s;
-    if ((s = dalloc_t(eng, &eng->batch_logits, (size_t)n_rows * eng->cfg.vocab)) != ICUA_OK) return s;
+    if (n_rows > eng->batch_logits_cap) {  // grow only: re-enabling reuses the buffer
+        if (eng->batch_logits_buf) {
+            CK(cudaStreamSynchronize(eng->stream));
+            auto& A = eng->allocations;
+            A.erase(std::remove(A.begin(), A.end(), (void*)eng->batch_logits_buf), A.end());
+            cudaFree(eng->batch_logits_buf);
+            eng->batch_logits_buf = nullptr;
+            eng->batch_logits_cap = 0;
+        }
+        icua_status s;
+        if ((s = dalloc_t(eng, &eng->batch_logits_buf, (size_t)n_rows * eng->cfg.vocab)) != ICUA_OK) return s;
+        eng->batch_logits_cap = n_rows;
+    }
+    eng->batch_logits = eng->batch_logits_buf;
     eng->batch_logits_host = host_out;
     eng->batch_logits_rows = n_rows;
     return ICUA_OK;

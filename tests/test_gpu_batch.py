@@ -100,6 +100,29 @@ def test_batch_in_tokens_and_continuation(tensors):
     assert np.array_equal(outs[0], outs[1])
 
 
+def test_batch_logits_capture_reenabled(tensors):
+    """Turning the logits capture off and on again, with fewer and then more rows than before,
+    reuses (or grows) one device buffer and captures the same logits as a capture set up once."""
+    n = 3
+    rng = np.random.default_rng(6)
+    k = rng.standard_normal((2, 40, 8, 128), dtype=np.float32)
+    v = rng.standard_normal((2, 40, 8, 128), dtype=np.float32)
+    caps = []
+    for toggled in (False, True):
+        e = make_engine(tensors, sessions=n)
+        for s in range(n):
+            e.inject_kv(k, v, session=s)
+        if toggled:
+            e.capture_batch_logits(2)
+            e.capture_batch_logits(None)
+            e.capture_batch_logits(1)
+        cap = e.capture_batch_logits(n)  # toggled: grows past the earlier two rows
+        e.decode_batch(list(range(n)), 2, in_tokens=[5, 6, 7])
+        caps.append(cap.copy())
+        e.close()
+    assert np.array_equal(caps[0], caps[1]) and np.abs(caps[0]).max() > 0
+
+
 def test_batch_errors(tensors):
     e = make_engine(tensors, sessions=2)
     with pytest.raises(IcuaError):
