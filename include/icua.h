@@ -253,7 +253,8 @@ icua_status icua_gemm_f16(int32_t n_rows, int32_t k, int32_t m_tok, const void* 
 /* Greedy head on the device: token = argmax_v (embed_v . RMSNorm(x) * norm_w), the tied q8 lm_head
  * of the reference (k_lm_head + k_commit, Shaders.swift:1452-1547; lowest index wins ties).
  * packed_embed_dev: q8 [vocab, 2048] in the device layout (icua_pack_matrix); x_dev fp32 [2048];
- * norm_w_dev fp32 [2048] or NULL (no norm); logits_dev fp32 [vocab] or NULL; token_dev int32 [1].
+ * norm_w_dev fp32 [2048] or NULL (no norm); logits_dev fp32 [vocab] or NULL; token_dev int32 [1]
+ * receives the argmax, or -1 when no logit is finite (NaN / inf in x or norm_w).
  * scratch_dev: icua_greedy_head_scratch_bytes(vocab) bytes of device memory for the per-CTA argmax
  * partials (no initialisation needed). */
 uint64_t icua_greedy_head_scratch_bytes(int32_t vocab);
@@ -267,13 +268,22 @@ icua_status icua_greedy_head(int32_t vocab, const void* packed_embed_dev, const 
  * allocates its pval/pidx buffers at init (Engine.swift:116-117).  Same arguments and results as
  * icua_greedy_head minus the scratch: the per-CTA partials live in a fixed 8 KiB device array of
  * the library (room for 1024 CTA partials; larger grids are rejected with ICUA_ERR_CAPACITY),
- * which every GPU that loads the library keeps until exit.  The first call on a device looks up
- * that array's address (cudaGetSymbolAddress) with the device current; make that first call
- * before any stream capture.  All calls share the array, so calls that overlap on the GPU (on
- * different streams or devices sharing nothing else) race; serialise them. */
+ * which every GPU that loads the library keeps until exit (one copy per CUDA context).  Calls
+ * made outside stream capture look up that array's address (cudaGetSymbolAddress) in the current
+ * context; a call under capture reuses the address an earlier call in the same context found, so
+ * make the first call in a context before any stream capture.  Calls on the same device share
+ * the array: serialise calls that could overlap on one device, even on different streams.  Calls
+ * on different devices do not interfere. */
 icua_status icua_greedy_head_noalloc(int32_t vocab, const void* packed_embed_dev, const float* x_dev,
                                      const float* norm_w_dev, float* logits_dev, int32_t* token_dev,
                                      void* stream);
+
+/* Poll limit of the bounded wait in which a decode GEMV waits for the copy of its RMSNorm weights,
+ * on the current device (default 4194304).  No reference counterpart: it exists so that tests can
+ * make that wait give up (polls = 0) and check the timeout report -- the kernel flags the step,
+ * still waits for its copy with the default bound, the engine call returns ICUA_ERR_TIMEOUT and
+ * later calls on that engine ICUA_ERR_STATE.  Set it back before running other work. */
+icua_status icua_set_wait_limit(uint32_t polls);
 
 /* Bit-exact dequantization of a packed device matrix to fp32 row-major [n_rows, k]. */
 icua_status icua_dequant(int32_t fmt, int32_t n_rows, int32_t k, const void* packed_dev, float* out_dev,

@@ -90,6 +90,7 @@ PROTOTYPES = {
     "icua_greedy_head_scratch_bytes": (C.c_uint64, [_I]),
     "icua_greedy_head": (_I, [_I, _P, _P, _P, _P, _P, _P, _P]),
     "icua_greedy_head_noalloc": (_I, [_I, _P, _P, _P, _P, _P, _P]),
+    "icua_set_wait_limit": (_I, [C.c_uint32]),
     "icua_quantize_q8": (_I, [_FP, _I, _I, _P, _P]),
     "icua_quantize_q4s": (_I, [_FP, _I, _I, _P, _P]),
 }

@@ -2326,6 +2326,13 @@ icua_status icua_greedy_head(int32_t vocab, const void* packed, const float* x, 
     return greedy_head_launch(m, packed, x, norm_w, logits, token, best_v, best_i, (cudaStream_t)stream);
 }
 
+icua_status icua_set_wait_limit(uint32_t polls) {
+    icua_engine* eng = nullptr;
+    CK(cudaMemcpyToSymbol(c_norm_wait_polls, &polls, sizeof polls));
+    CK(cudaDeviceSynchronize());
+    return ICUA_OK;
+}
+
 // ---- greedy head without allocation ------------------------------------------------------------
 // Some callers cannot call cudaMalloc at all: code running under a host allocator or memory
 // pool that owns all device memory, a plugin loaded into a process that forbids allocation
@@ -2335,7 +2342,22 @@ icua_status icua_greedy_head(int32_t vocab, const void* packed, const float* x, 
 constexpr int NOALLOC_MAX_PARTS = 1024;  // CTA partials (8 bytes each): grids up to 1024 CTAs
 static __device__ __align__(256) uint8_t g_greedy_head_scratch[NOALLOC_MAX_PARTS * 8];
 static std::mutex g_noalloc_mu;
-static void* g_noalloc_addr[64];  // device address of the array, per device ordinal
+static std::map<CUcontext, void*> g_noalloc_addr;  // device address of the array, per CUDA context
+
+static CUcontext current_context() {
+    static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    });
+    CUcontext c = nullptr;
+    if (fn) fn(&c);
+    return c;
+}
 
 icua_status icua_greedy_head_noalloc(int32_t vocab, const void* packed, const float* x, const float* norm_w,
                                      float* logits, int32_t* token, void* stream) {
@@ -2347,21 +2369,29 @@ icua_status icua_greedy_head_noalloc(int32_t vocab, const void* packed, const fl
     if (m.grid > NOALLOC_MAX_PARTS)
         return fail(nullptr, ICUA_ERR_CAPACITY, "greedy head needs %d CTA partials, the fixed scratch holds %d",
                     m.grid, NOALLOC_MAX_PARTS);
-    int dev = 0;
-    CK(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return fail(nullptr, ICUA_ERR_INVALID, "device ordinal %d out of range", dev);
+    // The array exists once per CUDA context that loaded this library (not once per device), so its
+    // address is kept per context.  Outside stream capture it is looked up on every call, which
+    // also picks up a context re-created by cudaDeviceReset; during capture the address of an
+    // earlier call in the same context is used, so the first call in a context must come before
+    // any capture.
+    const CUcontext ctx = current_context();
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    CK(cudaStreamIsCapturing((cudaStream_t)stream, &cap));
     void* base = nullptr;
     {
-        // first call on a device: look up the array's device address with that device current
         std::lock_guard<std::mutex> lk(g_noalloc_mu);
-        if (g_noalloc_addr[dev] == nullptr) {
+        if (cap == cudaStreamCaptureStatusNone) {
             void* a = nullptr;
             const cudaError_t e = cudaGetSymbolAddress(&a, g_greedy_head_scratch);
             if (e != cudaSuccess)
                 return fail(nullptr, ICUA_ERR_CUDA, "cudaGetSymbolAddress(greedy head scratch): %s", cudaGetErrorString(e));
-            g_noalloc_addr[dev] = a;
+            g_noalloc_addr[ctx] = a;
         }
-        base = g_noalloc_addr[dev];
+        auto it = g_noalloc_addr.find(ctx);
+        if (it == g_noalloc_addr.end())
+            return fail(nullptr, ICUA_ERR_STATE,
+                        "first icua_greedy_head_noalloc call in this context is under stream capture; call it once before capturing");
+        base = it->second;
     }
     // every partial is written by its CTA before it is read: nothing needs clearing between calls
     float* best_v = (float*)base;

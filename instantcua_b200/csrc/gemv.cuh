@@ -40,6 +40,11 @@ constexpr int ATT_PART = 4 + 2 * HD;  // per (kv head, part): m[2], l[2], o[2][1
 constexpr int ATT_MAX_PARTS = 8;
 constexpr int SMALL_MAX_TILES = 8;    // tiles per CTA of the register-accumulating path
 
+// Poll limit of a GEMV's wait for its RMSNorm weight copy (icua_set_wait_limit).  0 makes that wait
+// give up at once, which exercises the timeout report path (ERR_WAIT_GEMV -> ICUA_ERR_TIMEOUT)
+// without leaving a copy in flight: the kernel then waits for the copy with the default bound.
+__constant__ uint32_t c_norm_wait_polls = 1u << 22;
+
 struct GemvParams {
     const uint8_t* w;        // tile-packed units, slice-major
     int n_rows, k, upt;      // upt = k / 64 units per tile
@@ -231,7 +236,12 @@ __device__ __forceinline__ void store_input(const InputRegs<KMAX, NT>& r, const 
     const float* nws = reinterpret_cast<const float*>(smem + L.normw_off());
     float scale = 1.0f;
     if (p.norm_w != nullptr) {
-        if (!mbar_wait_bounded(nbar, 0) && tid == 0 && p.st) atomicOr(&p.st->error, ERR_WAIT_GEMV);
+        if (!mbar_wait_bounded(nbar, 0, c_norm_wait_polls)) {
+            // gave up: flag it, then still wait (default bound) so that the copy has landed before
+            // this CTA reads the weights or exits
+            if (tid == 0 && p.st) atomicOr(&p.st->error, ERR_WAIT_GEMV);
+            mbar_wait_bounded(nbar, 0);
+        }
         float ss = 0.f;
 #pragma unroll
         for (int j = 0; j < InputRegs<KMAX, NT>::PPT; ++j)
@@ -649,7 +659,8 @@ __global__ void __maxnreg__(64) gemv_kernel(const GemvParams p) {
     }
 }
 
-// Reduces per-CTA argmax partials to one token id (standalone greedy head): one CTA.
+// Reduces per-CTA argmax partials to one token id (standalone greedy head): one CTA; -1 when no
+// partial holds a finite logit.
 __global__ void __launch_bounds__(256) argmax_parts_kernel(const float* best_v, const int* best_i, int n_parts,
                                                            int* token) {
     pdl_wait();
@@ -668,7 +679,9 @@ __global__ void __launch_bounds__(256) argmax_parts_kernel(const float* best_v, 
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int w2 = 1; w2 < (int)(blockDim.x >> 5); ++w2) argmax_merge(sv[0], si[0], sv[w2], si[w2]);
-        *token = si[0];
+        // no finite logit (NaN activations or norm weights) leaves no winner: report -1, never an
+        // id that a caller could use as an index
+        *token = si[0] == 0x7fffffff ? -1 : si[0];
     }
 }
 

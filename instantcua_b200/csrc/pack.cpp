@@ -2,7 +2,7 @@
 //
 // Quantizers restate the reference Converter (Sources/Engine/Convert.swift:215-241 for q8) and the
 // BASELINE symmetric q4 defined by analogy with it; results are bit-identical to the numpy
-// restatement in oracle/qwen3vl_oracle.py (checked by tests/test_cpu_pack.py).  Compiled without
+// restatement in oracle/qwen3vl_oracle.py (checked by tests/test_cpu_abi.py).  Compiled without
 // fast-math so every fp32 operation rounds as IEEE-754 single precision.
 #include <cmath>
 #include <cstdint>

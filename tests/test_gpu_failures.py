@@ -40,3 +40,31 @@ def test_nan_logits_stop_batched_decode(nan_tensors):
     with pytest.raises(L.IcuaError, match="no finite logit"):
         e.decode_batch([0, 1, 2, 3], 3, in_tokens=np.array([1, 2, 3, 4], np.int32))
     e.close()
+
+
+def test_wait_timeout_reports_and_engine_stays_failed(require_gpu):
+    """A bounded device wait that gives up is reported, not hidden: with the GEMV's norm-weight wait
+    limited to 0 polls the decode kernels flag the step (after still waiting, with the default
+    bound, for their copies), the call returns ICUA_ERR_TIMEOUT, the engine refuses later calls
+    with ICUA_ERR_STATE, and a new engine works once the limit is back (the context is usable)."""
+    from _tiny import engine_tensors
+
+    tensors = engine_tensors()
+    lib = L.lib()
+    prompt = np.arange(20, dtype=np.int32)
+    e = make(tensors)
+    try:
+        L.check(lib.icua_set_wait_limit(0))
+        with pytest.raises(L.IcuaError) as ei:
+            e.generate_vision(prompt, 4)
+        assert ei.value.status == L.ERR_TIMEOUT
+        assert "bounded device wait" in str(ei.value)
+    finally:
+        L.check(lib.icua_set_wait_limit(1 << 22))
+    with pytest.raises(L.IcuaError) as ei:
+        e.generate_vision(prompt, 4)
+    assert ei.value.status == L.ERR_STATE
+    e.close()
+    e2 = make(tensors)
+    assert len(e2.generate_vision(prompt, 4)) == 4
+    e2.close()

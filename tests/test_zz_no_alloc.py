@@ -50,3 +50,14 @@ def test_noalloc_greedy_head_matches_allocating_entry_point(require_gpu):
         a, b = la.cpu().numpy(), lb.cpu().numpy()
         assert int(ta.item()) == int(tb.item()) == int(np.argmax(a)), call
         assert np.abs(a - b).max() <= GEMV_TOL * np.abs(a).max(), call
+    # no finite logit: both entry points report -1 rather than an id a caller could index with
+    x = torch.full((k,), float("nan"), device="cuda")
+    ta = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    tb = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    L.check(lib.icua_greedy_head(vocab, C.c_void_p(emb.data_ptr()), C.c_void_p(x.data_ptr()),
+                                 C.c_void_p(norm.data_ptr()), None, C.c_void_p(ta.data_ptr()),
+                                 C.c_void_p(scratch.data_ptr()), None))
+    L.check(lib.icua_greedy_head_noalloc(vocab, C.c_void_p(emb.data_ptr()), C.c_void_p(x.data_ptr()),
+                                         C.c_void_p(norm.data_ptr()), None, C.c_void_p(tb.data_ptr()), None))
+    torch.cuda.synchronize()
+    assert int(ta.item()) == int(tb.item()) == -1
