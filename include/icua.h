@@ -141,6 +141,18 @@ icua_status icua_decode(icua_engine* eng, int32_t session, int32_t max_new, int3
  * The step's logits are kept for icua_get_logits. */
 icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token, int32_t* out_token);
 
+/* Kernels one decode step launches on this engine: 3 for q4s engines on the persistent layers
+ * kernel (all layers in one cooperative launch, then the lm_head GEMV and the commit), else
+ * 5 x n_layers + 2 (one launch per projection / attention, lm_head, commit).  0 for NULL. */
+int32_t icua_decode_kernels_per_step(const icua_engine* eng);
+
+/* Measurement: decodes n_steps greedy steps of `session` (after a prefill, like icua_decode) with
+ * every launch issued directly on the engine stream and CUDA events around each step's decoder
+ * layers and around its lm_head + commit; *layers_ms / *head_ms receive the summed device times.
+ * The tokens are committed as by icua_decode.  Used by the benchmark for per-kernel rooflines. */
+icua_status icua_profile_decode(icua_engine* eng, int32_t session, int32_t n_steps, double* layers_ms,
+                                double* head_ms);
+
 /* Batched greedy decode (the serving counterpart of icua_decode): every step
  * decodes one token for each of n_sessions sessions together -- tensor-core GEMMs over the session
  * rows, per-session attention over each session's own cache, the tied lm_head with a per-row

@@ -30,6 +30,7 @@
 #include "../../include/icua.h"
 #include "attn_decode.cuh"
 #include "batch.cuh"
+#include "decode_mk.cuh"
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
@@ -128,7 +129,7 @@ struct icua_engine {
     // prefill rows through the tensor-core GEMM (max_pass rows each)
     float *px = nullptr, *pqkv = nullptr;
     void* pq = nullptr;   // prompt-row q in the cache type [max_pass][16][128]
-    void* pvt = nullptr;  // V^T of the session's cache slots [8][128][pvt_stride], cache type
+    void* pvt = nullptr;  // V^T of the session's cache slots [8][128][pvt_stride], fp16
     int pvt_stride = 0;
     __half *pxn = nullptr, *pattn = nullptr, *ph = nullptr;
     int* gemm_err = nullptr;                     // error flags of the batched kernels
@@ -169,6 +170,17 @@ struct icua_engine {
     float2* vrope = nullptr;
     __half* vvt = nullptr;  // V^T per head [16][64][vit_np_max + 8]
     int vis_rows = -1;
+    // persistent decode step (decode_mk.cuh): q4s engines run every layer of a step in one
+    // cooperative launch; mk is false when the device or configuration cannot (launch chain)
+    bool mk = false;
+    int mk_S = 0;                                // attention CTAs per kv head
+    uint8_t* mk_stream = nullptr;                // CTA weight streams
+    unsigned long long* mk_cta_base = nullptr;   // [n_sm]
+    MkLayer* mk_layers = nullptr;                // [n_layers]
+    unsigned long long* mk_words = nullptr;      // exchange words
+    unsigned long long* mk_parts = nullptr;      // attention split parts (exchange words)
+    unsigned* mk_cnt = nullptr;                  // CTAs done with the launch, launch epoch
+    int* mk_abort = nullptr;
 };
 
 namespace {
@@ -501,6 +513,8 @@ cudaError_t set_smem_attrs() {
     SETA((attn_decode_kernel<__nv_bfloat16, true>));
     SETA(commit_kernel);
     SETA(advance_kernel);
+    SETA(decode_mk_kernel<__half>);
+    SETA(decode_mk_kernel<__nv_bfloat16>);
     SETA(argmax_parts_kernel);
 #undef SETA
     for (const void* k :
@@ -579,10 +593,56 @@ cudaError_t launch_layer_gemv(const icua_engine* e, const Matrix& m, const GemvP
 }
 
 // DUAL: the kernels of grammar-commit engines (passes of one or two tokens).
+// Every layer of one step as one cooperative launch (decode_mk_kernel).
+template <typename KVT>
+cudaError_t launch_mk(icua_engine* e, Session& S) {
+    MkParams<KVT> p{};
+    p.stream = e->mk_stream;
+    p.cta_base = e->mk_cta_base;
+    p.layers = e->mk_layers;
+    p.n_layers = e->cfg.n_layers;
+    p.S = e->mk_S;
+    p.st = S.st;
+    p.prompt = S.prompt;
+    p.pooler = e->pooler;
+    for (int i = 0; i < 3; ++i) p.deepstack[i] = e->deepstack[i];
+    p.rope = S.rope;
+    p.kc = reinterpret_cast<KVT*>(S.kc);
+    p.vc = reinterpret_cast<KVT*>(S.vc);
+    p.max_ctx = e->cfg.max_context;
+    p.embed = e->embed.dev;
+    p.embed_tiles = e->embed.n_tiles;
+    p.embed_fmt = e->embed.fmt;
+    unsigned long long* w = e->mk_words;
+    p.qkv = w;
+    p.att = w + 4096;
+    p.xmid = w + 6144;
+    p.xout = w + 8192;
+    p.hbuf = w + 10240;
+    p.parts = e->mk_parts;
+    p.fin = e->mk_cnt;
+    p.epoch = e->mk_cnt + 1;
+    p.abort = e->mk_abort;
+    p.x_final = e->x;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(e->n_sm);
+    cfg.blockDim = dim3(MK_THREADS);
+    cfg.dynamicSmemBytes = MkSmem::total;
+    cfg.stream = e->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, decode_mk_kernel<KVT>, p);
+}
+
 template <bool DUAL>
 cudaError_t record_layers_t(icua_engine* e, Session& S) {
     cudaError_t err;
     const int L = e->cfg.n_layers;
+    if (!DUAL && e->mk)
+        return e->cfg.kv_dtype == ICUA_KV_BF16 ? launch_mk<__nv_bfloat16>(e, S) : launch_mk<__half>(e, S);
     for (int l = 0; l < L; ++l) {
         Layer& ly = e->layers[l];
         // 1. RMSNorm + QKV projection (layer 0 embeds the input row first)
@@ -684,7 +744,9 @@ cudaError_t record_head(icua_engine* e, Session& S) {
     // q8 heads always stream; a q4a head streams unless the vocabulary is small (tests).  Grammar
     // engines' heads read the last row of the pass.
     cudaError_t err;
-    if (e->grammar)
+    if (!e->grammar && e->mk)
+        err = launch_gemv<FMT_Q8, EPI_LOGITS, 2048, true, IN_F32>(e->embed, p, e->stream, false);
+    else if (e->grammar)
         err = e->embed.fmt != FMT_Q4A ? launch_gemv<FMT_Q8, EPI_LOGITS, 2048, true, IN_F32, true>(e->embed, p, e->stream)
               : e->embed.stream       ? launch_gemv<FMT_Q4A, EPI_LOGITS, 2048, true, IN_F32, true>(e->embed, p, e->stream)
                                       : launch_gemv<FMT_Q4A, EPI_LOGITS, 2048, false, IN_F32, true>(e->embed, p, e->stream);
@@ -706,7 +768,7 @@ icua_status build_graph(icua_engine* eng, Session& S, int kind, cudaGraphExec_t*
     cudaError_t err = cudaSuccess;
     if (kind == 0) {
         err = record_layers(eng, S);
-        if (err == cudaSuccess) err = launch(advance_kernel, 1, 32, 0, eng->stream, true, S.st);
+        if (err == cudaSuccess) err = launch(advance_kernel, 1, 32, 0, eng->stream, !(eng->mk && !eng->grammar), S.st);
     } else {
         const int n = kind == 1 ? 1 : eng->cfg.steps_per_graph;
         for (int i = 0; i < n && err == cudaSuccess; ++i) {
@@ -736,6 +798,14 @@ void drop_graphs(Session& S) {
 icua_status ensure_graphs(icua_engine* eng, Session& S) {
     icua_status s;
     if (eng->cfg.format == ICUA_FMT_F16) return ICUA_OK;  // f16 engines decode through the batched step
+    if (eng->mk && !eng->grammar && !S.g_step1) {
+        // the cooperative launch must be capturable; if this driver cannot, decode by the launch chain
+        if (build_graph(eng, S, 1, &S.g_step1) != ICUA_OK) {
+            cudaGetLastError();
+            eng->mk = false;
+            S.g_step1 = nullptr;
+        }
+    }
     if (!S.g_prefill_tok && (s = build_graph(eng, S, 0, &S.g_prefill_tok)) != ICUA_OK) return s;
     if (!S.g_step1 && (s = build_graph(eng, S, 1, &S.g_step1)) != ICUA_OK) return s;
     if (!S.g_stepn && (s = build_graph(eng, S, 2, &S.g_stepn)) != ICUA_OK) return s;
@@ -892,6 +962,71 @@ icua_status upload_matrix(icua_engine* eng, Matrix& m, int fmt, int rows, int k,
     return ICUA_OK;
 }
 
+// Persistent decode step set-up for q4s engines that ask for it (ICUA_DECODE=mk in the environment
+// when the weights are loaded): CTA weight streams (a second copy of the decoder matrices, 0.79 GB
+// at 28 layers, ordered by owning CTA), exchange words, counters.  The default decode path is the
+// launch chain, which measured a little faster (28.4 vs 29.5 us per layer at 4K context); devices
+// with fewer than 128 SMs, or engines where the cooperative grid does not fit, keep the chain too.
+icua_status mk_setup(icua_engine* eng) {
+    const char* env = getenv("ICUA_DECODE");
+    if (!env || strcmp(env, "mk") != 0) return ICUA_OK;
+    const int G = eng->n_sm, L = eng->cfg.n_layers;
+    int coop = 0, per_sm = 0;
+    CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, eng->cfg.device));
+    CK(set_smem_attrs());
+    cudaError_t oe = eng->cfg.kv_dtype == ICUA_KV_BF16
+                         ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mk_kernel<__nv_bfloat16>,
+                                                                         MK_THREADS, MkSmem::total)
+                         : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mk_kernel<__half>, MK_THREADS,
+                                                                         MkSmem::total);
+    if (oe != cudaSuccess || !coop || per_sm < 1 || G < MK_O_TILES || G / NKV > MK_MAX_S || L > MK_MAX_LAYERS) {
+        cudaGetLastError();
+        return ICUA_OK;
+    }
+    std::vector<unsigned long long> base(G);
+    unsigned long long total = 0;
+    for (int c = 0; c < G; ++c) {
+        base[c] = total;
+        total += (unsigned long long)L * mk_items_per_layer(c, G) * MK_ITEM;
+    }
+    icua_status st;
+    if ((st = dalloc_t(eng, &eng->mk_stream, total)) != ICUA_OK) return st;
+    if ((st = dalloc_t(eng, &eng->mk_cta_base, G)) != ICUA_OK) return st;
+    CK(cudaMemcpy(eng->mk_cta_base, base.data(), G * sizeof(unsigned long long), cudaMemcpyHostToDevice));
+    std::vector<const uint8_t*> mats(4 * L);
+    std::vector<MkLayer> lys(L);
+    for (int l = 0; l < L; ++l) {
+        const Layer& ly = eng->layers[l];
+        mats[4 * l + 0] = ly.qkv.dev;
+        mats[4 * l + 1] = ly.o.dev;
+        mats[4 * l + 2] = ly.gu.dev;
+        mats[4 * l + 3] = ly.d.dev;
+        lys[l] = MkLayer{ly.attn_norm, ly.q_norm, ly.k_norm, ly.mlp_norm};
+    }
+    const uint8_t** mats_dev = nullptr;
+    if ((st = dalloc_t(eng, &mats_dev, 4 * L)) != ICUA_OK) return st;
+    CK(cudaMemcpy(mats_dev, mats.data(), 4 * L * sizeof(void*), cudaMemcpyHostToDevice));
+    if ((st = dalloc_t(eng, &eng->mk_layers, L)) != ICUA_OK) return st;
+    CK(cudaMemcpy(eng->mk_layers, lys.data(), L * sizeof(MkLayer), cudaMemcpyHostToDevice));
+    mk_pack_kernel<<<G * L, 256>>>(eng->mk_stream, eng->mk_cta_base, mats_dev, L, G);
+    CK(cudaGetLastError());
+    eng->mk_S = G / NKV;
+    constexpr int n_words = 4096 + 2048 + 2048 + 2048 + 6144;
+    if ((st = dalloc_t(eng, &eng->mk_words, n_words)) != ICUA_OK) return st;
+    if ((st = dalloc_t(eng, &eng->mk_parts, (size_t)NKV * eng->mk_S * ATT_PART)) != ICUA_OK) return st;
+    if ((st = dalloc_t(eng, &eng->mk_cnt, 2)) != ICUA_OK) return st;
+    if ((st = dalloc_t(eng, &eng->mk_abort, 1)) != ICUA_OK) return st;
+    CK(cudaMemset(eng->mk_words, 0, n_words * sizeof(unsigned long long)));
+    CK(cudaMemset(eng->mk_cnt, 0, 2 * sizeof(unsigned)));
+    CK(cudaMemset(eng->mk_parts, 0, (size_t)NKV * eng->mk_S * ATT_PART * sizeof(unsigned long long)));
+    CK(cudaMemset(eng->mk_abort, 0, sizeof(int)));
+    const unsigned one = 1;  // epoch 1: no exchange word (tag 0 after the clear) looks current
+    CK(cudaMemcpy(eng->mk_cnt + 1, &one, sizeof one, cudaMemcpyHostToDevice));
+    CK(cudaDeviceSynchronize());
+    eng->mk = true;
+    return ICUA_OK;
+}
+
 icua_status try_finalize(icua_engine* eng) {
     if (eng->uploaded) return ICUA_OK;
     for (int id = 0; id < ICUA_TENSOR_COUNT; ++id)
@@ -932,6 +1067,7 @@ icua_status try_finalize(icua_engine* eng) {
     }
     CK(cudaDeviceSynchronize());  // the re-layout kernels ran on the legacy stream
     eng->staged.clear();
+    if (fmt == FMT_Q4S && (s = mk_setup(eng)) != ICUA_OK) return s;
     eng->uploaded = true;
     return ICUA_OK;
 }
@@ -949,7 +1085,7 @@ template <typename KVT>
 cudaError_t record_prefill_attention(icua_engine* e, const KVT* kc, const KVT* vc, int n_rows, int pos0, int* errp) {
     cudaStream_t st = e->stream;
     cudaError_t err;
-    KVT* vt = static_cast<KVT*>(e->pvt);
+    __half* vt = static_cast<__half*>(e->pvt);  // fp16 for both cache types (the P V operand)
     const int vs = e->pvt_stride;
     {
         cudaLaunchConfig_t cfg = {};
@@ -983,11 +1119,13 @@ cudaError_t record_prefill_attention(icua_engine* e, const KVT* kc, const KVT* v
     const cuuint32_t vb[3] = {PT_BK, HD, 1};
     if (enc(&qmap, dt, 4, e->pq, qd, qs, qb, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+
         // the cache rows are stored swizzled already: a plain copy lands them in the 128-byte swizzle
         enc(&kmap, dt, 4, const_cast<KVT*>(kc), kd, ks, kb, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
             CUDA_SUCCESS ||
-        enc(&vtmap, dt, 3, vt, vd, vsd, vb, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+        enc(&vtmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, vt, vd, vsd, vb, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
@@ -1960,6 +2098,52 @@ icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token
     S->step += 1;
     S->pos += 1;
     return ICUA_OK;
+}
+
+int32_t icua_decode_kernels_per_step(const icua_engine* eng) {
+    if (!eng) return 0;
+    if (eng->mk && !eng->grammar) return 3;  // persistent layers kernel, lm_head GEMV, commit
+    return 5 * eng->cfg.n_layers + 2;
+}
+
+icua_status icua_profile_decode(icua_engine* eng, int32_t session, int32_t n_steps, double* layers_ms, double* head_ms) {
+    if (!eng || !layers_ms || !head_ms || n_steps < 1) return fail(eng, ICUA_ERR_INVALID, "bad argument");
+    if (eng->cfg.format == ICUA_FMT_F16) return fail(eng, ICUA_ERR_UNSUPPORTED, "f16 engines decode through the batched step");
+    icua_status s;
+    if ((s = check_ready(eng)) != ICUA_OK) return s;
+    Session* S = get_session(eng, session);
+    if (!S) return fail(eng, ICUA_ERR_INVALID, "session %d out of range", session);
+    if (S->step < 1) return fail(eng, ICUA_ERR_STATE, "decode before prefill");
+    if (S->step + n_steps > eng->cfg.max_steps + 1 || S->pos + n_steps + 1 > eng->cfg.max_context)
+        return fail(eng, ICUA_ERR_CAPACITY, "%d steps exceed the step or context capacity", n_steps);
+    CK(cudaSetDevice(eng->cfg.device));
+    if ((s = ensure_graphs(eng, *S)) != ICUA_OK) return s;  // the launch path is decided with the graphs
+    const int ms_val = S->step + n_steps, zero = 0;
+    CK(cudaMemcpyAsync(&S->st->max_steps, &ms_val, 4, cudaMemcpyHostToDevice, eng->stream));
+    CK(cudaMemcpyAsync(&S->st->done, &zero, 4, cudaMemcpyHostToDevice, eng->stream));
+    std::vector<cudaEvent_t> ev(3 * n_steps);
+    for (auto& e : ev) CK(cudaEventCreate(&e));
+    cudaError_t err = cudaSuccess;
+    for (int i = 0; i < n_steps && err == cudaSuccess; ++i) {
+        cudaEventRecord(ev[3 * i], eng->stream);
+        err = record_layers(eng, *S);
+        cudaEventRecord(ev[3 * i + 1], eng->stream);
+        if (err == cudaSuccess) err = record_head(eng, *S);
+        cudaEventRecord(ev[3 * i + 2], eng->stream);
+    }
+    s = err == cudaSuccess ? sync_and_check(eng, *S) : fail(eng, ICUA_ERR_CUDA, "launch: %s", cudaGetErrorString(err));
+    double a = 0, b = 0;
+    for (int i = 0; i < n_steps && s == ICUA_OK; ++i) {
+        float x = 0, y = 0;
+        cudaEventElapsedTime(&x, ev[3 * i], ev[3 * i + 1]);
+        cudaEventElapsedTime(&y, ev[3 * i + 1], ev[3 * i + 2]);
+        a += x;
+        b += y;
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    *layers_ms = a;
+    *head_ms = b;
+    return s;
 }
 
 icua_status icua_decode_batch(icua_engine* eng, const int32_t* sessions, int32_t n_sessions, const int32_t* in_tokens,

@@ -11,7 +11,9 @@
 // within each 128-byte half, which is exactly the 128-byte swizzle of a tile whose first slot is a
 // multiple of 8, so a 4-D TMA map (dims 64 x 2 halves x slots x heads, no TMA swizzle) lands each
 // half as a ready K-major atom.  V enters the P V product as V^T [dims][slots] (K-major), written
-// per call by vt kernels.  S = Q K^T (M=128, N=64, K=128) and O_j = P_j V_j (M=128, N=128, K=64)
+// per call by vt kernels, always in fp16 (a bf16 cache's values convert to fp16 exactly within the
+// fp16 range), so P is rounded to fp16 for both cache types: 11 significant bits instead of bf16's
+// 8 in the probabilities.  S = Q K^T (M=128, N=64, K=128) and O_j = P_j V_j (M=128, N=128, K=64)
 // run on tcgen05 with S, P and O double-buffered; four softmax warps own one row per thread (the
 // tensor-memory lane), mask slots past the row's position on the diagonal blocks only, and fold
 // O_j into fp32 registers after producing the next P.  Every wait is bounded.
@@ -147,7 +149,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) prefill_attn_tc_kernel(const __
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t id_s = umma_idesc_kv<KVT>(PT_BQ, PT_BK), id_o = umma_idesc_kv<KVT>(PT_BQ, 128);
+            const uint32_t id_s = umma_idesc_kv<KVT>(PT_BQ, PT_BK), id_o = umma_idesc_kv<__half>(PT_BQ, 128);
             const uint32_t q_sa = smem_u32(smem + S::q_off);
             bool ok = mbar_wait_bounded(q_full, 0);
             auto issue_s = [&](int j) -> bool {
@@ -238,7 +240,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) prefill_attn_tc_kernel(const __
                     const float p0 = ex2_approx(fmaf(v[8 * c + 2 * e], l2e, off));
                     const float p1 = ex2_approx(fmaf(v[8 * c + 2 * e + 1], l2e, off));
                     sum += p0 + p1;
-                    w[e] = pack_kv2<KVT>(p0, p1);
+                    w[e] = pack_kv2<__half>(p0, p1);
                 }
                 *reinterpret_cast<uint4*>(P + row * 128 + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
@@ -280,10 +282,11 @@ __global__ void __launch_bounds__(PT_THREADS, 1) prefill_attn_tc_kernel(const __
     }
 }
 
-// V^T of the prompt rows: vt[h][d][pos0 + i] = v of row i (qkv columns 3072 + 128 h + d), in the
-// cache type, 32 x 32 tiles through shared memory.  Grid (ceil(n / 32), 1024 / 32), 32 x 8.
+// V^T of the prompt rows: vt[h][d][pos0 + i] = v of row i (qkv columns 3072 + 128 h + d) rounded to
+// the cache type as the cache stores it, held in fp16; 32 x 32 tiles through shared memory.  Grid
+// (ceil(n / 32), 1024 / 32), 32 x 8.
 template <typename KVT>
-__global__ void __launch_bounds__(256) prefill_vt_kernel(const float* qkv, int n, int pos0, KVT* vt, int vstride) {
+__global__ void __launch_bounds__(256) prefill_vt_kernel(const float* qkv, int n, int pos0, __half* vt, int vstride) {
     __shared__ float tile[32][33];
     const int i0 = blockIdx.x * 32, c0 = blockIdx.y * 32;  // c = h * 128 + d
     for (int r = threadIdx.y; r < 32; r += 8) {
@@ -293,14 +296,14 @@ __global__ void __launch_bounds__(256) prefill_vt_kernel(const float* qkv, int n
     __syncthreads();
     for (int r = threadIdx.y; r < 32; r += 8) {
         const int i = i0 + threadIdx.x;
-        if (i < n) vt[(size_t)(c0 + r) * vstride + pos0 + i] = float_to_kv<KVT>(tile[threadIdx.x][r]);
+        if (i < n) vt[(size_t)(c0 + r) * vstride + pos0 + i] = __float2half_rn(kv_to_float(float_to_kv<KVT>(tile[threadIdx.x][r])));
     }
 }
 
-// V^T of the cache slots [0, n_slots) written by earlier calls: vt[h][d][p] = vc[h][p][kv_swz(d, p)].
-// Grid (ceil(n_slots / 32), 1024 / 32), 32 x 8.
+// V^T of the cache slots [0, n_slots) written by earlier calls: vt[h][d][p] = vc[h][p][kv_swz(d, p)],
+// in fp16.  Grid (ceil(n_slots / 32), 1024 / 32), 32 x 8.
 template <typename KVT>
-__global__ void __launch_bounds__(256) prefill_vt_gather_kernel(const KVT* vc, int max_ctx, int n_slots, KVT* vt,
+__global__ void __launch_bounds__(256) prefill_vt_gather_kernel(const KVT* vc, int max_ctx, int n_slots, __half* vt,
                                                                 int vstride) {
     __shared__ KVT tile[32][34];
     const int p0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
@@ -313,7 +316,7 @@ __global__ void __launch_bounds__(256) prefill_vt_gather_kernel(const KVT* vc, i
     __syncthreads();
     for (int r = threadIdx.y; r < 32; r += 8) {
         const int p = p0 + threadIdx.x;
-        if (p < n_slots) vt[(size_t)(c0 + r) * vstride + p] = tile[threadIdx.x][r];
+        if (p < n_slots) vt[(size_t)(c0 + r) * vstride + p] = __float2half_rn(kv_to_float(tile[threadIdx.x][r]));
     }
 }
 

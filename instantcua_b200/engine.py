@@ -269,6 +269,18 @@ class Engine:
     def inject_kv_random(self, n_pos: int, seed: int = 2, session: int = 0) -> None:
         L.check(self._lib.icua_inject_kv_random(self._h, session, n_pos, seed), self._h)
 
+    @property
+    def kernels_per_step(self) -> int:
+        """Kernels one decode step launches (3 on the persistent layers kernel)."""
+        return int(self._lib.icua_decode_kernels_per_step(self._h))
+
+    def profile_decode(self, steps: int, session: int = 0) -> tuple:
+        """Decodes ``steps`` tokens with CUDA events around each step's layers and lm_head + commit;
+        returns (layers ms, head ms) summed over the steps."""
+        a, b = C.c_double(), C.c_double()
+        L.check(self._lib.icua_profile_decode(self._h, session, steps, C.byref(a), C.byref(b)), self._h)
+        return a.value, b.value
+
     def position(self, session: int = 0) -> int:
         p = C.c_int32()
         L.check(self._lib.icua_session_position(self._h, session, C.byref(p)), self._h)

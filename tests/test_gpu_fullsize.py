@@ -7,7 +7,7 @@ pinned to the reference's own qwen3vl_ref.py by tests/test_oracle_ref.py.
 * Config 2: KV cache pre-filled to 4096 N(0,1) positions in bf16 (the benchmarked workload), 16
   steps: the first through icua_decode_step, the rest through the graph path (icua_decode).
 * Config 3: 1000 visual rows (25 x 40 grid, DeepStack at layers 0-2, 3-D M-RoPE) + 256 text
-  tokens through the tensor-core prefill, then 4 decode steps.
+  tokens through the tensor-core prefill, then 4 decode steps, with the reference's fp16 KV cache.
 * Config 4: 64 sessions with 2048 cached positions each, decoded together (icua_decode_batch);
   four of them carry host-known KV values and are checked against the oracle's per-session decode.
 
@@ -119,7 +119,8 @@ def test_config2_long_context_decode(full, kv, ctx):
     check(f"config2 ({kv}, ctx {ctx})", logits, want, toks)
 
 
-def test_config3_multimodal_prefill_full_size(full):
+@pytest.mark.parametrize("kv", ["f16"])  # the reference's KV type (Shaders.swift:776-783)
+def test_config3_multimodal_prefill_full_size(full, kv):
     tensors, w = full
     import torch
 
@@ -132,7 +133,7 @@ def test_config3_multimodal_prefill_full_size(full):
     pooler = bf16(rng.standard_normal((n_vis, 2048), dtype=np.float32))
     ds = [bf16(rng.standard_normal((n_vis, 2048), dtype=np.float32)) for _ in range(3)]
     prompt = np.concatenate([np.full(n_vis, O.IMAGE_PAD, np.int32), rng.integers(0, 151643, n_text).astype(np.int32)])
-    e = Engine(tensors=tensors, max_context=len(prompt) + 64, max_pass=len(prompt), max_steps=16, kv_dtype="bf16")
+    e = Engine(tensors=tensors, max_context=len(prompt) + 64, max_pass=len(prompt), max_steps=16, kv_dtype=kv)
     e.stop_on_eos = False
     cap = e.capture_step_logits(steps)
     first = e.prefill(prompt, pooler=pooler, deepstack=ds, grid=(llm_h, llm_w), write_logits=True)
@@ -141,9 +142,9 @@ def test_config3_multimodal_prefill_full_size(full):
     e.close()
     toks = [first] + rest
     logits = np.concatenate([first_logits[None], cap[: steps - 1]])
-    want = teacher_logits(O.TextModel(w, kv_dtype="bf16"), prompt, toks, pooler=pooler, deepstack=ds,
+    want = teacher_logits(O.TextModel(w, kv_dtype=kv), prompt, toks, pooler=pooler, deepstack=ds,
                           llm_hw=(llm_h, llm_w))
-    check("config3 1000 visual + 256 text", logits, want, toks)
+    check(f"config3 1000 visual + 256 text ({kv} KV)", logits, want, toks)
 
 
 def test_config4_batched_sessions_vs_oracle(full):
