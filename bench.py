@@ -108,7 +108,7 @@ def model_source_key() -> str:
     return h.hexdigest()[:16]
 
 
-def model_file(rank_local: int, dist, device: int) -> str:
+def model_file(rank_local: int, group, device: int) -> str:
     """Generates the seeded q4s model once per box (local rank 0) into /tmp and reuses it while the
     sources that produce it are unchanged."""
     path = f"/tmp/icua_bench_seed{SEED}_q4s_{model_source_key()}.icua"
@@ -119,59 +119,32 @@ def model_file(rank_local: int, dist, device: int) -> str:
         tmp = path + f".{os.getpid()}.tmp"
         model.write_icua(tmp, tensors)
         os.replace(tmp, path)
-    if dist is not None:
-        dist.barrier()
+    if group is not None:
+        group.barrier()
     return path
 
 
-def init_replicas(backend: str = "nccl"):
-    """One process per GPU (torchrun env).  Returns (dist or None, world, rank, local rank).  The
-    process group carries only the barriers and the max-over-ranks timing: every replica owns its
-    weights and caches, nothing crosses GPUs on the decode path."""
-    import datetime
+def replica_group(backend: str = "nccl"):
+    """The replicas of this launch (one process per GPU under torchrun): the product's ReplicaGroup,
+    whose process group carries only barriers and the end-of-run gather of counts and times."""
+    from instantcua_b200.replicas import ReplicaGroup
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world == 1:
-        return None, 1, 0, local
-    import torch
-    import torch.distributed as tdist
-
-    kw = {}
-    if backend == "nccl":
-        torch.cuda.set_device(local)
-        kw["device_id"] = torch.device("cuda", local)
-    tdist.init_process_group(backend, timeout=datetime.timedelta(seconds=600), **kw)
-    return tdist, world, rank, local
-
-
-def max_over_ranks(dist, value: float, device: str = "cuda") -> float:
-    """Max of a per-rank time over all ranks (the slowest replica sets the job time)."""
-    if dist is None:
-        return value
-    import torch
-
-    t = torch.tensor([value], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
-def aggregate_rate(units_per_rank: int, world: int, max_time_s: float) -> float:
-    """Whole-job rate: the units all ranks processed over the slowest rank's time."""
-    return world * units_per_rank / max_time_s
+    return ReplicaGroup(backend)
 
 
 def run_ours(args):
     import numpy as np
     import torch
 
-    dist, world, rank, local = init_replicas("nccl")
+    from instantcua_b200.replicas import aggregate_rate
+
+    group = replica_group("nccl")
+    world, rank, local = group.world, group.rank, group.local
     torch.cuda.set_device(local)
     from instantcua_b200 import Engine
     from instantcua_b200 import _lib as L
 
-    path = model_file(local, dist, local)
+    path = model_file(local, group, local)
     K, W = args.steps, args.warmup
     # S more warm-up steps run while the clock sampler starts (about half a second of decoding), so
     # the sampler's start-up never overlaps the timed steps; the cache is pre-filled so that the
@@ -187,21 +160,18 @@ def run_ours(args):
     tok = eng.decode_step(tok)  # primes the session
     eng.decode(W)  # warm-up steps (graphs instantiated, clocks up)
 
-    if dist is not None:
-        dist.barrier()
+    group.barrier()
     torch.cuda.synchronize()
     with Clocks(local) as clk:
         eng.decode(S)
         torch.cuda.synchronize()
         ctx0 = eng.position()
-        if dist is not None:
-            dist.barrier()
+        group.barrier()
         eng.decode(K)
         ms = eng.last_timing.decode_ms
     torch.cuda.synchronize()
-    ms = max_over_ranks(dist, ms)
-    if dist is not None:
-        dist.barrier()
+    ms = group.max_over_ranks(ms)
+    group.barrier()
     ms_step = ms / K
     value = aggregate_rate(K, world, ms / 1e3)
 
@@ -209,12 +179,11 @@ def run_ours(args):
     # to host, synchronised each call (inputs and results cross PCIe every step).
     KE = min(K, 64)
     cur = eng.decode(1)[-1]
-    if dist is not None:
-        dist.barrier()
+    group.barrier()
     t0 = time.perf_counter()
     for _ in range(KE):
         cur = eng.decode_step(cur)
-    e2e_s = max_over_ranks(dist, time.perf_counter() - t0)
+    e2e_s = group.max_over_ranks(time.perf_counter() - t0)
     e2e = aggregate_rate(KE, world, e2e_s)
 
     # Per-kernel rooflines: PROFILE_STEPS more steps with CUDA events (engine stream) around each
@@ -268,9 +237,7 @@ def run_ours(args):
             "gpu_launches": K * kps,
             "clocks": clk.summary(),
         }
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    group.close()
     if rank == 0 and not args.no_cpu_baseline and world == 1:
         out["cpu_baseline"] = cpu_baseline(path)
     if rank == 0:
@@ -641,31 +608,39 @@ BATCH_SESSIONS, BATCH_CTX, BATCH_STEPS = 64, 2048, 128
 
 
 def run_batched(args):
-    """Config 4: 64 concurrent sessions on one GPU (2048-position random KV each), greedy decode
-    of all of them together through the batched step (tensor-core GEMMs over the session rows,
-    per-session attention, per-row argmax).  value = tokens/s over all sessions; roofline = HBM
-    bytes of a step (weights once + every session's KV) per second."""
+    """Config 4: 64 concurrent sessions per GPU (2048-position random KV each), greedy decode of all
+    of them together through the batched step (tensor-core GEMMs over the session rows,
+    per-session attention, per-row argmax).  Under torchrun the job's 64 x N sessions are sharded
+    round-robin over the N replicas (instantcua_b200.replicas: one engine per GPU, no collective
+    while decoding, the counts and device times gathered at the end); value = tokens/s of the whole
+    job over the slowest replica's time; roofline = HBM bytes of one replica's step (weights once +
+    its sessions' KV) per second."""
     import numpy as np
     import torch
 
     from instantcua_b200 import Engine
+    from instantcua_b200.replicas import decode_shard, local_sessions
 
-    torch.cuda.set_device(0)
-    path = model_file(0, None, 0)
+    group = replica_group("nccl")
+    world, rank, local = group.world, group.rank, group.local
+    torch.cuda.set_device(local)
+    path = model_file(local, group, local)
     n, K, W = BATCH_SESSIONS, args.steps, args.warmup
     ctx = args.batch_ctx  # config 4: 2048; smaller for profiler captures of the same GEMM shapes
+    job = list(range(n * world))
+    mine = local_sessions(job, group)
     eng = Engine(path, max_context=ctx + K + W + 64, max_pass=n, max_steps=K + W + 16, kv_dtype="bf16",
-                 steps_per_graph=8, max_sessions=n)
+                 steps_per_graph=8, max_sessions=n, device=local)
     eng.stop_on_eos = False
-    for s in range(n):
-        eng.inject_kv_random(ctx, seed=100 + s, session=s)
-    toks = np.random.default_rng(4).integers(0, 151643, n).astype(np.int32)
-    sess = list(range(n))
-    eng.decode_batch(sess, max(W, 1), in_tokens=toks)  # warm-up (graphs built, clocks up)
+    for g, s in mine.items():
+        eng.inject_kv_random(ctx, seed=100 + g, session=s)
+    toks = {g: int(t) for g, t in zip(job, np.random.default_rng(4).integers(0, 151643, len(job)))}
+    decode_shard(eng, group, job, max(W, 1), in_tokens=toks)  # warm-up (graphs built, clocks up)
     ctx0 = eng.position(0)
     torch.cuda.synchronize()
-    with Clocks(0) as clk:
-        out = eng.decode_batch(sess, K)
+    group.barrier()
+    with Clocks(local) as clk:
+        _, total, job_s = decode_shard(eng, group, job, K)
         ms = eng.last_timing.decode_ms
     eng.close()
     ms_step = ms / K
@@ -673,17 +648,21 @@ def run_batched(args):
     step_b = NL * Q4_LAYER_BYTES + Q8_HEAD_BYTES + NORM_BYTES + n * KV_BYTES_PER_POS * ctx_mid
     peak, peak_kind = peaks()
     ach = step_b / (ms_step / 1e3) / 1e9
+    group.close()
+    if rank != 0:
+        return
     print(json.dumps({
-        "metric": "batched decode tokens/s (config 4, 64 sessions x 2K ctx)", "value": round(n * K / (ms / 1e3), 1),
-        "unit": "tokens/s", "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": round(ms_step, 4),
+        "metric": "batched decode tokens/s (config 4, 64 sessions x 2K ctx per GPU)", "value": round(total / job_s, 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(job_s * 1e3 / K, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "q4s/q8 weights as fp16 operands, fp32 accumulate, bf16 KV", "data": "synthetic (seeded weights, N(0,1) KV)",
-        "config": {"workload": f"config 4: {n} sessions, KV pre-filled to {ctx} positions, {K} batched greedy steps",
-                   "context_range": [ctx0, ctx0 + K]},
+        "config": {"workload": f"config 4: {n} sessions per GPU, KV pre-filled to {ctx} positions, {K} batched greedy steps",
+                   "sessions": len(job), "context_range": [ctx0, ctx0 + K],
+                   "parallelism": f"replicas x{world}, sessions sharded round-robin"},
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
                      "traffic": None, "bytes_per_step": int(step_b),
-                     "note": f"weights once + {n} sessions' KV at ctx {int(ctx_mid)} per step; peak {peak_kind}"},
-        "tokens_checked": int((out >= 0).sum()), "clocks": clk.summary(),
+                     "note": f"rank 0: weights once + {n} sessions' KV at ctx {int(ctx_mid)} per step; peak {peak_kind}"},
+        "tokens_checked": int(total), "clocks": clk.summary(),
     }))
 
 

@@ -93,3 +93,34 @@ class ReplicaGroup:
 def aggregate_rate(units_per_rank: int, world: int, max_time_s: float) -> float:
     """Whole-job rate when every replica processes the same number of units."""
     return world * units_per_rank / max_time_s
+
+
+def local_sessions(global_ids, group: ReplicaGroup) -> dict:
+    """{global session id: engine session index} for this replica's share (indices 0, 1, ... in the
+    order of the share)."""
+    return {g: i for i, g in enumerate(group.shard(global_ids))}
+
+
+def decode_shard(engine, group: ReplicaGroup, global_ids, steps: int, in_tokens=None):
+    """Decodes this replica's share of the job's sessions together (one batched call on its own
+    engine; the sessions must have been prefilled or injected at the indices of
+    :func:`local_sessions`) and gathers the job totals on the host.
+
+    ``in_tokens``: None to continue every session from its last token, or {global id: token}.
+    Returns ({global id: generated tokens (list, -1 after an EOS)}, job tokens, job seconds), where
+    job tokens counts every replica's generated tokens and job seconds is the slowest replica's
+    device time of its call.  No collective runs during decoding."""
+    mine = group.shard(global_ids)
+    results, n_tok, seconds = {}, 0, 0.0
+    if mine:
+        idx = list(range(len(mine)))
+        toks = None if in_tokens is None else [int(in_tokens[g]) for g in mine]
+        import numpy as np
+
+        out = engine.decode_batch(idx, steps, in_tokens=None if toks is None else np.asarray(toks, np.int32))
+        seconds = engine.last_timing.decode_ms / 1e3
+        for g, row in zip(mine, out):
+            results[g] = [int(t) for t in row]
+            n_tok += int((row >= 0).sum())
+    total, job_s = group.gather(n_tok, seconds)
+    return results, total, job_s

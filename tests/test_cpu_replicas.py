@@ -1,11 +1,16 @@
-"""The multi-GPU plumbing of bench.py on CPU: two `gloo` ranks (127.0.0.1) run the same replica
-bookkeeping the GPU run does under torchrun -- process group from the torchrun environment,
-max-over-ranks timing, whole-job rate -- with no data-path collective."""
+"""The multi-GPU plumbing on CPU: two `gloo` ranks (127.0.0.1) run the replica bookkeeping of
+instantcua_b200.replicas that bench.py and a serving host use under torchrun -- process group from
+the torchrun environment, round-robin session routing, max-over-ranks timing, the end-of-run gather
+of token counts -- with no collective while decoding (a stand-in engine records what each rank was
+asked to decode)."""
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch.multiprocessing as mp
+
+from instantcua_b200 import replicas as R
 
 
 def _free_port():
@@ -16,23 +21,43 @@ def _free_port():
     return port
 
 
+class _FakeEngine:
+    """decode_batch / last_timing of Engine, recording the calls (no GPU)."""
+
+    class _T:
+        decode_ms = 0.0
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.calls = []
+        self.last_timing = self._T()
+
+    def decode_batch(self, sessions, steps, in_tokens=None):
+        self.calls.append((list(sessions), steps, None if in_tokens is None else list(in_tokens)))
+        self.last_timing.decode_ms = 100.0 + 25.0 * self.rank  # the slowest rank sets the job time
+        out = np.full((len(sessions), steps), 7, np.int32)
+        if len(sessions):
+            out[0, steps - 1] = -1  # one session stopped early: counts exclude it
+        return out
+
+
 def _rank_main(rank, world, port, q):
     os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "WORLD_SIZE": str(world),
                        "RANK": str(rank), "LOCAL_RANK": str(rank)})
-    import bench
-
-    dist, w, r, local = bench.init_replicas("gloo")
-    assert (w, r, local) == (world, rank, rank)
-    ms = 100.0 + 25.0 * rank  # the slowest rank sets the job time
-    ms_max = bench.max_over_ranks(dist, ms, device="cpu")
-    rate = bench.aggregate_rate(64, w, ms_max / 1e3)
-    dist.barrier()
-    dist.destroy_process_group()
-    q.put((rank, ms_max, rate))
+    g = R.ReplicaGroup("gloo", timeout_s=60)
+    assert (g.world, g.rank, g.local) == (world, rank, rank)
+    ms_max = g.max_over_ranks(100.0 + 25.0 * rank)
+    rate = R.aggregate_rate(64, g.world, ms_max / 1e3)
+    job = list(range(10))
+    eng = _FakeEngine(rank)
+    toks = {gid: 1000 + gid for gid in job}
+    res, total, job_s = R.decode_shard(eng, g, job, 3, in_tokens=toks)
+    g.close()
+    q.put((rank, ms_max, rate, eng.calls, sorted(res), total, job_s, R.local_sessions(job, g)))
 
 
 @pytest.mark.parametrize("world", [2])
-def test_replica_timing_over_gloo(world):
+def test_replica_routing_and_timing_over_gloo(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -44,19 +69,38 @@ def test_replica_timing_over_gloo(world):
         assert p.exitcode == 0
     res = sorted(q.get(timeout=10) for _ in range(world))
     slowest = 100.0 + 25.0 * (world - 1)
-    for rank, ms_max, rate in res:
+    seen = []
+    for rank, ms_max, rate, calls, got, total, job_s, mapping in res:
         assert ms_max == slowest
         assert rate == pytest.approx(world * 64 / (slowest / 1e3))
+        mine = list(range(10))[rank::world]
+        assert got == mine and list(mapping) == mine and list(mapping.values()) == list(range(len(mine)))
+        ((sess, steps, toks),) = calls  # one batched call per rank, on engine indices 0..n-1
+        assert sess == list(range(len(mine))) and steps == 3 and toks == [1000 + g for g in mine]
+        assert total == 10 * 3 - world  # every rank's tokens, minus one stopped session per rank
+        assert job_s == pytest.approx(slowest / 1e3)
+        seen += got
+    assert sorted(seen) == list(range(10))
+
+
+def test_shard_sessions_round_robin():
+    ids = [11, 12, 13, 14, 15, 16, 17]
+    shards = [R.shard_sessions(ids, 3, r) for r in range(3)]
+    assert shards == [[11, 14, 17], [12, 15], [13, 16]]
+    assert sorted(sum(shards, [])) == ids
+    assert all(R.owner_of(i, 3) == r for r in range(3) for i in range(r, len(ids), 3))
+    with pytest.raises(ValueError):
+        R.shard_sessions(ids, 2, 2)
 
 
 def test_single_process_needs_no_group():
-    import bench
-
     env = {k: os.environ.pop(k) for k in ("WORLD_SIZE", "RANK", "LOCAL_RANK") if k in os.environ}
     try:
-        dist, w, r, local = bench.init_replicas("gloo")
-        assert dist is None and (w, r) == (1, 0)
-        assert bench.max_over_ranks(None, 3.5) == 3.5
+        g = R.ReplicaGroup("gloo")
+        assert g.dist is None and (g.world, g.rank) == (1, 0)
+        assert g.max_over_ranks(3.5) == 3.5 and g.gather(5, 2.0) == (5, 2.0)
+        assert g.shard([4, 5]) == [4, 5]
+        g.close()
     finally:
         os.environ.update(env)
 
