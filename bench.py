@@ -666,6 +666,32 @@ def run_batched(args):
     }))
 
 
+def run_probe(args):
+    """A small decode run for profiler captures of the decode kernels (not a bench line of the
+    headline): a synthetic model with --probe-layers decoder layers and --probe-vocab rows of tied
+    embedding (default 16384: a smaller lm_head than the bench's), KV pre-filled to --probe-ctx bf16
+    positions, then
+    warm-up steps and --steps steps through the CUDA-graph path.  Prints the per-step time."""
+    import torch
+
+    from instantcua_b200 import Engine, model
+
+    torch.cuda.set_device(0)
+    nl, ctx, K, voc = args.probe_layers, args.probe_ctx, args.steps, args.probe_vocab
+    t = model.quantize_stream(model.synthetic_fp32_fast(seed=SEED, n_layers=nl, vocab=voc))
+    eng = Engine(tensors=t, n_layers=nl, vocab=voc, max_context=ctx + K + args.warmup + 64, max_pass=16,
+                 max_steps=K + args.warmup + 16, kv_dtype="bf16", steps_per_graph=8)
+    eng.stop_on_eos = False
+    eng.inject_kv_random(ctx, seed=2)
+    tok = eng.decode_step(5)
+    eng.decode(max(args.warmup, 1))
+    eng.decode(K)
+    ms = eng.last_timing.decode_ms
+    print(json.dumps({"probe": f"{nl} layers, ctx {ctx}, {K} steps", "ms_per_step": round(ms / K, 5),
+                      "kernels_per_step": eng.kernels_per_step, "first_token": tok}))
+    eng.close()
+
+
 def host_blas_threads():
     """All host cores for the numpy oracle's BLAS, whatever OMP_NUM_THREADS torchrun exported."""
     from threadpoolctl import threadpool_limits
@@ -729,10 +755,14 @@ def main():
     ap.add_argument("--batched", action="store_true", help="config 4: 64 sessions decoded together")
     ap.add_argument("--gemm", action="store_true", help="the prefill GEMMs alone (config 3 shapes)")
     ap.add_argument("--vision", action="store_true", help="the vision encoder on a config-3 sized image")
+    ap.add_argument("--probe", action="store_true", help="small decode run for profiler captures")
+    ap.add_argument("--probe-layers", type=int, default=4)
+    ap.add_argument("--probe-ctx", type=int, default=4096)
+    ap.add_argument("--probe-vocab", type=int, default=16384)
     ap.add_argument("--batch-ctx", type=int, default=BATCH_CTX,
                     help="--batched: KV positions per session (config 4: 2048; smaller for ncu captures)")
     args = ap.parse_args()
-    if args.warmup < 3 and not (args.prefill or args.batched or args.micro or args.gemm or args.vision):
+    if args.warmup < 3 and not (args.prefill or args.batched or args.micro or args.gemm or args.vision or args.probe):
         args.warmup = 3  # the headline bench always warms up; the side modes allow short profiling runs
     if args.impl == "reference":
         run_reference(args)
@@ -746,6 +776,8 @@ def main():
         run_gemm(args)
     elif args.vision:
         run_vision(args)
+    elif args.probe:
+        run_probe(args)
     else:
         run_ours(args)
 
