@@ -192,6 +192,7 @@ def run_ours(args):
     ctx_p = eng.position()
     lay_ms, head_ms = eng.profile_decode(PROFILE_STEPS)
     kps = eng.kernels_per_step
+    dev_bytes = eng.device_bytes
     roof = None
     if rank == 0:
         roof = lm_head_roofline(torch, L, peak)
@@ -235,6 +236,7 @@ def run_ours(args):
             "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 24, "d2h_bytes_per_step": 4,
                     "api": "icua_decode_step (host token in, host token out, synchronised per step)", "steps": KE},
             "gpu_launches": K * kps,
+            "engine_device_bytes": dev_bytes,
             "clocks": clk.summary(),
         }
     group.close()

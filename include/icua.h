@@ -141,6 +141,11 @@ icua_status icua_decode(icua_engine* eng, int32_t session, int32_t max_new, int3
  * The step's logits are kept for icua_get_logits. */
 icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token, int32_t* out_token);
 
+/* Device memory the engine holds (bytes of its own allocations: weights, KV caches, scratch). The
+ * tensor-core tile order copy of the quantised matrices, read only by batched decode, is allocated
+ * on the first icua_decode_batch.  0 for NULL. */
+uint64_t icua_device_bytes(const icua_engine* eng);
+
 /* Kernels one decode step launches on this engine: 3 for q4s engines on the persistent layers
  * kernel (all layers in one cooperative launch, then the lm_head GEMV and the commit), else
  * 5 x n_layers + 2 (one launch per projection / attention, lm_head, commit).  0 for NULL. */

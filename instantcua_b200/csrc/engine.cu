@@ -118,6 +118,7 @@ struct icua_engine {
     int* cta_best_i = nullptr;
     std::vector<Session> sessions;
     std::vector<void*> allocations;
+    unsigned long long device_bytes = 0;  // sum of the allocations' sizes
     int eos0 = 151645, eos1 = 151643, stop_on_eos = 1;
     int prefix_cache = 1;  // reference Engine.usePrefixCache (Engine.swift:40), on by default
     // grammar-guided 2-token commit (reference k_commit): off unless icua_set_grammar_commit
@@ -170,6 +171,7 @@ struct icua_engine {
     float2* vrope = nullptr;
     __half* vvt = nullptr;  // V^T per head [16][64][vit_np_max + 8]
     int vis_rows = -1;
+    bool tc_ready = false;  // tensor-core tile order copies made (ensure_tc_order)
     // persistent decode step (decode_mk.cuh): q4s engines run every layer of a step in one
     // cooperative launch; mk is false when the device or configuration cannot (launch chain)
     bool mk = false;
@@ -206,6 +208,7 @@ icua_status dalloc(icua_engine* eng, void** p, size_t bytes) {
     cudaError_t e = cudaMalloc(p, bytes < 16 ? 16 : bytes);
     if (e != cudaSuccess) return fail(eng, ICUA_ERR_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
     eng->allocations.push_back(*p);
+    eng->device_bytes += bytes < 16 ? 16 : bytes;
     return ICUA_OK;
 }
 
@@ -953,12 +956,29 @@ icua_status upload_matrix(icua_engine* eng, Matrix& m, int fmt, int rows, int k,
     icua_status s = dalloc(eng, reinterpret_cast<void**>(&m.dev), bytes);
     if (s != ICUA_OK) return s;
     CK(cudaMemcpy(m.dev, packed.data(), bytes, cudaMemcpyHostToDevice));
-    if (rows % TC_BM == 0) {  // every matrix the tensor-core GEMMs read
-        if ((s = dalloc(eng, reinterpret_cast<void**>(&m.tc), bytes)) != ICUA_OK) return s;
+    return ICUA_OK;
+}
+
+// The tensor-core tile order of a quantised matrix (128-row groups of 8 units contiguous per
+// k-block, one bulk copy per GEMM stage) is a second copy of it, read only by the batched decode
+// GEMMs.  It is made on the first batched decode, so that batch-1 engines, whose GEMVs read the
+// device tile layout, hold each matrix once.
+icua_status ensure_tc_order(icua_engine* eng) {
+    if (eng->tc_ready) return ICUA_OK;
+    std::vector<Matrix*> ms{&eng->embed};
+    for (Layer& ly : eng->layers) ms.insert(ms.end(), {&ly.qkv, &ly.o, &ly.gu, &ly.d});
+    icua_status s;
+    for (Matrix* m : ms) {
+        if (m->fmt == FMT_F16 || m->tc || m->n_rows % TC_BM) continue;
+        const size_t bytes = icua_packed_bytes(m->fmt, m->n_rows, m->k);
+        if ((s = dalloc(eng, reinterpret_cast<void**>(&m->tc), bytes)) != ICUA_OK) return s;
         const long long nv = (long long)bytes / 16;
-        tc_order_kernel<<<(int)std::min<long long>((nv + 255) / 256, 4096), 256>>>(m.dev, fmt, rows / 16, k / 64, m.tc);
+        tc_order_kernel<<<(int)std::min<long long>((nv + 255) / 256, 4096), 256, 0, eng->stream>>>(
+            m->dev, m->fmt, m->n_rows / 16, m->k / 64, m->tc);
         CK(cudaGetLastError());
     }
+    CK(cudaStreamSynchronize(eng->stream));
+    eng->tc_ready = true;
     return ICUA_OK;
 }
 
@@ -2103,6 +2123,8 @@ icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token
     return ICUA_OK;
 }
 
+uint64_t icua_device_bytes(const icua_engine* eng) { return eng ? eng->device_bytes : 0; }
+
 int32_t icua_decode_kernels_per_step(const icua_engine* eng) {
     if (!eng) return 0;
     if (eng->mk && !eng->grammar) return 3;  // persistent layers kernel, lm_head GEMV, commit
@@ -2181,6 +2203,7 @@ static icua_status decode_batch_impl(icua_engine* eng, const int32_t* sessions, 
     }
     CK(cudaSetDevice(eng->cfg.device));
     const int spg = eng->cfg.steps_per_graph;
+    if ((s = ensure_tc_order(eng)) != ICUA_OK) return s;
     if (key != eng->batch_key) {
         drop_batch_graphs(eng);
         CK(cudaMemcpy(eng->batch_rows, key.data(), (size_t)n_sessions * 4, cudaMemcpyHostToDevice));

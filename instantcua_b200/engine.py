@@ -274,6 +274,11 @@ class Engine:
         """Kernels one decode step launches (3 on the persistent layers kernel)."""
         return int(self._lib.icua_decode_kernels_per_step(self._h))
 
+    @property
+    def device_bytes(self) -> int:
+        """Bytes of device memory the engine holds (its own allocations)."""
+        return int(self._lib.icua_device_bytes(self._h))
+
     def profile_decode(self, steps: int, session: int = 0) -> tuple:
         """Decodes ``steps`` tokens with CUDA events around each step's layers and lm_head + commit;
         returns (layers ms, head ms) summed over the steps."""

@@ -132,3 +132,21 @@ def test_batch_errors(tensors):
     with pytest.raises(IcuaError):
         e.decode_batch([0, 5], 2, in_tokens=[1, 2])  # out of range
     e.close()
+
+
+def test_tile_order_copy_made_on_first_batched_decode(tensors):
+    """The q4s/q8 matrices are held once until a batched decode asks for the tensor-core tile
+    order; then exactly one copy of each matrix the batched GEMMs read is added."""
+    e = make_engine(tensors, sessions=2)
+    first = e.prefill(prompts(1)[0], session=0)
+    e.decode(4)
+    before = e.device_bytes
+    e.decode_batch([0], 2, in_tokens=[first])
+    added = e.device_bytes - before
+    H, QKV, GU, FF, V = 2048, 4096, 12288, 6144, 1024
+    want = L.lib().icua_packed_bytes(L.FMT_Q8, V, H) + 2 * sum(
+        L.lib().icua_packed_bytes(L.FMT_Q4S, r, k) for r, k in ((QKV, H), (H, H), (GU, H), (H, FF)))
+    assert added == want, (added, want)
+    e.decode_batch([0], 2)  # a second call adds nothing
+    assert e.device_bytes == before + added
+    e.close()
