@@ -395,7 +395,8 @@ cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaSt
     cfg.gridDim = dim3((p.m_tok + t.bn - 1) / t.bn, p.n_rows / (TC_BM * t.mh), ksplit);
     cfg.blockDim = dim3(TC_THREADS);
     p.max_stages = max_stages;
-    cfg.dynamicSmemBytes = TcLayout(t.bn, t.mh, FMT, EPI == TC_ARGMAX, max_stages).alloc;
+    cfg.dynamicSmemBytes =
+        TcLayout(t.bn, t.mh, FMT, EPI == TC_ARGMAX, max_stages, tc_a_in_tmem(FMT, p.wtc != nullptr, t.mh, t.bn)).alloc;
     cfg.stream = s;
     // programmatic dependent launch: only where the weights are not the previous kernel's output
     // (engine matrices); the kernel waits for the previous kernel before its activation loads
@@ -413,6 +414,10 @@ cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaSt
 }
 
 constexpr int SPLITK_MAX = 8;      // K slices of the batched GEMMs
+// Pipeline depth of the batched 4-bit GEMMs: with the A tiles in tensor memory a stage holds only
+// the quantised weights and the activation tile in shared memory (12.6 KB at 64 rows), so two CTAs
+// (this GEMM's and the next kernel's, programmatic launch) still fit on an SM at this depth.
+constexpr int BATCH_STAGES_4BIT = 6;
 constexpr int SPLITK_MAX_ROWS = 128;  // split K only for batches of up to this many rows
 
 // Batched-decode GEMM over few rows: when the weight-row tiles alone cannot fill the GPU, K is
@@ -430,8 +435,8 @@ cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmPar
             return launch_tc_gemm<E, FMT_F16>(x, e->cfg.max_pass, q, s, reinterpret_cast<const __half*>(m.dev), ksplit,
                                               true, 3);
         if (m.fmt == FMT_Q8) return launch_tc_gemm<E, FMT_Q8>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, 3);
-        if (m.fmt == FMT_Q4A) return launch_tc_gemm<E, FMT_Q4A>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, 3);
-        return launch_tc_gemm<E, FMT_Q4S>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, 3);
+        if (m.fmt == FMT_Q4A) return launch_tc_gemm<E, FMT_Q4A>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, BATCH_STAGES_4BIT);
+        return launch_tc_gemm<E, FMT_Q4S>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, BATCH_STAGES_4BIT);
     };
     if (ks < 2 || p.m_tok > SPLITK_MAX_ROWS) return run(std::integral_constant<int, EPI>{}, p, 1);
     TcGemmParams q = p;
@@ -959,9 +964,9 @@ icua_status upload_matrix(icua_engine* eng, Matrix& m, int fmt, int rows, int k,
     return ICUA_OK;
 }
 
-// The tensor-core tile order of a quantised matrix (128-row groups of 8 units contiguous per
-// k-block, one bulk copy per GEMM stage) is a second copy of it, read only by the batched decode
-// GEMMs.  It is made on the first batched decode, so that batch-1 engines, whose GEMVs read the
+// The tensor-core order of a quantised matrix (each 128-row block of a k-block contiguous, one
+// bulk copy per GEMM stage; rows of 32 bytes for the 4-bit formats) is a second copy of it, read
+// only by the batched decode GEMMs.  It is made on the first batched decode, so that batch-1 engines, whose GEMVs read the
 // device tile layout, hold each matrix once.
 icua_status ensure_tc_order(icua_engine* eng) {
     if (eng->tc_ready) return ICUA_OK;
@@ -973,8 +978,11 @@ icua_status ensure_tc_order(icua_engine* eng) {
         const size_t bytes = icua_packed_bytes(m->fmt, m->n_rows, m->k);
         if ((s = dalloc(eng, reinterpret_cast<void**>(&m->tc), bytes)) != ICUA_OK) return s;
         const long long nv = (long long)bytes / 16;
-        tc_order_kernel<<<(int)std::min<long long>((nv + 255) / 256, 4096), 256, 0, eng->stream>>>(
-            m->dev, m->fmt, m->n_rows / 16, m->k / 64, m->tc);
+        const int grid = (int)std::min<long long>((nv + 255) / 256, 4096);
+        if (m->fmt == FMT_Q8)
+            tc_order_kernel<<<grid, 256, 0, eng->stream>>>(m->dev, m->fmt, m->n_rows / 16, m->k / 64, m->tc);
+        else  // 4-bit formats: row order, 16-byte stores in the GEMM's dequantisation
+            tc_order_rows_kernel<<<grid, 256, 0, eng->stream>>>(m->dev, m->fmt, m->n_rows / 16, m->k / 64, m->tc);
         CK(cudaGetLastError());
     }
     CK(cudaStreamSynchronize(eng->stream));

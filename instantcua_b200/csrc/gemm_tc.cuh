@@ -43,8 +43,9 @@ enum TcEpi { TC_STORE = 0, TC_RESID = 1, TC_SWIGLU = 2, TC_ARGMAX = 3, TC_GELU =
 
 struct TcGemmParams {
     const uint8_t* w;          // weights in the device tile layout [n_rows, k] (q4s, q4a or q8)
-    const uint8_t* wtc;        // the same weights in tensor-core tile order (tc_order_kernel), or
-                               //   nullptr: then each stage gathers 8 x MH units from `w`
+    const uint8_t* wtc;        // the same weights in tensor-core order (tc_order_kernel for q8,
+                               //   tc_order_rows_kernel for the 4-bit formats), or nullptr: then
+                               //   each stage gathers 8 x MH units from `w`
     int n_rows, k, n_tiles, upt;
     int m_tok;                 // activation rows (tokens)
     int bn;                    // tokens per CTA tile (multiple of 16, <= 256; the TMA box height)
@@ -79,6 +80,18 @@ __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f 
 
 // Shared-memory layout of one CTA for a (BN, MH, format) choice; the same arithmetic runs on the
 // host (launch size) and the device (offsets).
+// A operand in tensor memory: for the 4-bit formats in row order (the batched decode GEMMs) with one
+// accumulator of at most 128 columns, the dequantising warps write each stage's A tile [128 rows][64]
+// with tcgen05.st into TMEM columns after the accumulator (lane = weight row, two fp16 of
+// consecutive k per 32-bit column), and the MMA reads it from there: the A tile never passes
+// through shared memory, whose bandwidth (A written by the CUDA cores and read by the tensor core
+// at 4 bytes per weight) bounded these GEMMs.  256 TMEM columns: the accumulator, then 32 per stage.
+__host__ __device__ constexpr int tc_acc_cols(int bn) { return (bn + 31) & ~31; }
+__host__ __device__ constexpr int tc_tmem_a_slots(int bn) { return (256 - tc_acc_cols(bn)) / 32; }
+__host__ __device__ constexpr bool tc_a_in_tmem(int fmt, bool row_order, int mh, int bn) {
+    return (fmt == 2 || fmt == 3) && row_order && mh == 1 && bn <= 128;  // FMT_Q4A, FMT_Q4S
+}
+
 struct TcLayout {
     int S;                                   // pipeline stages
     int a_bytes, b_bytes, raw_bytes, stage_bytes;
@@ -86,14 +99,17 @@ struct TcLayout {
     // max_stages: 8 for throughput GEMMs; the batched-decode GEMMs take 3, which halves the
     // footprint so that the next kernel's CTA (programmatic launch) fits beside this one on an SM
     // (measured 2% faster per batched step than 4 to 7 stages, 6% faster than 2)
-    __host__ __device__ TcLayout(int bn, int mh, int fmt, bool argmax, int max_stages = 8) {
-        a_bytes = mh * TC_BM * 128;          // fp16 [mh * 128][64], swizzled
+    // a_tmem: the dequantised A tiles live in tensor memory (tc_a_in_tmem), at most
+    // tc_tmem_a_slots(bn) stages of them
+    __host__ __device__ TcLayout(int bn, int mh, int fmt, bool argmax, int max_stages = 8, bool a_tmem = false) {
+        a_bytes = a_tmem ? 0 : mh * TC_BM * 128;  // fp16 [mh * 128][64], swizzled
         b_bytes = bn * 128;                  // fp16 [bn][64], swizzled by TMA
         raw_bytes = mh * 8 * unit_bytes(fmt);
         stage_bytes = a_bytes + b_bytes + raw_bytes;
         const int red = argmax ? 4 * mh * bn * 8 : 0;
         S = (TC_SMEM_BUDGET - red - 1024 - 512) / stage_bytes;
         if (S > max_stages) S = max_stages;
+        if (a_tmem && S > tc_tmem_a_slots(bn)) S = tc_tmem_a_slots(bn);
         a_off = 0;
         b_off = a_off + S * a_bytes;
         raw_off = b_off + S * b_bytes;
@@ -140,6 +156,27 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t tmem_d, uint64_t adesc, uint
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
+}
+
+// The same with A read from tensor memory at `tmem_a` (K-major, 128 lanes = rows).
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes from registers, then waits until the
+// stores are done.
+__device__ __forceinline__ void tmem_st16_wait(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Arrives on `bar` once every tcgen05.mma issued so far by this thread has completed.
@@ -300,6 +337,100 @@ __device__ __forceinline__ void dequant_q4a_lane(const uint8_t* unit, int l, uin
     }
 }
 
+// Row order of the 4-bit formats (q4s, q4a) for the batched GEMMs: the 128-row block of one
+// 64-column k-block sits at ((tile / 8) * upt + kk) * 4608 as in tc_order_kernel, but inside the
+// block each row owns 32 contiguous bytes (row r at r * 32) whose 32-bit word j holds columns
+// 8j .. 8j+7 with column 8j + 2i in bits 4i .. 4i+3 and 8j + 2i + 1 in bits 16 + 4i .. 19 + 4i, so
+// that ((w >> 4i) & 0x000F000F) is the fp16 pair of two consecutive columns and one thread writes
+// 8 consecutive columns of the A tile with one 16-byte store.  The 512 bytes after them hold per
+// row the two 32-column group scales (q4s) or the unit's (scale, bias) pair (q4a), 4 bytes a row.
+// One thread per output word (nibbles gathered from the device tile layout) and per row's scales.
+constexpr int TC_ROWS_BLOCK = 4608;
+__global__ void tc_order_rows_kernel(const uint8_t* src, int fmt, int n_tiles, int upt, uint8_t* dst) {
+    const long long blocks = (long long)(n_tiles / 8) * upt;
+    const long long words = blocks * 128 * 8, total = words + blocks * 128;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const bool is_word = i < words;
+        const long long e = is_word ? i : i - words;
+        const long long b = is_word ? e >> 10 : e >> 7;   // block index: (g8 * upt + kk)
+        const int r = is_word ? (int)((e >> 3) & 127) : (int)(e & 127);
+        const int g8 = (int)(b / upt), kk = (int)(b % upt);
+        const int tile = g8 * 8 + (r >> 4), rt = r & 15, gq = rt & 7, up = rt >> 3;
+        const uint8_t* ub = src + icua_layout::unit_offset(fmt, n_tiles, upt, tile, kk);
+        uint8_t* blk = dst + b * TC_ROWS_BLOCK;
+        if (is_word) {
+            const int j = (int)(e & 7);
+            uint32_t w = 0;
+#pragma unroll
+            for (int c8 = 0; c8 < 8; ++c8) {  // column 8j + c8 of the unit
+                const int kin = 8 * j + c8, step = kin >> 4, k16 = kin & 15;
+                const int t = (k16 & 7) >> 1, odd = k16 & 1, hi8 = k16 >> 3;
+                const uint32_t sw = *reinterpret_cast<const uint32_t*>(ub + (gq * 4 + t) * 16 + step * 4);
+                const uint32_t u = (sw >> (odd * 16 + hi8 * 8 + up * 4)) & 0xFu;
+                w |= u << ((c8 & 1) * 16 + (c8 >> 1) * 4);
+            }
+            *reinterpret_cast<uint32_t*>(blk + r * 32 + j * 4) = w;
+        } else {
+            uint16_t v[2];
+            if (fmt == FMT_Q4S) {  // group scales of rows g (low half) and g + 8 (high half)
+                v[0] = *reinterpret_cast<const uint16_t*>(ub + 512 + gq * 8 + up * 2);
+                v[1] = *reinterpret_cast<const uint16_t*>(ub + 512 + gq * 8 + 4 + up * 2);
+            } else {  // q4a: (scale, bias) of row g at +0, of row g + 8 at +4
+                v[0] = *reinterpret_cast<const uint16_t*>(ub + 512 + gq * 8 + up * 4);
+                v[1] = *reinterpret_cast<const uint16_t*>(ub + 512 + gq * 8 + up * 4 + 2);
+            }
+            *reinterpret_cast<uint32_t*>(blk + 4096 + r * 4) = (uint32_t)v[0] | ((uint32_t)v[1] << 16);
+        }
+    }
+}
+
+// Dequantises half of one row of a row-order block: row r, columns 32 half .. +31 (one q4s scale
+// group), as 16 fp16 pairs of consecutive columns, with the arithmetic of dequant_q4s_lane /
+// dequant_q4a_lane (bit-identical values).
+template <int FMT>
+__device__ __forceinline__ void dequant_rows_regs(const uint8_t* blk, int r, int half, uint32_t (&h)[16]) {
+    const uint4 nib = *reinterpret_cast<const uint4*>(blk + r * 32 + half * 16);
+    const uint32_t sv = *reinterpret_cast<const uint32_t*>(blk + 4096 + r * 4);
+    __half2 mul, add;
+    if (FMT == FMT_Q4S) {
+        const __half s1 = __ushort_as_half((uint16_t)(half ? sv >> 16 : sv & 0xFFFFu));
+        mul = __halves2half2(s1, s1);
+        add = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032: u - 8 - 1024
+    } else {
+        const __half2 sb = *reinterpret_cast<const __half2*>(&sv);
+        mul = __half2half2(__low2half(sb));
+        add = __half2half2(__high2half(sb));
+    }
+    const __half2 base = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));  // 1024
+    const uint32_t w[4] = {nib.x, nib.y, nib.z, nib.w};
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t v = ((w[jj] >> (4 * i)) & 0x000F000Fu) | 0x64006400u;
+            __half2 x = *reinterpret_cast<const __half2*>(&v);
+            if (FMT == FMT_Q4S)
+                x = __hmul2(__hsub2(x, add), mul);
+            else
+                x = __hfma2(__hsub2(x, base), mul, add);
+            h[jj * 4 + i] = *reinterpret_cast<uint32_t*>(&x);
+        }
+    }
+}
+
+// The same into the swizzled shared-memory A tile: thread d takes row d / 2 and half d % 2, four
+// 16-byte stores of 8 consecutive columns.
+template <int FMT>
+__device__ __forceinline__ void dequant_rows_half(const uint8_t* blk, int d, uint8_t* A, int row_base) {
+    const int r = d >> 1, half = d & 1;
+    uint32_t h[16];
+    dequant_rows_regs<FMT>(blk, r, half, h);
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj)
+        *reinterpret_cast<uint4*>(A + sw128_off(row_base + r, 32 * half + 8 * jj)) =
+            make_uint4(h[jj * 4], h[jj * 4 + 1], h[jj * 4 + 2], h[jj * 4 + 3]);
+}
+
 template <int EPI, int FMT, int MH>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
                                                                 const __grid_constant__ CUtensorMap wmap,
@@ -307,8 +438,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     constexpr int UB = unit_bytes(FMT);
     constexpr int NU = 8 * MH;  // 16-row units per stage
     const int BN = p.bn;
-    const TcLayout SM(BN, MH, FMT, EPI == TC_ARGMAX, p.max_stages);
+    const bool ATM = tc_a_in_tmem(FMT, p.wtc != nullptr, MH, BN);  // A tiles in tensor memory
+    const TcLayout SM(BN, MH, FMT, EPI == TC_ARGMAX, p.max_stages, ATM);
     const int S = SM.S;
+    const uint32_t a_col0 = (uint32_t)tc_acc_cols(BN);  // ATM: stage s's A tile at columns a_col0 + 32 s
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base_u = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((base_u + 1023u) & ~1023u) - base_u);
@@ -426,6 +559,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 }
                 tc_fence_after();
                 const uint64_t bd = umma_desc_sw128(smem_u32(smem + SM.b_off + s * SM.b_bytes));
+                if (ATM) {
+                    const uint32_t at = tmem + a_col0 + 32u * (uint32_t)s;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)  // K = 16 per MMA: 8 TMEM columns of fp16 pairs
+                        tc_mma_f16_ts(tmem, at + 8u * (uint32_t)ks, bd + 2 * ks, idesc, (kc | ks) != 0);
+                    tc_commit(&empty[s]);
+                    continue;
+                }
 #pragma unroll
                 for (int h = 0; h < MH; ++h) {
                     const uint64_t ad = umma_desc_sw128(smem_u32(smem + SM.a_off + s * SM.a_bytes + h * TC_BM * 128));
@@ -449,15 +590,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             }
             const uint8_t* raw = smem + SM.raw_off + s * SM.raw_bytes;
             uint8_t* A = smem + SM.a_off + s * SM.a_bytes;
+            if (ATM) {
+                // warp w writes TMEM lanes 32 (w % 4) .. + 31 (its lane quarter): row 32 (w % 4) +
+                // lane, columns 32 half .. + 31 with half = 0 for warps 2..5, 1 for warps 6..9.  The
+                // slot was last read by the MMAs of stage kc - S, complete before this stage's copy
+                // was issued.
+                tc_fence_after();
+                const int q = warp & 3, half = (warp - 2) >> 2;
+                uint32_t h[16];
+                dequant_rows_regs<FMT>(raw, q * 32 + lane, half, h);
+                tmem_st16_wait(tmem + ((uint32_t)(q * 32) << 16) + a_col0 + 32u * (uint32_t)s + 16u * (uint32_t)half, h);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&afull[s]);
+                continue;
+            }
+            if (FMT != FMT_Q8 && p.wtc != nullptr) {
+                // row order (tc_order_rows_kernel): 16-byte stores of 8 consecutive columns
 #pragma unroll
-            for (int i = 0; i < MH; ++i) {
-                const int pi = d + 256 * i, t = pi >> 5;
-                if constexpr (FMT == FMT_Q4S)
-                    dequant_q4s_lane(raw + t * UB, pi & 31, A, t * 16);
-                else if constexpr (FMT == FMT_Q8)
-                    dequant_q8_lane(raw + t * UB, pi & 31, A, t * 16);
-                else if constexpr (FMT == FMT_Q4A)
-                    dequant_q4a_lane(raw + t * UB, pi & 31, A, t * 16);
+                for (int i = 0; i < MH; ++i) dequant_rows_half<FMT>(raw + i * TC_ROWS_BLOCK, d, A, i * TC_BM);
+            } else {
+#pragma unroll
+                for (int i = 0; i < MH; ++i) {
+                    const int pi = d + 256 * i, t = pi >> 5;
+                    if constexpr (FMT == FMT_Q4S)
+                        dequant_q4s_lane(raw + t * UB, pi & 31, A, t * 16);
+                    else if constexpr (FMT == FMT_Q8)
+                        dequant_q8_lane(raw + t * UB, pi & 31, A, t * 16);
+                    else if constexpr (FMT == FMT_Q4A)
+                        dequant_q4a_lane(raw + t * UB, pi & 31, A, t * 16);
+                }
             }
             fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
             __syncwarp();
