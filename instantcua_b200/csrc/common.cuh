@@ -135,6 +135,17 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     return false;
 }
 
+// Bounded wait that sleeps `ns` nanoseconds between polls after the first: for warps that are off
+// the critical path, so that their polling does not take issue slots from the thread that is on it.
+__device__ __forceinline__ bool mbar_wait_nap(uint64_t* bar, uint32_t parity, uint32_t ns, uint32_t limit = (1u << 22)) {
+    if (mbar_try_wait(bar, parity)) return true;
+    for (uint32_t i = 0; i < limit; ++i) {
+        __nanosleep(ns);
+        if (mbar_try_wait(bar, parity)) return true;
+    }
+    return false;
+}
+
 // L2 prefetch plan of a kernel: byte ranges that a later kernel of the step will read (weights,
 // cache rows), split evenly over this kernel's CTAs and requested before griddepcontrol.wait, so
 // HBM streams ahead of the dependency chain.  Ranges: `n` plain ranges, plus optionally the

@@ -471,7 +471,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         for (int s = 0; s < S; ++s) {
             mbar_init(&rawfull[s], 1);
             mbar_init(&bfull[s], 1);
-            mbar_init(&afull[s], 8);
+            mbar_init(&afull[s], ATM ? 9 : 8);  // ATM: + the producer's arrival with the activation bytes
             mbar_init(&empty[s], 1);
         }
         mbar_init(accfull, 1);
@@ -529,13 +529,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             int kc = 0;
             for (; kc < nk; ++kc) {
                 const int s = kc % S;
-                if (kc >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((kc / S - 1) & 1))) {
+                if (kc >= S && !(ATM ? mbar_wait_nap(&empty[s], (uint32_t)((kc / S - 1) & 1), 64)
+                                     : mbar_wait_bounded(&empty[s], (uint32_t)((kc / S - 1) & 1)))) {
                     atomicOr(p.err, ERR_WAIT_PREFILL);
                     break;
                 }
                 if (kc >= pre) issue_w(kc);
-                if (FMT != FMT_F16) mbar_expect_tx(&bfull[s], (uint32_t)SM.b_bytes);
-                tma_load_2d(smem + SM.b_off + s * SM.b_bytes, &xmap, (kb0 + (kc + krot) % nk) * TC_BK, tok0, &bfull[s]);
+                // ATM: the activation tile completes on afull[s] with the dequantised A tile, so that
+                // the MMA thread waits on one barrier per stage
+                uint64_t* xbar = ATM ? &afull[s] : &bfull[s];
+                if (FMT != FMT_F16) mbar_expect_tx(xbar, (uint32_t)SM.b_bytes);
+                tma_load_2d(smem + SM.b_off + s * SM.b_bytes, &xmap, (kb0 + (kc + krot) % nk) * TC_BK, tok0, xbar);
             }
             // the copies of the last stages complete before the CTA may exit (at once on success);
             // after a failed wait at kc >= S the stages issued are [0, kc), all within this range
@@ -543,13 +547,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             const int issued = kc < pre ? pre : kc;
             for (int c = (issued > S ? issued - S : 0); c < issued; ++c) {
                 if (FMT != FMT_F16) mbar_wait_bounded(&rawfull[c % S], (uint32_t)((c / S) & 1));
-                if (c < kc) mbar_wait_bounded(&bfull[c % S], (uint32_t)((c / S) & 1));
+                if (c < kc) mbar_wait_bounded(ATM ? &afull[c % S] : &bfull[c % S], (uint32_t)((c / S) & 1));
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_f16(TC_BM, BN);
-            for (int kc = 0; kc < nk; ++kc) {
+            if (ATM) {
+                // this thread paces the GEMM: one barrier per stage (A tile and activation tile),
+                // stage and phase as counters, the MMAs read the stage's A columns of TMEM
+                const uint64_t bd0 = umma_desc_sw128(smem_u32(smem + SM.b_off));
+                const uint32_t b_step = (uint32_t)SM.b_bytes >> 4;  // descriptor address units
+                int s = 0;
+                uint32_t ph = 0;
+                for (int kc = 0; kc < nk; ++kc) {
+                    if (!mbar_wait_bounded(&afull[s], ph)) {
+                        atomicOr(p.err, ERR_WAIT_PREFILL);
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t bd = bd0 + (uint64_t)(b_step * (uint32_t)s);
+                    const uint32_t at = tmem + a_col0 + 32u * (uint32_t)s;
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)  // K = 16 per MMA: 8 TMEM columns of fp16 pairs
+                        tc_mma_f16_ts(tmem, at + 8u * (uint32_t)ks, bd + 2 * ks, idesc, (kc | ks) != 0);
+                    tc_commit(&empty[s]);
+                    if (++s == S) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+                tc_commit(accfull);  // also on the error path: tracks the MMAs already issued
+            }
+            for (int kc = 0; kc < (ATM ? 0 : nk); ++kc) {
                 const int s = kc % S;
                 const uint32_t ph = (uint32_t)((kc / S) & 1);
                 // A operand: dequantised by the CUDA-core warps (afull), or fp16 weights by TMA (rawfull)
@@ -559,14 +589,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 }
                 tc_fence_after();
                 const uint64_t bd = umma_desc_sw128(smem_u32(smem + SM.b_off + s * SM.b_bytes));
-                if (ATM) {
-                    const uint32_t at = tmem + a_col0 + 32u * (uint32_t)s;
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks)  // K = 16 per MMA: 8 TMEM columns of fp16 pairs
-                        tc_mma_f16_ts(tmem, at + 8u * (uint32_t)ks, bd + 2 * ks, idesc, (kc | ks) != 0);
-                    tc_commit(&empty[s]);
-                    continue;
-                }
 #pragma unroll
                 for (int h = 0; h < MH; ++h) {
                     const uint64_t ad = umma_desc_sw128(smem_u32(smem + SM.a_off + s * SM.a_bytes + h * TC_BM * 128));
@@ -576,14 +598,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 }
                 tc_commit(&empty[s]);
             }
-            tc_commit(accfull);  // also on the error path: tracks the MMAs already issued
+            if (!ATM) tc_commit(accfull);  // also on the error path: tracks the MMAs already issued
         }
     } else {
         // ---- dequantisation: NU units x 32 lanes per stage over 256 threads ----
         const int d = threadIdx.x - 64;
         for (int kc = 0; kc < (FMT == FMT_F16 ? 0 : nk); ++kc) {
             const int s = kc % S;
-            const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(&rawfull[s], (uint32_t)((kc / S) & 1)));
+            const bool got = __all_sync(0xffffffffu, ATM ? mbar_wait_nap(&rawfull[s], (uint32_t)((kc / S) & 1), 32)
+                                                         : mbar_wait_bounded(&rawfull[s], (uint32_t)((kc / S) & 1)));
             if (!got) {
                 if (lane == 0) atomicOr(p.err, ERR_WAIT_PREFILL);
                 break;
