@@ -50,6 +50,10 @@ struct AttnParams {
     long long sess_rope_elems;  // float2 entries between sessions' RoPE tables
     int qkv_stride;
     __half* out16;
+    // split-K projection: the qkv rows are the sum of qkv_parts partial products qkv_part_stride
+    // floats apart, added here in slice order (0 or 1: qkv holds the projection itself)
+    int qkv_parts;
+    long long qkv_part_stride;
 };
 
 // NT: query tokens per pass the layout holds (2 in the grammar-commit kernels).
@@ -294,7 +298,15 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
     float4 x4 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (prep) {
         const int base = role < 2 ? (2 * h + role) * HD : (role == 2 ? 2048 + h * HD : 3072 + h * HD);
-        x4 = *reinterpret_cast<const float4*>(qkv + tk * QKV_ROWS + base + 4 * lane);
+        const float* src = qkv + tk * QKV_ROWS + base + 4 * lane;
+        x4 = *reinterpret_cast<const float4*>(src);
+        for (int z = 1; z < p.qkv_parts; ++z) {
+            const float4 y = *reinterpret_cast<const float4*>(src + z * p.qkv_part_stride);
+            x4.x += y.x;
+            x4.y += y.y;
+            x4.z += y.z;
+            x4.w += y.w;
+        }
     }
 
     if (*(volatile int*)&st->done) {  // uniform over the grid: no CTA reaches the cluster barriers

@@ -423,8 +423,13 @@ constexpr int SPLITK_MAX_ROWS = 128;  // split K only for batches of up to this 
 // Batched-decode GEMM over few rows: when the weight-row tiles alone cannot fill the GPU, K is
 // split over up to 8 CTA slices whose partial products a finish kernel sums in slice order
 // (deterministic) before the epilogue.
+// norm_w / norm_out (TC_RESID): the RMSNorm of the updated residual rows that follows, written
+// as fp16 rows; with split K it runs inside the finish kernel.  parts_out (TC_STORE): the caller
+// consumes the partial products itself (e->splitk_part, [parts][m][n]); *parts_out = the K split,
+// 1 when the GEMM stored its result in p.out.
 template <int EPI>
-cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmParams p, cudaStream_t s) {
+cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmParams p, cudaStream_t s,
+                       const float* norm_w = nullptr, __half* norm_out = nullptr, int* parts_out = nullptr) {
     const TcTile t = choose_tc_tile(p.n_rows, p.m_tok, e->n_sm, true);
     const int tiles = (p.n_rows / (TC_BM * t.mh)) * ((p.m_tok + t.bn - 1) / t.bn);
     int ks = std::min(SPLITK_MAX, e->n_sm / std::max(tiles, 1));
@@ -438,17 +443,35 @@ cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmPar
         if (m.fmt == FMT_Q4A) return launch_tc_gemm<E, FMT_Q4A>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, BATCH_STAGES_4BIT);
         return launch_tc_gemm<E, FMT_Q4S>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, BATCH_STAGES_4BIT);
     };
-    if (ks < 2 || p.m_tok > SPLITK_MAX_ROWS) return run(std::integral_constant<int, EPI>{}, p, 1);
+    if (parts_out) *parts_out = 1;
+    cudaError_t err;
+    if (ks < 2 || p.m_tok > SPLITK_MAX_ROWS) {
+        if ((err = run(std::integral_constant<int, EPI>{}, p, 1)) != cudaSuccess) return err;
+        if (EPI == TC_RESID && norm_w)
+            return launch(rmsnorm_rows_f16_kernel, p.m_tok, 256, 0, s, true, (const float*)p.out, norm_w, p.m_tok,
+                          norm_out);
+        return cudaSuccess;
+    }
     TcGemmParams q = p;
     q.out = e->splitk_part;
     q.ldo = p.n_rows;
     q.out_zstride = (long long)p.m_tok * p.n_rows;
-    cudaError_t err = run(std::integral_constant<int, TC_STORE>{}, q, ks);
-    if (err != cudaSuccess) return err;
+    if ((err = run(std::integral_constant<int, TC_STORE>{}, q, ks)) != cudaSuccess) return err;
+    if (EPI == TC_STORE && parts_out) {
+        *parts_out = ks;
+        return cudaSuccess;
+    }
+    if (EPI == TC_RESID && norm_w && p.n_rows == H)
+        return launch(splitk_resid_norm_kernel, p.m_tok, 256, 0, s, true, (const float*)e->splitk_part, ks, p.m_tok,
+                      p.out, norm_w, norm_out);
     const long long total = (long long)p.m_tok * p.n_rows;
     const int grid = (int)std::min<long long>((total + 255) / 256, 4LL * e->n_sm);
-    return launch(splitk_finish_kernel<EPI>, grid, 256, 0, s, true, (const float*)e->splitk_part, ks, p.m_tok,
-                  p.n_rows, p.out, p.out_h);
+    if ((err = launch(splitk_finish_kernel<EPI>, grid, 256, 0, s, true, (const float*)e->splitk_part, ks, p.m_tok,
+                      p.n_rows, p.out, p.out_h)) != cudaSuccess)
+        return err;
+    if (EPI == TC_RESID && norm_w)
+        return launch(rmsnorm_rows_f16_kernel, p.m_tok, 256, 0, s, true, (const float*)p.out, norm_w, p.m_tok, norm_out);
+    return cudaSuccess;
 }
 
 cudaError_t launch_dequant_f16(const Matrix& m, __half* out, int n_sm, cudaStream_t s) {
@@ -1281,19 +1304,25 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
                       (const DevState*)e->st_all, (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->embed.fmt, e->px)) != cudaSuccess)
         return err;
     const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
+    // the RMSNorm before each projection runs in the finish of the GEMM that updated the residual
+    // (o-proj, down), so only layer 0's input norm is a launch of its own
+    if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, true, (const float*)e->px,
+                      (const float*)e->layers[0].attn_norm, n_rows, e->pxn)) != cudaSuccess)
+        return err;
     for (int l = 0; l < L; ++l) {
         Layer& ly = e->layers[l];
-        if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, true, (const float*)e->px,
-                          (const float*)ly.attn_norm, n_rows, e->pxn)) != cudaSuccess)
-            return err;
         TcGemmParams p = tc_params(ly.qkv, n_rows, e->gemm_err);
         p.out = e->pqkv;
         p.ldo = QKV_ROWS;
-        if ((err = batch_gemm<TC_STORE>(e, ly.qkv, e->pxn, p, st)) != cudaSuccess) return err;
+        int qkv_parts = 1;  // split K: the attention kernel adds the partial products itself
+        if ((err = batch_gemm<TC_STORE>(e, ly.qkv, e->pxn, p, st, nullptr, nullptr, &qkv_parts)) != cudaSuccess)
+            return err;
         {
             AttnParams<KVT> a{};
-            a.qkv = e->pqkv;
+            a.qkv = qkv_parts > 1 ? e->splitk_part : e->pqkv;
             a.qkv_stride = QKV_ROWS;
+            a.qkv_parts = qkv_parts;
+            a.qkv_part_stride = (long long)n_rows * QKV_ROWS;
             a.q_norm = ly.q_norm;
             a.k_norm = ly.k_norm;
             a.rope = e->rope_all;
@@ -1331,10 +1360,7 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
         p = tc_params(ly.o, n_rows, e->gemm_err);
         p.out = e->px;
         p.ldo = H;
-        if ((err = batch_gemm<TC_RESID>(e, ly.o, e->pattn, p, st)) != cudaSuccess) return err;
-        if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, true, (const float*)e->px,
-                          (const float*)ly.mlp_norm, n_rows, e->pxn)) != cudaSuccess)
-            return err;
+        if ((err = batch_gemm<TC_RESID>(e, ly.o, e->pattn, p, st, ly.mlp_norm, e->pxn)) != cudaSuccess) return err;
         p = tc_params(ly.gu, n_rows, e->gemm_err);
         p.out_h = e->ph;
         p.ldh = FF;
@@ -1342,11 +1368,9 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
         p = tc_params(ly.d, n_rows, e->gemm_err);
         p.out = e->px;
         p.ldo = H;
-        if ((err = batch_gemm<TC_RESID>(e, ly.d, e->ph, p, st)) != cudaSuccess) return err;
+        const float* next_norm = l + 1 < L ? e->layers[l + 1].attn_norm : e->final_norm;
+        if ((err = batch_gemm<TC_RESID>(e, ly.d, e->ph, p, st, next_norm, e->pxn)) != cudaSuccess) return err;
     }
-    if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, true, (const float*)e->px,
-                      (const float*)e->final_norm, n_rows, e->pxn)) != cudaSuccess)
-        return err;
     TcGemmParams p = tc_params(e->embed, n_rows, e->gemm_err);
     p.best_v = e->batch_best_v;
     p.best_i = e->batch_best_i;

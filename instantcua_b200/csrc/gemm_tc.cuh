@@ -885,4 +885,54 @@ __global__ void __launch_bounds__(256) splitk_finish_kernel(const float* part, i
     }
 }
 
+// Split-K finish of a residual GEMM over rows of H = 2048 fused with the RMSNorm that follows it:
+// one CTA per token row adds the Z partial products to the residual row in slice order (the sums
+// of splitk_finish_kernel<TC_RESID>), then writes the normalised fp16 row with the arithmetic of
+// rmsnorm_rows_f16_kernel (same element mapping and reduction order), so that the pair of kernels
+// it replaces and this one give the same bits.
+__global__ void __launch_bounds__(256) splitk_resid_norm_kernel(const float* part, int Z, int m, float* x,
+                                                                const float* w, __half* out) {
+    __shared__ float red[8];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int i = blockIdx.x, tid = threadIdx.x;
+    if (i >= m) return;
+    const long long total = (long long)m * H;
+    float4* xr = reinterpret_cast<float4*>(x + (size_t)i * H);
+    const float4* pr = reinterpret_cast<const float4*>(part + (size_t)i * H);
+    float4 a = pr[tid], b = pr[tid + 256];
+    for (int z = 1; z < Z; ++z) {
+        const float4* pz = reinterpret_cast<const float4*>(part + z * total + (size_t)i * H);
+        const float4 za = pz[tid], zb = pz[tid + 256];
+        a.x += za.x; a.y += za.y; a.z += za.z; a.w += za.w;
+        b.x += zb.x; b.y += zb.y; b.z += zb.z; b.w += zb.w;
+    }
+    const float4 xa = xr[tid], xb = xr[tid + 256];
+    a = make_float4(xa.x + a.x, xa.y + a.y, xa.z + a.z, xa.w + a.w);
+    b = make_float4(xb.x + b.x, xb.y + b.y, xb.z + b.z, xb.w + b.w);
+    xr[tid] = a;
+    xr[tid + 256] = b;
+    float ss = a.x * a.x;
+    ss = fmaf(a.y, a.y, ss);
+    ss = fmaf(a.z, a.z, ss);
+    ss = fmaf(a.w, a.w, ss);
+    ss = fmaf(b.x, b.x, ss);
+    ss = fmaf(b.y, b.y, ss);
+    ss = fmaf(b.z, b.z, ss);
+    ss = fmaf(b.w, b.w, ss);
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w2 = 0; w2 < 8; ++w2) tot += red[w2];
+    const float r = 1.0f / sqrtf(tot / (float)H + EPS);
+    const float4 wa = reinterpret_cast<const float4*>(w)[tid], wb = reinterpret_cast<const float4*>(w)[tid + 256];
+    __half2* o = reinterpret_cast<__half2*>(out + (size_t)i * H);
+    o[2 * tid] = __floats2half2_rn(a.x * r * wa.x, a.y * r * wa.y);
+    o[2 * tid + 1] = __floats2half2_rn(a.z * r * wa.z, a.w * r * wa.w);
+    o[2 * (tid + 256)] = __floats2half2_rn(b.x * r * wb.x, b.y * r * wb.y);
+    o[2 * (tid + 256) + 1] = __floats2half2_rn(b.z * r * wb.z, b.w * r * wb.w);
+}
+
 }  // namespace icua
