@@ -22,6 +22,7 @@ namespace icua {
 
 constexpr int ATT_SLOT = 16;   // cache rows per ring slot (one MMA block)
 constexpr int ATT_NS = 2;      // ring slots per warp
+constexpr int ATT_QKV_PARTS_MAX = 8;  // split-K slices of the projection the kernel can sum
 
 // KV rows are stored with their sixteen 16-byte chunks permuted by the row's position:
 // element d of position p lives at chunk (d / 8) ^ (p & 7).  Eight consecutive rows then cover
@@ -300,12 +301,20 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
         const int base = role < 2 ? (2 * h + role) * HD : (role == 2 ? 2048 + h * HD : 3072 + h * HD);
         const float* src = qkv + tk * QKV_ROWS + base + 4 * lane;
         x4 = *reinterpret_cast<const float4*>(src);
-        for (int z = 1; z < p.qkv_parts; ++z) {
-            const float4 y = *reinterpret_cast<const float4*>(src + z * p.qkv_part_stride);
-            x4.x += y.x;
-            x4.y += y.y;
-            x4.z += y.z;
-            x4.w += y.w;
+        if (p.qkv_parts > 1) {  // the slices' loads first, then the sums in slice order
+            float4 y[ATT_QKV_PARTS_MAX - 1];
+#pragma unroll
+            for (int z = 1; z < ATT_QKV_PARTS_MAX; ++z)
+                if (z < p.qkv_parts) y[z - 1] = *reinterpret_cast<const float4*>(src + z * p.qkv_part_stride);
+#pragma unroll
+            for (int z = 1; z < ATT_QKV_PARTS_MAX; ++z) {
+                if (z < p.qkv_parts) {
+                    x4.x += y[z - 1].x;
+                    x4.y += y[z - 1].y;
+                    x4.z += y[z - 1].z;
+                    x4.w += y[z - 1].w;
+                }
+            }
         }
     }
 

@@ -414,6 +414,7 @@ cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaSt
 }
 
 constexpr int SPLITK_MAX = 8;      // K slices of the batched GEMMs
+static_assert(SPLITK_MAX <= TC_SPLITK_MAX && SPLITK_MAX <= ATT_QKV_PARTS_MAX, "finish kernels unroll over the slices");
 // Pipeline depth of the batched 4-bit GEMMs: with the A tiles in tensor memory a stage holds only
 // the quantised weights and the activation tile in shared memory (12.6 KB at 64 rows), so two CTAs
 // (this GEMM's and the next kernel's, programmatic launch) still fit on an SM at this depth.

@@ -33,6 +33,7 @@
 namespace icua {
 
 constexpr int TC_BM = 128;      // weight rows per accumulator (UMMA M)
+constexpr int TC_SPLITK_MAX = 8;  // K slices of a split GEMM (finish kernels unroll over them)
 constexpr int TC_BK = 64;       // columns per stage: one 128-byte swizzle row of fp16
 constexpr int TC_THREADS = 320; // producer warp, MMA warp, 8 dequant / epilogue warps
 constexpr int TC_SMEM_BUDGET = 225 * 1024;
@@ -867,8 +868,13 @@ __global__ void __launch_bounds__(256) splitk_finish_kernel(const float* part, i
     pdl_launch_dependents();
     const long long total = (long long)m * n;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-        float acc = part[i];
-        for (int z = 1; z < Z; ++z) acc += part[(long long)z * total + i];
+        float pz[TC_SPLITK_MAX];
+#pragma unroll
+        for (int z = 0; z < TC_SPLITK_MAX; ++z) pz[z] = z < Z ? part[(long long)z * total + i] : 0.f;
+        float acc = pz[0];
+#pragma unroll
+        for (int z = 1; z < TC_SPLITK_MAX; ++z)
+            if (z < Z) acc += pz[z];
         if (EPI == TC_STORE) {
             out[i] = acc;
         } else if (EPI == TC_RESID) {
@@ -900,14 +906,25 @@ __global__ void __launch_bounds__(256) splitk_resid_norm_kernel(const float* par
     const long long total = (long long)m * H;
     float4* xr = reinterpret_cast<float4*>(x + (size_t)i * H);
     const float4* pr = reinterpret_cast<const float4*>(part + (size_t)i * H);
-    float4 a = pr[tid], b = pr[tid + 256];
-    for (int z = 1; z < Z; ++z) {
-        const float4* pz = reinterpret_cast<const float4*>(part + z * total + (size_t)i * H);
-        const float4 za = pz[tid], zb = pz[tid + 256];
-        a.x += za.x; a.y += za.y; a.z += za.z; a.w += za.w;
-        b.x += zb.x; b.y += zb.y; b.z += zb.z; b.w += zb.w;
+    // every load first (independent, in flight together), then the sums in slice order
+    float4 za[TC_SPLITK_MAX], zb[TC_SPLITK_MAX];
+#pragma unroll
+    for (int z = 0; z < TC_SPLITK_MAX; ++z) {
+        if (z < Z) {
+            const float4* pz = reinterpret_cast<const float4*>(part + z * total + (size_t)i * H);
+            za[z] = pz[tid];
+            zb[z] = pz[tid + 256];
+        }
     }
     const float4 xa = xr[tid], xb = xr[tid + 256];
+    float4 a = za[0], b = zb[0];
+#pragma unroll
+    for (int z = 1; z < TC_SPLITK_MAX; ++z) {
+        if (z < Z) {
+            a.x += za[z].x; a.y += za[z].y; a.z += za[z].z; a.w += za[z].w;
+            b.x += zb[z].x; b.y += zb[z].y; b.z += zb[z].z; b.w += zb[z].w;
+        }
+    }
     a = make_float4(xa.x + a.x, xa.y + a.y, xa.z + a.z, xa.w + a.w);
     b = make_float4(xb.x + b.x, xb.y + b.y, xb.z + b.z, xb.w + b.w);
     xr[tid] = a;
