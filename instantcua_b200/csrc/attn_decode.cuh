@@ -55,6 +55,7 @@ struct AttnParams {
     // floats apart, added here in slice order (0 or 1: qkv holds the projection itself)
     int qkv_parts;
     long long qkv_part_stride;
+    int out16_hilo;  // out16 as fp16 hi / lo row pairs (the batched GEMMs' input)
 };
 
 // NT: query tokens per pass the layout holds (2 in the grammar-commit kernels).
@@ -487,7 +488,15 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
             }
         }
         if (p.out16 != nullptr) {
-            p.out16[(size_t)row * H + (2 * h + hh) * HD + d] = __float2half_rn(O / Lsum);
+            const float y = O / Lsum;
+            const size_t col = (size_t)(2 * h + hh) * HD + d;
+            if (p.out16_hilo) {  // fp16 hi / lo rows 2 row, 2 row + 1
+                const __half hi = __float2half_rn(y);
+                p.out16[(size_t)(2 * row) * H + col] = hi;
+                p.out16[(size_t)(2 * row + 1) * H + col] = __float2half_rn(y - __half2float(hi));
+            } else {
+                p.out16[(size_t)row * H + col] = __float2half_rn(y);
+            }
         } else {
             // token tq's parts follow token 0's ([NTK][NKV][parts][ATT_PART])
             float* out = p.part + ((long long)(tq * NKV + h) * (NSP / CL) + j / CL) * ATT_PART;

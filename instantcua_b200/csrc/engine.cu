@@ -153,6 +153,7 @@ struct icua_engine {
     float* batch_best_v = nullptr;
     int* batch_best_i = nullptr;
     std::vector<int> batch_key;
+    int batch_ctx = 0;  // mean cache position of the sessions the batch graphs are recorded for
     cudaGraphExec_t g_batch1 = nullptr, g_batchn = nullptr;
     float* batch_logits = nullptr;  // [rows][vocab] of the last batched step, when requested
     float* batch_logits_buf = nullptr;  // its allocation, kept across disable / enable
@@ -372,16 +373,22 @@ int g_n_sm_cache = 0;
 // Launches the GEMM over activations `x` ([rows_alloc, k] fp16) with a TMA map built for the
 // chosen tile height.  FMT_F16: the weights are the row-major fp16 matrix w16 (dequantised by
 // dequant_q4s_f16_kernel), brought in by TMA as well.
+// one_tile: every activation row in one tile (MH = 1, BN = all B rows, at most 128), so that each
+// weight tile is dequantised by exactly one CTA (the batched decode GEMMs, which read the weights
+// once; the tile search below would trade that for fewer MMA columns).
 template <int EPI, int FMT = FMT_Q4S>
 cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaStream_t s, const __half* w16 = nullptr,
-                           int ksplit = 1, bool pdl = false, int max_stages = 8) {
-    if (p.n_rows % TC_BM || p.k % TC_BK || p.m_tok < 1 || p.m_tok > rows_alloc) return cudaErrorInvalidValue;
+                           int ksplit = 1, bool pdl = false, int max_stages = 8, bool one_tile = false) {
+    // rows_alloc: rows of the activation buffer x (B rows: 2 per token with p.hilo)
+    const int b_rows = p.hilo ? 2 * p.m_tok : p.m_tok;
+    if (p.n_rows % TC_BM || p.k % TC_BK || p.m_tok < 1 || b_rows > rows_alloc) return cudaErrorInvalidValue;
     if (!g_n_sm_cache) {
         int dev = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&g_n_sm_cache, cudaDevAttrMultiProcessorCount, dev);
     }
-    const TcTile t = choose_tc_tile(p.n_rows, p.m_tok, g_n_sm_cache, EPI != TC_ARGMAX);
+    const TcTile t = (one_tile && b_rows <= 128) ? TcTile{1, (b_rows + 15) / 16 * 16}
+                                                 : choose_tc_tile(p.n_rows, b_rows, g_n_sm_cache, EPI != TC_ARGMAX);
     p.bn = t.bn;
     CUtensorMap map, wmap;
     if (!make_act_map(&map, x, rows_alloc, p.k, t.bn)) return cudaErrorInvalidValue;
@@ -392,7 +399,7 @@ cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaSt
     }
     cudaLaunchConfig_t cfg = {};
     if (ksplit > 1 && (EPI != TC_STORE || ksplit > p.k / TC_BK)) return cudaErrorInvalidValue;
-    cfg.gridDim = dim3((p.m_tok + t.bn - 1) / t.bn, p.n_rows / (TC_BM * t.mh), ksplit);
+    cfg.gridDim = dim3((b_rows + t.bn - 1) / t.bn, p.n_rows / (TC_BM * t.mh), ksplit);
     cfg.blockDim = dim3(TC_THREADS);
     p.max_stages = max_stages;
     cfg.dynamicSmemBytes =
@@ -431,26 +438,33 @@ constexpr int SPLITK_MAX_ROWS = 128;  // split K only for batches of up to this 
 template <int EPI>
 cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmParams p, cudaStream_t s,
                        const float* norm_w = nullptr, __half* norm_out = nullptr, int* parts_out = nullptr) {
-    const TcTile t = choose_tc_tile(p.n_rows, p.m_tok, e->n_sm, true);
-    const int tiles = (p.n_rows / (TC_BM * t.mh)) * ((p.m_tok + t.bn - 1) / t.bn);
+    // the batched step's activations are fp16 hi / lo row pairs (2 max_pass rows per buffer);
+    // its SwiGLU output (the down GEMM's input) and the norms after the residual GEMMs are too
+    p.hilo = 1;
+    if (EPI == TC_SWIGLU) p.hilo_out = 1;
+    const int rows = 2 * e->cfg.max_pass;
+    const TcTile t = 2 * p.m_tok <= 128 ? TcTile{1, (2 * p.m_tok + 15) / 16 * 16}
+                                        : choose_tc_tile(p.n_rows, 2 * p.m_tok, e->n_sm, true);
+    const int tiles = (p.n_rows / (TC_BM * t.mh)) * ((2 * p.m_tok + t.bn - 1) / t.bn);
     int ks = std::min(SPLITK_MAX, e->n_sm / std::max(tiles, 1));
     ks = std::min(ks, p.k / TC_BK / 4);  // at least four k-blocks per slice
     auto run = [&](auto epi_tag, const TcGemmParams& q, int ksplit) -> cudaError_t {
         constexpr int E = decltype(epi_tag)::value;
         if (m.fmt == FMT_F16)
-            return launch_tc_gemm<E, FMT_F16>(x, e->cfg.max_pass, q, s, reinterpret_cast<const __half*>(m.dev), ksplit,
-                                              true, 3);
-        if (m.fmt == FMT_Q8) return launch_tc_gemm<E, FMT_Q8>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, 3);
-        if (m.fmt == FMT_Q4A) return launch_tc_gemm<E, FMT_Q4A>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, BATCH_STAGES_4BIT);
-        return launch_tc_gemm<E, FMT_Q4S>(x, e->cfg.max_pass, q, s, nullptr, ksplit, true, BATCH_STAGES_4BIT);
+            return launch_tc_gemm<E, FMT_F16>(x, rows, q, s, reinterpret_cast<const __half*>(m.dev), ksplit, true, 3,
+                                              true);
+        if (m.fmt == FMT_Q8) return launch_tc_gemm<E, FMT_Q8>(x, rows, q, s, nullptr, ksplit, true, 3, true);
+        if (m.fmt == FMT_Q4A)
+            return launch_tc_gemm<E, FMT_Q4A>(x, rows, q, s, nullptr, ksplit, true, BATCH_STAGES_4BIT, true);
+        return launch_tc_gemm<E, FMT_Q4S>(x, rows, q, s, nullptr, ksplit, true, BATCH_STAGES_4BIT, true);
     };
     if (parts_out) *parts_out = 1;
     cudaError_t err;
     if (ks < 2 || p.m_tok > SPLITK_MAX_ROWS) {
         if ((err = run(std::integral_constant<int, EPI>{}, p, 1)) != cudaSuccess) return err;
         if (EPI == TC_RESID && norm_w)
-            return launch(rmsnorm_rows_f16_kernel, p.m_tok, 256, 0, s, true, (const float*)p.out, norm_w, p.m_tok,
-                          norm_out);
+            return launch(rmsnorm_rows_f16_kernel<true>, p.m_tok, 256, 0, s, true, (const float*)p.out, norm_w,
+                          p.m_tok, norm_out);
         return cudaSuccess;
     }
     TcGemmParams q = p;
@@ -464,14 +478,15 @@ cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmPar
     }
     if (EPI == TC_RESID && norm_w && p.n_rows == H)
         return launch(splitk_resid_norm_kernel, p.m_tok, 256, 0, s, true, (const float*)e->splitk_part, ks, p.m_tok,
-                      p.out, norm_w, norm_out);
+                      p.out, norm_w, norm_out, 1);
     const long long total = (long long)p.m_tok * p.n_rows;
     const int grid = (int)std::min<long long>((total + 255) / 256, 4LL * e->n_sm);
     if ((err = launch(splitk_finish_kernel<EPI>, grid, 256, 0, s, true, (const float*)e->splitk_part, ks, p.m_tok,
-                      p.n_rows, p.out, p.out_h)) != cudaSuccess)
+                      p.n_rows, p.out, p.out_h, p.hilo_out)) != cudaSuccess)
         return err;
     if (EPI == TC_RESID && norm_w)
-        return launch(rmsnorm_rows_f16_kernel, p.m_tok, 256, 0, s, true, (const float*)p.out, norm_w, p.m_tok, norm_out);
+        return launch(rmsnorm_rows_f16_kernel<true>, p.m_tok, 256, 0, s, true, (const float*)p.out, norm_w, p.m_tok,
+                      norm_out);
     return cudaSuccess;
 }
 
@@ -1248,7 +1263,7 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
             w16[2] = reinterpret_cast<const __half*>(ly.gu.dev);
             w16[3] = reinterpret_cast<const __half*>(ly.d.dev);
         }
-        if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
+        if ((err = launch(rmsnorm_rows_f16_kernel<false>, n_rows, 256, 0, st, false, (const float*)e->px,
                           (const float*)ly.attn_norm, n_rows, e->pxn)) != cudaSuccess)
             return err;
         TcGemmParams p = tc_params(ly.qkv, n_rows, errp);
@@ -1269,7 +1284,7 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
         if ((err = gemm_ready()) != cudaSuccess) return err;
         if ((err = launch_tc_gemm<TC_RESID, FMT_F16>(e->pattn, e->cfg.max_pass, p, st, w16[1])) != cudaSuccess) return err;
         if ((err = gemm_issued()) != cudaSuccess) return err;
-        if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, false, (const float*)e->px,
+        if ((err = launch(rmsnorm_rows_f16_kernel<false>, n_rows, 256, 0, st, false, (const float*)e->px,
                           (const float*)ly.mlp_norm, n_rows, e->pxn)) != cudaSuccess)
             return err;
         p = tc_params(ly.gu, n_rows, errp);
@@ -1307,7 +1322,7 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
     const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
     // the RMSNorm before each projection runs in the finish of the GEMM that updated the residual
     // (o-proj, down), so only layer 0's input norm is a launch of its own
-    if ((err = launch(rmsnorm_rows_f16_kernel, n_rows, 256, 0, st, true, (const float*)e->px,
+    if ((err = launch(rmsnorm_rows_f16_kernel<true>, n_rows, 256, 0, st, true, (const float*)e->px,
                       (const float*)e->layers[0].attn_norm, n_rows, e->pxn)) != cudaSuccess)
         return err;
     for (int l = 0; l < L; ++l) {
@@ -1332,16 +1347,29 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
             a.vc = reinterpret_cast<KVT*>(e->vc_all) + kv_layer * l;
             a.sess_kv_elems = (long long)e->kv_elems;
             a.max_ctx = e->cfg.max_context;
-            // one cluster per (row, kv head): one part, normalised in place.  The cluster size is
-            // the smallest that gives about six waves of CTAs (short tail), up to the decode's.
+            // one cluster per (row, kv head): one part, normalised in place.  Cluster size cl splits
+            // each row's context over cl CTAs; the choice minimises waves x (streaming time of a
+            // CTA + its fixed cost): ceil(rows x 8 x cl / SMs) x (T / cl + O), T = one (row, head)'s
+            // cache at the HBM share of an SM (ctx x 512 B / 43 GB/s), O = 5 us of q/k/v staging
+            // and combines (measured: at 64 rows and 2K context, cl = 1 beats 2 by 4%, 4 by 22%).
+            const double T_us = (double)std::max(e->batch_ctx, 1) * 512.0 / 43.0e3, O_us = 5.0;
             int cl = 1;
-            while (cl < e->att_cluster && n_rows * NKV * cl < 6 * e->n_sm) cl *= 2;
+            double best = 1e30;
+            for (int c = 1; c <= e->att_cluster; c *= 2) {
+                const double waves = std::ceil((double)n_rows * NKV * c / e->n_sm);
+                const double cost = waves * (T_us / c + O_us);
+                if (cost < best - 1e-9) {
+                    best = cost;
+                    cl = c;
+                }
+            }
             a.n_split = cl;
             a.cluster = cl;
             a.part = e->att_part;
             a.st = e->st_all;
             a.rows_sess = e->batch_rows;
             a.out16 = e->pattn;
+            a.out16_hilo = 1;
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(NKV * a.n_split, n_rows);
             cfg.blockDim = dim3(256);
@@ -1379,11 +1407,13 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
     // the GEMV head does
     p.out = e->batch_logits ? e->batch_logits : (e->embed.fmt == FMT_F16 && n_rows == 1 ? e->logits : nullptr);
     p.ldo = e->cfg.vocab;
-    err = e->embed.fmt == FMT_Q4A ? launch_tc_gemm<TC_ARGMAX, FMT_Q4A>(e->pxn, e->cfg.max_pass, p, st, nullptr, 1, true)
-        : e->embed.fmt == FMT_F16 ? launch_tc_gemm<TC_ARGMAX, FMT_F16>(e->pxn, e->cfg.max_pass, p, st,
+    p.hilo = 1;  // the final norm's hi / lo rows
+    const int rows = 2 * e->cfg.max_pass;
+    err = e->embed.fmt == FMT_Q4A ? launch_tc_gemm<TC_ARGMAX, FMT_Q4A>(e->pxn, rows, p, st, nullptr, 1, true)
+        : e->embed.fmt == FMT_F16 ? launch_tc_gemm<TC_ARGMAX, FMT_F16>(e->pxn, rows, p, st,
                                                                        reinterpret_cast<const __half*>(e->embed.dev), 1,
                                                                        true)
-                                  : launch_tc_gemm<TC_ARGMAX, FMT_Q8>(e->pxn, e->cfg.max_pass, p, st, nullptr, 1, true);
+                                  : launch_tc_gemm<TC_ARGMAX, FMT_Q8>(e->pxn, rows, p, st, nullptr, 1, true);
     if (err != cudaSuccess) return err;
     return launch(batch_commit_kernel, n_rows, 256, 0, st, true, (const float*)e->batch_best_v,
                   (const int*)e->batch_best_i, e->cfg.vocab / TC_BM, n_rows, (const int*)e->batch_rows, e->st_all,
@@ -1534,9 +1564,10 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
         eng->pvt_stride = (cfg->max_context + 63) / 64 * 64 + 64;
         TRY(dalloc(eng, &eng->pvt, (size_t)NKV * HD * eng->pvt_stride * 2));
         cudaMemsetAsync(eng->pvt, 0, (size_t)NKV * HD * eng->pvt_stride * 2, eng->stream);  // slots past a call stay finite
-        TRY(dalloc_t(eng, &eng->pxn, P * H));
-        TRY(dalloc_t(eng, &eng->pattn, P * H));
-        TRY(dalloc_t(eng, &eng->ph, P * FF));
+        // 2 P rows: the batched step stores each token's GEMM input as an fp16 hi / lo row pair
+        TRY(dalloc_t(eng, &eng->pxn, 2 * P * H));
+        TRY(dalloc_t(eng, &eng->pattn, 2 * P * H));
+        TRY(dalloc_t(eng, &eng->ph, 2 * P * FF));
         TRY(dalloc_t(eng, &eng->gemm_err, 1));
         TRY(dalloc_t(eng, &eng->splitk_part, (size_t)SPLITK_MAX * SPLITK_MAX_ROWS * GU_ROWS));
         for (int set = 0; set < 2; ++set) {
@@ -1550,9 +1581,9 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
             cudaEventCreateWithFlags(&eng->ev_done[i], cudaEventDisableTiming);
         }
         cudaStreamCreateWithFlags(&eng->side, cudaStreamNonBlocking);
-        cudaMemsetAsync(eng->ph, 0, P * FF * sizeof(__half), eng->stream);
-        cudaMemsetAsync(eng->pxn, 0, P * H * sizeof(__half), eng->stream);
-        cudaMemsetAsync(eng->pattn, 0, P * H * sizeof(__half), eng->stream);
+        cudaMemsetAsync(eng->ph, 0, 2 * P * FF * sizeof(__half), eng->stream);
+        cudaMemsetAsync(eng->pxn, 0, 2 * P * H * sizeof(__half), eng->stream);
+        cudaMemsetAsync(eng->pattn, 0, 2 * P * H * sizeof(__half), eng->stream);
         cudaMemsetAsync(eng->gemm_err, 0, sizeof(int), eng->stream);
         CUtensorMap probe;
         if (!make_act_map(&probe, eng->pxn, (int)P, H, 16))
@@ -2239,6 +2270,9 @@ static icua_status decode_batch_impl(icua_engine* eng, const int32_t* sessions, 
     if ((s = ensure_tc_order(eng)) != ICUA_OK) return s;
     if (key != eng->batch_key) {
         drop_batch_graphs(eng);
+        long long ctx_sum = 0;
+        for (int i = 0; i < n_sessions; ++i) ctx_sum += get_session(eng, key[i])->pos;
+        eng->batch_ctx = (int)(ctx_sum / n_sessions);
         CK(cudaMemcpy(eng->batch_rows, key.data(), (size_t)n_sessions * 4, cudaMemcpyHostToDevice));
         if (eng->batch_logits_rows > 0 && eng->batch_logits_rows < n_sessions)
             return fail(eng, ICUA_ERR_CAPACITY, "batch logits capture holds %d rows", eng->batch_logits_rows);

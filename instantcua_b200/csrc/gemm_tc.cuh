@@ -68,7 +68,50 @@ struct TcGemmParams {
                                //   weights are requested before griddepcontrol.wait (else only the
                                //   first, so that the first activation tile is not queued behind S
                                //   weight tiles)
+    int hilo;                  // activations as fp16 hi / lo row pairs (rows 2t, 2t + 1 of token
+                               //   t: x = hi + lo to ~22 bits): B has 2 m_tok rows, the epilogue
+                               //   adds the pair's accumulator columns (batched decode)
+    int hilo_out;              // TC_SWIGLU: out_h written as hi / lo row pairs as well
 };
+
+// Stores the normalised fp16 values of row i for thread tid's eight elements (4 tid .. 4 tid + 3
+// and 1024 + 4 tid ..): out[i] or, hilo, the fp16 hi / lo rows 2i and 2i + 1 (hi + lo = the fp32
+// value to ~22 bits, the batched decode GEMMs' input).
+__device__ __forceinline__ void store_norm_row(__half* out, int i, int tid, float4 a, float4 b, float r, float4 wa,
+                                               float4 wb, bool hilo) {
+    const float y[8] = {a.x * r * wa.x, a.y * r * wa.y, a.z * r * wa.z, a.w * r * wa.w,
+                        b.x * r * wb.x, b.y * r * wb.y, b.z * r * wb.z, b.w * r * wb.w};
+    if (!hilo) {
+        __half2* o = reinterpret_cast<__half2*>(out + (size_t)i * H);
+        o[2 * tid] = __floats2half2_rn(y[0], y[1]);
+        o[2 * tid + 1] = __floats2half2_rn(y[2], y[3]);
+        o[2 * (tid + 256)] = __floats2half2_rn(y[4], y[5]);
+        o[2 * (tid + 256) + 1] = __floats2half2_rn(y[6], y[7]);
+        return;
+    }
+    __half hi[8], lo[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        hi[e] = __float2half_rn(y[e]);
+        lo[e] = __float2half_rn(y[e] - __half2float(hi[e]));
+    }
+    __half2* oh = reinterpret_cast<__half2*>(out + (size_t)(2 * i) * H);
+    __half2* ol = reinterpret_cast<__half2*>(out + (size_t)(2 * i + 1) * H);
+    oh[2 * tid] = __halves2half2(hi[0], hi[1]);
+    oh[2 * tid + 1] = __halves2half2(hi[2], hi[3]);
+    oh[2 * (tid + 256)] = __halves2half2(hi[4], hi[5]);
+    oh[2 * (tid + 256) + 1] = __halves2half2(hi[6], hi[7]);
+    ol[2 * tid] = __halves2half2(lo[0], lo[1]);
+    ol[2 * tid + 1] = __halves2half2(lo[2], lo[3]);
+    ol[2 * (tid + 256)] = __halves2half2(lo[4], lo[5]);
+    ol[2 * (tid + 256) + 1] = __halves2half2(lo[6], lo[7]);
+}
+
+// fp16 hi / lo pair of x: hi = fp16(x), lo = fp16(x - hi).
+__device__ __forceinline__ void split_hilo(float x, __half& hi, __half& lo) {
+    hi = __float2half_rn(x);
+    lo = __float2half_rn(x - __half2float(hi));
+}
 
 // Epilogue activations on the hardware approximations (tanh.approx, ex2.approx through __expf,
 // __fdividef): their outputs are rounded to fp16 right after, well above the approximation error.
@@ -661,16 +704,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             const int h = MH == 2 ? wg : 0;
             const int row = row0 + h * TC_BM + q * 32 + lane;
             const int cstep = MH == 2 ? 1 : 2;
+            const int HL = p.hilo ? 2 : 1;  // accumulator columns per token
 #pragma unroll 1
             for (int c = (MH == 2 ? 0 : wg); c * 32 < BN; c += cstep) {
-                if (tok0 + c * 32 >= p.m_tok) break;
+                if (tok0 + c * 32 >= p.m_tok * HL) break;
                 float v[32];
                 const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * half_cols + c * 32);
-                const int ncol = min(32, BN - c * 32);  // 32 or 16
-                if (ncol == 32)
+                const int ncol_b = min(32, BN - c * 32);  // 32 or 16 accumulator columns
+                if (ncol_b == 32)
                     tmem_ld32(taddr, v);
                 else
                     tmem_ld16(taddr, v);
+                if (p.hilo) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = v[2 * j] + v[2 * j + 1];
+                }
+                // from here on: tokens ctok .. ctok + ncol - 1 of the chunk in v[0 .. ncol - 1]
+                const int ctok = (tok0 + c * 32) / HL, ncol = ncol_b / HL;
                 if (FMT == FMT_F16 && p.bias != nullptr) {
                     const float b = p.bias[row];
 #pragma unroll
@@ -678,7 +728,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 }
                 if (EPI == TC_GELU) {
                     // one weight row per thread, 32 tokens: fp16 stores strided by ldh
-                    const int nj = min(ncol, p.m_tok - (tok0 + c * 32));
+                    const int nj = min(ncol, p.m_tok - ctok);
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         if (j < nj) {
@@ -686,7 +736,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                             const float g = p.gelu_erf ? 0.5f * x * (1.0f + erff(x * 0.70710678118654752f))
                                                        : 0.5f * x * (1.0f + tanh_approx(0.79788456080286536f *
                                                                                   (x + 0.044715f * x * x * x)));
-                            p.out_h[(size_t)(tok0 + c * 32 + j) * p.ldh + row] = __float2half_rn(g);
+                            p.out_h[(size_t)(ctok + j) * p.ldh + row] = __float2half_rn(g);
                         }
                     }
                     continue;
@@ -695,14 +745,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                     // residual rows: the chunk's loads first (independent, in flight together),
                     // then the adds and stores; DeepStack rows (three layers of a visual prefill)
                     // are added after the residual, as the reference does
-                    const int nj = min(ncol, p.m_tok - (tok0 + c * 32));
+                    const int nj = min(ncol, p.m_tok - ctok);
                     float old[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
-                        old[j] = j < nj ? p.out[(size_t)(tok0 + c * 32 + j) * p.ldo + row] : 0.f;
+                        old[j] = j < nj ? p.out[(size_t)(ctok + j) * p.ldo + row] : 0.f;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
-                        const int tok = tok0 + c * 32 + j;
+                        const int tok = ctok + j;
                         if (j < nj) {
                             float nv = old[j] + v[j];
                             if (p.deepstack != nullptr && tok >= p.ds_row0 && tok < p.ds_row0 + p.ds_rows)
@@ -714,7 +764,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 }
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const int tok = tok0 + c * 32 + j;
+                    const int tok = ctok + j;
                     if (j >= ncol || tok >= p.m_tok) break;
                     if (EPI == TC_STORE) {
                         p.out[blockIdx.z * p.out_zstride + (size_t)tok * p.ldo + row] = v[j];
@@ -725,7 +775,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                         warp_argmax(bv, bi);
                         if (lane == 0) {
                             float2* red = reinterpret_cast<float2*>(smem + SM.red_off);
-                            red[(h * 4 + q) * BN + c * 32 + j] = make_float2(bv, __int_as_float(bi));
+                            red[(h * 4 + q) * BN + (c * 32) / HL + j] = make_float2(bv, __int_as_float(bi));
                         }
                     } else {
                         // rows of a 16-row tile: 0..7 gate j, 8..15 up j (tile * 8 + r)
@@ -733,7 +783,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                         if (!(lane & 8)) {
                             const float gv = v[j];
                             const float hv = silu_fast(gv) * u;
-                            p.out_h[(size_t)tok * p.ldh + (row >> 4) * 8 + (lane & 7)] = __float2half_rn(hv);
+                            const size_t col = (size_t)(row >> 4) * 8 + (lane & 7);
+                            if (p.hilo_out) {
+                                __half hi, lo;
+                                split_hilo(hv, hi, lo);
+                                p.out_h[(size_t)(2 * tok) * p.ldh + col] = hi;
+                                p.out_h[(size_t)(2 * tok + 1) * p.ldh + col] = lo;
+                            } else {
+                                p.out_h[(size_t)tok * p.ldh + col] = __float2half_rn(hv);
+                            }
                         }
                     }
                 }
@@ -745,15 +803,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     if (EPI == TC_ARGMAX) {
         // combine the 4 x MH row quarters of this tile per token (lower row on ties)
         const float2* red = reinterpret_cast<const float2*>(smem + SM.red_off);
-        for (int t = threadIdx.x; t < BN && tok0 + t < p.m_tok; t += blockDim.x) {
+        const int HL = p.hilo ? 2 : 1, ttok0 = tok0 / HL;
+        for (int t = threadIdx.x; t < BN / HL && ttok0 + t < p.m_tok; t += blockDim.x) {
             float bv = -INFINITY;
             int bi = 0x7fffffff;
             for (int q = 0; q < 4 * MH; ++q) {
                 const float2 e = red[q * BN + t];
                 argmax_merge(bv, bi, e.x, __float_as_int(e.y));
             }
-            p.best_v[(size_t)rtile * p.m_tok + tok0 + t] = bv;
-            p.best_i[(size_t)rtile * p.m_tok + tok0 + t] = bi;
+            p.best_v[(size_t)rtile * p.m_tok + ttok0 + t] = bv;
+            p.best_i[(size_t)rtile * p.m_tok + ttok0 + t] = bi;
         }
     }
     if (warp == 1) {
@@ -863,7 +922,7 @@ __global__ void tc_order_kernel(const uint8_t* src, int fmt, int n_tiles, int up
 // rows 8..15 of each 16-row tile) into fp16.
 template <int EPI>
 __global__ void __launch_bounds__(256) splitk_finish_kernel(const float* part, int Z, int m, int n, float* out,
-                                                            __half* out_h) {
+                                                            __half* out_h, int hilo_out) {
     pdl_wait();
     pdl_launch_dependents();
     const long long total = (long long)m * n;
@@ -885,7 +944,16 @@ __global__ void __launch_bounds__(256) splitk_finish_kernel(const float* part, i
                 float up = part[i + 8];
                 for (int z = 1; z < Z; ++z) up += part[(long long)z * total + i + 8];
                 const long long tok = i / n;
-                out_h[tok * (n / 2) + (row >> 4) * 8 + r] = __float2half_rn((acc / (1.0f + expf(-acc))) * up);
+                const float hv = (acc / (1.0f + expf(-acc))) * up;
+                const long long col = (row >> 4) * 8 + r;
+                if (hilo_out) {
+                    __half hi, lo;
+                    split_hilo(hv, hi, lo);
+                    out_h[(2 * tok) * (n / 2) + col] = hi;
+                    out_h[(2 * tok + 1) * (n / 2) + col] = lo;
+                } else {
+                    out_h[tok * (n / 2) + col] = __float2half_rn(hv);
+                }
             }
         }
     }
@@ -897,7 +965,7 @@ __global__ void __launch_bounds__(256) splitk_finish_kernel(const float* part, i
 // rmsnorm_rows_f16_kernel (same element mapping and reduction order), so that the pair of kernels
 // it replaces and this one give the same bits.
 __global__ void __launch_bounds__(256) splitk_resid_norm_kernel(const float* part, int Z, int m, float* x,
-                                                                const float* w, __half* out) {
+                                                                const float* w, __half* out, int hilo) {
     __shared__ float red[8];
     pdl_wait();
     pdl_launch_dependents();
@@ -945,11 +1013,7 @@ __global__ void __launch_bounds__(256) splitk_resid_norm_kernel(const float* par
     for (int w2 = 0; w2 < 8; ++w2) tot += red[w2];
     const float r = 1.0f / sqrtf(tot / (float)H + EPS);
     const float4 wa = reinterpret_cast<const float4*>(w)[tid], wb = reinterpret_cast<const float4*>(w)[tid + 256];
-    __half2* o = reinterpret_cast<__half2*>(out + (size_t)i * H);
-    o[2 * tid] = __floats2half2_rn(a.x * r * wa.x, a.y * r * wa.y);
-    o[2 * tid + 1] = __floats2half2_rn(a.z * r * wa.z, a.w * r * wa.w);
-    o[2 * (tid + 256)] = __floats2half2_rn(b.x * r * wb.x, b.y * r * wb.y);
-    o[2 * (tid + 256) + 1] = __floats2half2_rn(b.z * r * wb.z, b.w * r * wb.w);
+    store_norm_row(out, i, tid, a, b, r, wa, wb, hilo != 0);
 }
 
 }  // namespace icua

@@ -9,6 +9,7 @@
 #pragma once
 #include "attn_decode.cuh"
 #include "common.cuh"
+#include "gemm_tc.cuh"
 #include "gemv.cuh"
 
 namespace icua {
@@ -32,6 +33,8 @@ __global__ void prefill_embed_kernel(const int* prompt, int n, int vis_off, int 
 
 // out[i] = fp16(x[i] * rsqrt(mean(x[i]^2) + eps) * w): the fp16 GEMM input of a prompt row.
 // One CTA of 256 threads per row of 2048.
+// hilo: the output rows are fp16 hi / lo pairs (store_norm_row).
+template <bool HILO = false>
 __global__ void __launch_bounds__(256) rmsnorm_rows_f16_kernel(const float* x, const float* w, int n, __half* out) {
     __shared__ float red[8];
     pdl_wait();
@@ -56,11 +59,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_f16_kernel(const float* x, c
     for (int w2 = 0; w2 < 8; ++w2) tot += red[w2];
     const float r = 1.0f / sqrtf(tot / (float)H + EPS);
     const float4 wa = reinterpret_cast<const float4*>(w)[tid], wb = reinterpret_cast<const float4*>(w)[tid + 256];
-    __half2* o = reinterpret_cast<__half2*>(out + (size_t)i * H);
-    o[2 * tid] = __floats2half2_rn(a.x * r * wa.x, a.y * r * wa.y);
-    o[2 * tid + 1] = __floats2half2_rn(a.z * r * wa.z, a.w * r * wa.w);
-    o[2 * (tid + 256)] = __floats2half2_rn(b.x * r * wb.x, b.y * r * wb.y);
-    o[2 * (tid + 256) + 1] = __floats2half2_rn(b.z * r * wb.z, b.w * r * wb.w);
+    store_norm_row(out, i, tid, a, b, r, wa, wb, HILO);
 }
 
 // Per prompt row: RMSNorm(128) of the 16 q and 8 k heads, rotate-half RoPE from the cache slot's

@@ -42,7 +42,7 @@ def prompts(n, seed=5):
 def test_batch_matches_one_at_a_time(tensors, kv, n):
     """Teacher-forced: every step both paths get the same input token per session (the batch-1
     path's choice), so the per-row logits are compared on identical contexts.  4 rows run the
-    attention in clusters of 4 CTAs per (row, head), 56 rows in clusters of 2."""
+    attention split over a cluster of CTAs per (row, head), 56 rows one CTA per (row, head)."""
     steps = 4
     ps = prompts(n)
     order = [int(v) for v in np.random.default_rng(n).permutation(n)]  # batch rows in a shuffled order
