@@ -1018,9 +1018,10 @@ icua_status ensure_tc_order(icua_engine* eng) {
         if ((s = dalloc(eng, reinterpret_cast<void**>(&m->tc), bytes)) != ICUA_OK) return s;
         const long long nv = (long long)bytes / 16;
         const int grid = (int)std::min<long long>((nv + 255) / 256, 4096);
+        // row order: each dequantising thread takes 32 consecutive columns of one row
         if (m->fmt == FMT_Q8)
-            tc_order_kernel<<<grid, 256, 0, eng->stream>>>(m->dev, m->fmt, m->n_rows / 16, m->k / 64, m->tc);
-        else  // 4-bit formats: row order, 16-byte stores in the GEMM's dequantisation
+            tc_order_rows_q8_kernel<<<grid, 256, 0, eng->stream>>>(m->dev, m->n_rows / 16, m->k / 64, m->tc);
+        else
             tc_order_rows_kernel<<<grid, 256, 0, eng->stream>>>(m->dev, m->fmt, m->n_rows / 16, m->k / 64, m->tc);
         CK(cudaGetLastError());
     }

@@ -44,9 +44,9 @@ enum TcEpi { TC_STORE = 0, TC_RESID = 1, TC_SWIGLU = 2, TC_ARGMAX = 3, TC_GELU =
 
 struct TcGemmParams {
     const uint8_t* w;          // weights in the device tile layout [n_rows, k] (q4s, q4a or q8)
-    const uint8_t* wtc;        // the same weights in tensor-core order (tc_order_kernel for q8,
-                               //   tc_order_rows_kernel for the 4-bit formats), or nullptr: then
-                               //   each stage gathers 8 x MH units from `w`
+    const uint8_t* wtc;        // the same weights in tensor-core row order (tc_order_rows_kernel,
+                               //   tc_order_rows_q8_kernel), or nullptr: then each stage gathers
+                               //   8 x MH units from `w`
     int n_rows, k, n_tiles, upt;
     int m_tok;                 // activation rows (tokens)
     int bn;                    // tokens per CTA tile (multiple of 16, <= 256; the TMA box height)
@@ -133,7 +133,7 @@ __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f 
 __host__ __device__ constexpr int tc_acc_cols(int bn) { return (bn + 31) & ~31; }
 __host__ __device__ constexpr int tc_tmem_a_slots(int bn) { return (256 - tc_acc_cols(bn)) / 32; }
 __host__ __device__ constexpr bool tc_a_in_tmem(int fmt, bool row_order, int mh, int bn) {
-    return (fmt == 2 || fmt == 3) && row_order && mh == 1 && bn <= 128;  // FMT_Q4A, FMT_Q4S
+    return (fmt == 1 || fmt == 2 || fmt == 3) && row_order && mh == 1 && bn <= 128;  // FMT_Q8, FMT_Q4A, FMT_Q4S
 }
 
 struct TcLayout {
@@ -428,11 +428,65 @@ __global__ void tc_order_rows_kernel(const uint8_t* src, int fmt, int n_tiles, i
     }
 }
 
-// Dequantises half of one row of a row-order block: row r, columns 32 half .. +31 (one q4s scale
+// Row order of q8 (the tied embedding / lm_head of the batched step): the same blocks of 128 rows x
+// 64 columns (8,704 bytes, as 8 q8 units) with row r's 64 code bytes in column order at r * 64 and
+// its two 32-column group scales at 8192 + r * 4.  One thread per 16 code bytes and per row's scales.
+constexpr int TC_ROWS_BLOCK_Q8 = 8704;
+__global__ void tc_order_rows_q8_kernel(const uint8_t* src, int n_tiles, int upt, uint8_t* dst) {
+    const long long blocks = (long long)(n_tiles / 8) * upt;
+    const long long chunks = blocks * 128 * 4, total = chunks + blocks * 128;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const bool is_chunk = i < chunks;
+        const long long e = is_chunk ? i : i - chunks;
+        const long long b = is_chunk ? e >> 9 : e >> 7;  // block index: (g8 * upt + kk)
+        const int r = is_chunk ? (int)((e >> 2) & 127) : (int)(e & 127);
+        const int g8 = (int)(b / upt), kk = (int)(b % upt);
+        const int tile = g8 * 8 + (r >> 4), rt = r & 15, gq = rt & 7, up = rt >> 3;
+        const uint8_t* ub = src + icua_layout::unit_offset(FMT_Q8, n_tiles, upt, tile, kk);
+        uint8_t* blk = dst + b * TC_ROWS_BLOCK_Q8;
+        if (is_chunk) {
+            const int j = (int)(e & 3);
+            uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {  // column 16 j + c of the unit
+                const int kin = 16 * j + c, step = kin >> 4, k16 = kin & 15;
+                const int t = (k16 & 7) >> 1, odd = k16 & 1, hi8 = k16 >> 3;
+                const uint8_t* wp = ub + (step >> 1) * 512 + (gq * 4 + t) * 16 + ((step & 1) * 2 + hi8) * 4;
+                w[c >> 2] |= (uint32_t)wp[odd * 2 + up] << ((c & 3) * 8);
+            }
+            *reinterpret_cast<uint4*>(blk + r * 64 + j * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        } else {
+            const uint16_t v0 = *reinterpret_cast<const uint16_t*>(ub + 1024 + gq * 8 + up * 2);
+            const uint16_t v1 = *reinterpret_cast<const uint16_t*>(ub + 1024 + gq * 8 + 4 + up * 2);
+            *reinterpret_cast<uint32_t*>(blk + 8192 + r * 4) = (uint32_t)v0 | ((uint32_t)v1 << 16);
+        }
+    }
+}
+
+// Dequantises half of one row of a row-order block: row r, columns 32 half .. +31 (one scale
 // group), as 16 fp16 pairs of consecutive columns, with the arithmetic of dequant_q4s_lane /
-// dequant_q4a_lane (bit-identical values).
+// dequant_q4a_lane / dequant_q8_lane (bit-identical values).
 template <int FMT>
 __device__ __forceinline__ void dequant_rows_regs(const uint8_t* blk, int r, int half, uint32_t (&h)[16]) {
+    if constexpr (FMT == FMT_Q8) {
+        // fp16(1024 + u) from the code byte, - 1152 = q exactly, then one rounding of q * scale
+        const uint4 b0 = *reinterpret_cast<const uint4*>(blk + r * 64 + half * 32);
+        const uint4 b1 = *reinterpret_cast<const uint4*>(blk + r * 64 + half * 32 + 16);
+        const uint32_t sv = *reinterpret_cast<const uint32_t*>(blk + 8192 + r * 4);
+        const __half s1 = __ushort_as_half((uint16_t)(half ? sv >> 16 : sv & 0xFFFFu));
+        const __half2 mul = __halves2half2(s1, s1);
+        const __half2 off = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+        const uint32_t w[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t lo = __byte_perm(w[k], 0x6464u, 0x5140), hi = __byte_perm(w[k], 0x6464u, 0x5342);
+            __half2 x0 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&lo), off), mul);
+            __half2 x1 = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&hi), off), mul);
+            h[2 * k] = *reinterpret_cast<uint32_t*>(&x0);
+            h[2 * k + 1] = *reinterpret_cast<uint32_t*>(&x1);
+        }
+        return;
+    }
     const uint4 nib = *reinterpret_cast<const uint4*>(blk + r * 32 + half * 16);
     const uint32_t sv = *reinterpret_cast<const uint32_t*>(blk + 4096 + r * 4);
     __half2 mul, add;
@@ -672,10 +726,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 if (lane == 0) mbar_arrive(&afull[s]);
                 continue;
             }
-            if (FMT != FMT_Q8 && p.wtc != nullptr) {
-                // row order (tc_order_rows_kernel): 16-byte stores of 8 consecutive columns
+            if (p.wtc != nullptr) {
+                // row order (tc_order_rows_kernel / tc_order_rows_q8_kernel): 16-byte stores of 8
+                // consecutive columns
 #pragma unroll
-                for (int i = 0; i < MH; ++i) dequant_rows_half<FMT>(raw + i * TC_ROWS_BLOCK, d, A, i * TC_BM);
+                for (int i = 0; i < MH; ++i) dequant_rows_half<FMT>(raw + i * 8 * UB, d, A, i * TC_BM);
             } else {
 #pragma unroll
                 for (int i = 0; i < MH; ++i) {
