@@ -368,6 +368,25 @@ TcTile choose_tc_tile(int n_rows, int m_tok, int n_sm, bool allow_mh2) {
     return best;
 }
 
+// Tile shape of a GEMM whose A tiles go to tensor memory (one accumulator of up to 256 columns):
+// each 64-column stage costs about the same up to 256 activation rows (the MMA-issuing thread, not
+// the tensor core, paces it), so the shape minimises waves x (max(bn, 128) + 64).
+TcTile choose_tc_tile_atm(int n_rows, int b_rows, int n_sm) {
+    TcTile best{1, 16};
+    double best_cost = 1e30;
+    const int bn_max = std::min(256, (b_rows + 15) / 16 * 16);
+    for (int bn = bn_max; bn >= 16; bn -= 16) {
+        const long tiles = (long)(n_rows / TC_BM) * ((b_rows + bn - 1) / bn);
+        const long waves = (tiles + n_sm - 1) / n_sm;
+        const double cost = (double)waves * (std::max(bn, 128) + 64);
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = TcTile{1, bn};
+        }
+    }
+    return best;
+}
+
 int g_n_sm_cache = 0;
 
 // Launches the GEMM over activations `x` ([rows_alloc, k] fp16) with a TMA map built for the
@@ -387,7 +406,9 @@ cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaSt
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&g_n_sm_cache, cudaDevAttrMultiProcessorCount, dev);
     }
+    const bool atm_ok = FMT != FMT_F16 && p.wtc != nullptr;  // row-order weights: A can go to TMEM
     const TcTile t = (one_tile && b_rows <= 128) ? TcTile{1, (b_rows + 15) / 16 * 16}
+                     : atm_ok                    ? choose_tc_tile_atm(p.n_rows, b_rows, g_n_sm_cache)
                                                  : choose_tc_tile(p.n_rows, b_rows, g_n_sm_cache, EPI != TC_ARGMAX);
     p.bn = t.bn;
     CUtensorMap map, wmap;

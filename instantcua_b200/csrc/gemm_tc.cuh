@@ -129,11 +129,15 @@ __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f 
 // with tcgen05.st into TMEM columns after the accumulator (lane = weight row, two fp16 of
 // consecutive k per 32-bit column), and the MMA reads it from there: the A tile never passes
 // through shared memory, whose bandwidth (A written by the CUDA cores and read by the tensor core
-// at 4 bytes per weight) bounded these GEMMs.  256 TMEM columns: the accumulator, then 32 per stage.
+// at 4 bytes per weight) bounded these GEMMs.  TMEM columns: the accumulator, then 32 per stage;
+// 256 columns up to 128 activation rows, all 512 above (one such CTA per SM).
 __host__ __device__ constexpr int tc_acc_cols(int bn) { return (bn + 31) & ~31; }
-__host__ __device__ constexpr int tc_tmem_a_slots(int bn) { return (256 - tc_acc_cols(bn)) / 32; }
+__host__ __device__ constexpr int tc_tmem_cols(int mh, int bn, bool a_tmem) {
+    return (mh == 2 || (a_tmem && bn > 128)) ? 512 : 256;
+}
+__host__ __device__ constexpr int tc_tmem_a_slots(int bn) { return (tc_tmem_cols(1, bn, true) - tc_acc_cols(bn)) / 32; }
 __host__ __device__ constexpr bool tc_a_in_tmem(int fmt, bool row_order, int mh, int bn) {
-    return (fmt == 1 || fmt == 2 || fmt == 3) && row_order && mh == 1 && bn <= 128;  // FMT_Q8, FMT_Q4A, FMT_Q4S
+    return (fmt == 1 || fmt == 2 || fmt == 3) && row_order && mh == 1 && bn <= 256;  // FMT_Q8, FMT_Q4A, FMT_Q4S
 }
 
 struct TcLayout {
@@ -562,7 +566,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     // CTAs that share a weight tile start at different k-blocks (rotation by the token-tile
     // index), so they do not all request the same rows from L2 at the same moment
     const int krot = (int)((blockIdx.x * 5u) % (unsigned)nk);
-    constexpr uint32_t tmem_cols = MH == 2 ? 512 : 256;
+    const uint32_t tmem_cols = (uint32_t)tc_tmem_cols(MH, BN, ATM);
     constexpr int half_cols = 256;  // column offset of the second accumulator
 
     if (threadIdx.x == 0) {
