@@ -423,8 +423,9 @@ cudaError_t launch_tc_gemm(const void* x, int rows_alloc, TcGemmParams p, cudaSt
     cfg.gridDim = dim3((b_rows + t.bn - 1) / t.bn, p.n_rows / (TC_BM * t.mh), ksplit);
     cfg.blockDim = dim3(TC_THREADS);
     p.max_stages = max_stages;
+    const bool atm = tc_a_in_tmem(FMT, p.wtc != nullptr, t.mh, t.bn);
     cfg.dynamicSmemBytes =
-        TcLayout(t.bn, t.mh, FMT, EPI == TC_ARGMAX, max_stages, tc_a_in_tmem(FMT, p.wtc != nullptr, t.mh, t.bn)).alloc;
+        TcLayout(t.bn, t.mh, FMT, EPI == TC_ARGMAX, max_stages, atm, tc_kb(atm, p.k / TC_BK, ksplit)).alloc;
     cfg.stream = s;
     // programmatic dependent launch: only where the weights are not the previous kernel's output
     // (engine matrices); the kernel waits for the previous kernel before its activation loads

@@ -139,6 +139,12 @@ __host__ __device__ constexpr int tc_tmem_a_slots(int bn) { return (tc_tmem_cols
 __host__ __device__ constexpr bool tc_a_in_tmem(int fmt, bool row_order, int mh, int bn) {
     return (fmt == 1 || fmt == 2 || fmt == 3) && row_order && mh == 1 && bn <= 256;  // FMT_Q8, FMT_Q4A, FMT_Q4S
 }
+// k-blocks per pipeline stage: two with the A tiles in tensor memory when every K slice has an even
+// number of them (the MMA-issuing thread, which paces these GEMMs, then waits, commits and loops
+// once per 128 columns), else one.
+__host__ __device__ constexpr int tc_kb(bool a_tmem, int nk_all, int ksplit) {
+    return (a_tmem && nk_all % (2 * ksplit) == 0) ? 2 : 1;
+}
 
 struct TcLayout {
     int S;                                   // pipeline stages
@@ -149,15 +155,17 @@ struct TcLayout {
     // (measured 2% faster per batched step than 4 to 7 stages, 6% faster than 2)
     // a_tmem: the dequantised A tiles live in tensor memory (tc_a_in_tmem), at most
     // tc_tmem_a_slots(bn) stages of them
-    __host__ __device__ TcLayout(int bn, int mh, int fmt, bool argmax, int max_stages = 8, bool a_tmem = false) {
+    // kb: k-blocks per stage (tc_kb); a stage holds kb activation tiles and kb quantised blocks
+    __host__ __device__ TcLayout(int bn, int mh, int fmt, bool argmax, int max_stages = 8, bool a_tmem = false,
+                                 int kb = 1) {
         a_bytes = a_tmem ? 0 : mh * TC_BM * 128;  // fp16 [mh * 128][64], swizzled
-        b_bytes = bn * 128;                  // fp16 [bn][64], swizzled by TMA
-        raw_bytes = mh * 8 * unit_bytes(fmt);
+        b_bytes = kb * bn * 128;             // kb x fp16 [bn][64], swizzled by TMA
+        raw_bytes = kb * mh * 8 * unit_bytes(fmt);
         stage_bytes = a_bytes + b_bytes + raw_bytes;
         const int red = argmax ? 4 * mh * bn * 8 : 0;
         S = (TC_SMEM_BUDGET - red - 1024 - 512) / stage_bytes;
         if (S > max_stages) S = max_stages;
-        if (a_tmem && S > tc_tmem_a_slots(bn)) S = tc_tmem_a_slots(bn);
+        if (a_tmem && S > tc_tmem_a_slots(bn) / kb) S = tc_tmem_a_slots(bn) / kb;
         a_off = 0;
         b_off = a_off + S * a_bytes;
         raw_off = b_off + S * b_bytes;
@@ -541,8 +549,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     constexpr int NU = 8 * MH;  // 16-row units per stage
     const int BN = p.bn;
     const bool ATM = tc_a_in_tmem(FMT, p.wtc != nullptr, MH, BN);  // A tiles in tensor memory
-    const TcLayout SM(BN, MH, FMT, EPI == TC_ARGMAX, p.max_stages, ATM);
+    const int KB = tc_kb(ATM, p.k / TC_BK, gridDim.z);           // k-blocks per stage
+    const TcLayout SM(BN, MH, FMT, EPI == TC_ARGMAX, p.max_stages, ATM, KB);
     const int S = SM.S;
+    const int b_tile = BN * 128;  // bytes of one activation tile (64 columns)
     const uint32_t a_col0 = (uint32_t)tc_acc_cols(BN);  // ATM: stage s's A tile at columns a_col0 + 32 s
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base_u = smem_u32(smem_raw);
@@ -562,7 +572,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     const int tok0 = blockIdx.x * BN;
     const int nk_all = p.k / TC_BK;
     const int kb0 = (int)((long long)nk_all * blockIdx.z / gridDim.z);
-    const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb0;
+    // stages of this K slice (KB k-blocks each)
+    const int nk = ((int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb0) / KB;
     // CTAs that share a weight tile start at different k-blocks (rotation by the token-tile
     // index), so they do not all request the same rows from L2 at the same moment
     const int krot = (int)((blockIdx.x * 5u) % (unsigned)nk);
@@ -601,7 +612,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             // requested ahead of griddepcontrol.wait
             auto issue_w = [&](int kc) {
                 const int s = kc % S;
-                const int kblk = kb0 + (kc + krot) % nk;
+                const int kblk = kb0 + KB * ((kc + krot) % nk);
                 if constexpr (FMT == FMT_F16) {
                     mbar_expect_tx(&bfull[s], (uint32_t)(SM.a_bytes + SM.b_bytes));
 #pragma unroll
@@ -610,13 +621,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                                     row0 + h * TC_BM, &bfull[s]);
                 } else {
                     uint8_t* raw = smem + SM.raw_off + s * SM.raw_bytes;
-                    mbar_expect_tx(&rawfull[s], NU * UB);
+                    mbar_expect_tx(&rawfull[s], KB * NU * UB);
                     if (p.wtc != nullptr) {
-                        // tensor-core tile order: the 8 units of a 128-row group are contiguous
+                        // tensor-core order: a 128-row block of a k-block is contiguous, and so are the
+                        // KB blocks of a stage (consecutive k-blocks of one row tile)
 #pragma unroll
                         for (int h = 0; h < MH; ++h)
-                            bulk_g2s(raw + h * 8 * UB, p.wtc + ((size_t)(rtile * MH + h) * p.upt + kblk) * 8 * UB, 8 * UB,
-                                     &rawfull[s]);
+                            bulk_g2s(raw + h * KB * 8 * UB, p.wtc + ((size_t)(rtile * MH + h) * p.upt + kblk) * 8 * UB,
+                                     KB * 8 * UB, &rawfull[s]);
                     } else {
 #pragma unroll 1
                         for (int t = 0; t < NU; ++t)
@@ -641,7 +653,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 // the MMA thread waits on one barrier per stage
                 uint64_t* xbar = ATM ? &afull[s] : &bfull[s];
                 if (FMT != FMT_F16) mbar_expect_tx(xbar, (uint32_t)SM.b_bytes);
-                tma_load_2d(smem + SM.b_off + s * SM.b_bytes, &xmap, (kb0 + (kc + krot) % nk) * TC_BK, tok0, xbar);
+                for (int kb = 0; kb < KB; ++kb)
+                    tma_load_2d(smem + SM.b_off + s * SM.b_bytes + kb * b_tile, &xmap,
+                                (kb0 + KB * ((kc + krot) % nk) + kb) * TC_BK, tok0, xbar);
             }
             // the copies of the last stages complete before the CTA may exit (at once on success);
             // after a failed wait at kc >= S the stages issued are [0, kc), all within this range
@@ -659,7 +673,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 // this thread paces the GEMM: one barrier per stage (A tile and activation tile),
                 // stage and phase as counters, the MMAs read the stage's A columns of TMEM
                 const uint64_t bd0 = umma_desc_sw128(smem_u32(smem + SM.b_off));
-                const uint32_t b_step = (uint32_t)SM.b_bytes >> 4;  // descriptor address units
+                const uint32_t b_step = (uint32_t)b_tile >> 4;  // one activation tile, descriptor units
                 int s = 0;
                 uint32_t ph = 0;
                 for (int kc = 0; kc < nk; ++kc) {
@@ -668,11 +682,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t bd = bd0 + (uint64_t)(b_step * (uint32_t)s);
-                    const uint32_t at = tmem + a_col0 + 32u * (uint32_t)s;
+                    for (int kb = 0; kb < KB; ++kb) {
+                        const uint32_t slot = (uint32_t)(s * KB + kb);
+                        const uint64_t bd = bd0 + (uint64_t)(b_step * slot);
+                        const uint32_t at = tmem + a_col0 + 32u * slot;
 #pragma unroll
-                    for (int ks = 0; ks < 4; ++ks)  // K = 16 per MMA: 8 TMEM columns of fp16 pairs
-                        tc_mma_f16_ts(tmem, at + 8u * (uint32_t)ks, bd + 2 * ks, idesc, (kc | ks) != 0);
+                        for (int ks = 0; ks < 4; ++ks)  // K = 16 per MMA: 8 TMEM columns of fp16 pairs
+                            tc_mma_f16_ts(tmem, at + 8u * (uint32_t)ks, bd + 2 * ks, idesc, (kc | kb | ks) != 0);
+                    }
                     tc_commit(&empty[s]);
                     if (++s == S) {
                         s = 0;
@@ -722,9 +739,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 // was issued.
                 tc_fence_after();
                 const int q = warp & 3, half = (warp - 2) >> 2;
-                uint32_t h[16];
-                dequant_rows_regs<FMT>(raw, q * 32 + lane, half, h);
-                tmem_st16_wait(tmem + ((uint32_t)(q * 32) << 16) + a_col0 + 32u * (uint32_t)s + 16u * (uint32_t)half, h);
+                for (int kb = 0; kb < KB; ++kb) {
+                    uint32_t h[16];
+                    dequant_rows_regs<FMT>(raw + kb * 8 * UB, q * 32 + lane, half, h);
+                    tmem_st16_wait(tmem + ((uint32_t)(q * 32) << 16) + a_col0 + 32u * (uint32_t)(s * KB + kb) +
+                                       16u * (uint32_t)half,
+                                   h);
+                }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&afull[s]);
