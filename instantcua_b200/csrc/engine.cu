@@ -140,6 +140,11 @@ struct icua_engine {
     __half* wscr[2][4] = {{nullptr, nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr, nullptr}};
     cudaStream_t side = nullptr;
     cudaEvent_t ev_ready[8] = {}, ev_done[8] = {};  // per GEMM of the sequence, mod 8
+    // batched step: row groups recorded as parallel chains (second group on `side`); 1 unless
+    // ICUA_BATCH_GROUPS=2 (measured within the run-to-run spread at config 4, and each group reads
+    // the weights once)
+    int batch_groups = 1;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     // sessions (contiguous arrays; Session holds pointers into them)
     DevState* st_all = nullptr;
     int* out_all = nullptr;
@@ -457,14 +462,17 @@ constexpr int SPLITK_MAX_ROWS = 128;  // split K only for batches of up to this 
 // as fp16 rows; with split K it runs inside the finish kernel.  parts_out (TC_STORE): the caller
 // consumes the partial products itself (e->splitk_part, [parts][m][n]); *parts_out = the K split,
 // 1 when the GEMM stored its result in p.out.
+// x: the first B row of the caller's row group, rows_alloc: B rows from x to the end of the
+// buffer; splitk: the group's split-K scratch ([parts][m][n], at most SPLITK_MAX x m_tok x n).
 template <int EPI>
-cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmParams p, cudaStream_t s,
-                       const float* norm_w = nullptr, __half* norm_out = nullptr, int* parts_out = nullptr) {
+cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, int rows_alloc, float* splitk, TcGemmParams p,
+                       cudaStream_t s, const float* norm_w = nullptr, __half* norm_out = nullptr,
+                       int* parts_out = nullptr) {
     // the batched step's activations are fp16 hi / lo row pairs (2 max_pass rows per buffer);
     // its SwiGLU output (the down GEMM's input) and the norms after the residual GEMMs are too
     p.hilo = 1;
     if (EPI == TC_SWIGLU) p.hilo_out = 1;
-    const int rows = 2 * e->cfg.max_pass;
+    const int rows = rows_alloc;
     const TcTile t = 2 * p.m_tok <= 128 ? TcTile{1, (2 * p.m_tok + 15) / 16 * 16}
                                         : choose_tc_tile(p.n_rows, 2 * p.m_tok, e->n_sm, true);
     const int tiles = (p.n_rows / (TC_BM * t.mh)) * ((2 * p.m_tok + t.bn - 1) / t.bn);
@@ -490,7 +498,7 @@ cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmPar
         return cudaSuccess;
     }
     TcGemmParams q = p;
-    q.out = e->splitk_part;
+    q.out = splitk;
     q.ldo = p.n_rows;
     q.out_zstride = (long long)p.m_tok * p.n_rows;
     if ((err = run(std::integral_constant<int, TC_STORE>{}, q, ks)) != cudaSuccess) return err;
@@ -499,12 +507,12 @@ cudaError_t batch_gemm(icua_engine* e, const Matrix& m, const void* x, TcGemmPar
         return cudaSuccess;
     }
     if (EPI == TC_RESID && norm_w && p.n_rows == H)
-        return launch(splitk_resid_norm_kernel, p.m_tok, 256, 0, s, true, (const float*)e->splitk_part, ks, p.m_tok,
-                      p.out, norm_w, norm_out, 1);
+        return launch(splitk_resid_norm_kernel, p.m_tok, 256, 0, s, true, (const float*)splitk, ks, p.m_tok, p.out,
+                      norm_w, norm_out, 1);
     const long long total = (long long)p.m_tok * p.n_rows;
     const int grid = (int)std::min<long long>((total + 255) / 256, 4LL * e->n_sm);
-    if ((err = launch(splitk_finish_kernel<EPI>, grid, 256, 0, s, true, (const float*)e->splitk_part, ks, p.m_tok,
-                      p.n_rows, p.out, p.out_h, p.hilo_out)) != cudaSuccess)
+    if ((err = launch(splitk_finish_kernel<EPI>, grid, 256, 0, s, true, (const float*)splitk, ks, p.m_tok, p.n_rows,
+                      p.out, p.out_h, p.hilo_out)) != cudaSuccess)
         return err;
     if (EPI == TC_RESID && norm_w)
         return launch(rmsnorm_rows_f16_kernel<true>, p.m_tok, 256, 0, s, true, (const float*)p.out, norm_w, p.m_tok,
@@ -1331,34 +1339,45 @@ cudaError_t record_prefill_rows(icua_engine* e, Session& S, int n_rows, int vis_
     return cudaSuccess;
 }
 
-// One batched decode step over rows [0, n_rows) (row r -> session eng->batch_rows[r]): embedding
-// of each session's current token, the layers through the tensor-core GEMMs with per-row
-// attention, the tied lm_head GEMM with per-row argmax partials, and the per-session commit.
+// One batched decode step over rows [r0, r0 + n_rows) (row r -> session eng->batch_rows[r]) on
+// stream st: embedding of each session's current token, the layers through the tensor-core GEMMs
+// with per-row attention, the tied lm_head GEMM with per-row argmax partials, and the per-session
+// commit.  Every row buffer (residual, GEMM inputs as hi / lo row pairs, projections, argmax
+// partials, logits) is addressed from the group's first row, so two groups of one step touch
+// disjoint memory except for the split-K scratch, which each group brings (splitk) and the error
+// flags (atomic OR).
 template <typename KVT>
-cudaError_t record_batch_step(icua_engine* e, int n_rows) {
+cudaError_t record_batch_rows(icua_engine* e, cudaStream_t st, int r0, int n_rows, float* splitk) {
     cudaError_t err;
-    cudaStream_t st = e->stream;
     const int L = e->cfg.n_layers;
-    if ((err = launch(batch_embed_kernel, n_rows, 256, 0, st, true, (const int*)e->batch_rows,
-                      (const DevState*)e->st_all, (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->embed.fmt, e->px)) != cudaSuccess)
+    const int P2 = 2 * e->cfg.max_pass - 2 * r0;  // hi / lo rows from the group's first one
+    const int* rows = e->batch_rows + r0;
+    float* px = e->px + (size_t)r0 * H;
+    float* pqkv = e->pqkv + (size_t)r0 * QKV_ROWS;
+    __half* pxn = e->pxn + (size_t)2 * r0 * H;
+    __half* pattn = e->pattn + (size_t)2 * r0 * H;
+    __half* ph = e->ph + (size_t)2 * r0 * FF;
+    if ((err = launch(batch_embed_kernel, n_rows, 256, 0, st, true, rows, (const DevState*)e->st_all,
+                      (const uint8_t*)e->embed.dev, e->embed.n_tiles, e->embed.fmt, px)) != cudaSuccess)
         return err;
     const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
     // the RMSNorm before each projection runs in the finish of the GEMM that updated the residual
     // (o-proj, down), so only layer 0's input norm is a launch of its own
-    if ((err = launch(rmsnorm_rows_f16_kernel<true>, n_rows, 256, 0, st, true, (const float*)e->px,
-                      (const float*)e->layers[0].attn_norm, n_rows, e->pxn)) != cudaSuccess)
+    if ((err = launch(rmsnorm_rows_f16_kernel<true>, n_rows, 256, 0, st, true, (const float*)px,
+                      (const float*)e->layers[0].attn_norm, n_rows, pxn)) != cudaSuccess)
         return err;
     for (int l = 0; l < L; ++l) {
         Layer& ly = e->layers[l];
         TcGemmParams p = tc_params(ly.qkv, n_rows, e->gemm_err);
-        p.out = e->pqkv;
+        p.out = pqkv;
         p.ldo = QKV_ROWS;
         int qkv_parts = 1;  // split K: the attention kernel adds the partial products itself
-        if ((err = batch_gemm<TC_STORE>(e, ly.qkv, e->pxn, p, st, nullptr, nullptr, &qkv_parts)) != cudaSuccess)
+        if ((err = batch_gemm<TC_STORE>(e, ly.qkv, pxn, P2, splitk, p, st, nullptr, nullptr, &qkv_parts)) !=
+            cudaSuccess)
             return err;
         {
             AttnParams<KVT> a{};
-            a.qkv = qkv_parts > 1 ? e->splitk_part : e->pqkv;
+            a.qkv = qkv_parts > 1 ? splitk : pqkv;
             a.qkv_stride = QKV_ROWS;
             a.qkv_parts = qkv_parts;
             a.qkv_part_stride = (long long)n_rows * QKV_ROWS;
@@ -1390,8 +1409,8 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
             a.cluster = cl;
             a.part = e->att_part;
             a.st = e->st_all;
-            a.rows_sess = e->batch_rows;
-            a.out16 = e->pattn;
+            a.rows_sess = rows;
+            a.out16 = pattn;
             a.out16_hilo = 1;
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(NKV * a.n_split, n_rows);
@@ -1410,37 +1429,75 @@ cudaError_t record_batch_step(icua_engine* e, int n_rows) {
             if ((err = cudaLaunchKernelEx(&cfg, attn_decode_kernel<KVT>, a)) != cudaSuccess) return err;
         }
         p = tc_params(ly.o, n_rows, e->gemm_err);
-        p.out = e->px;
+        p.out = px;
         p.ldo = H;
-        if ((err = batch_gemm<TC_RESID>(e, ly.o, e->pattn, p, st, ly.mlp_norm, e->pxn)) != cudaSuccess) return err;
+        if ((err = batch_gemm<TC_RESID>(e, ly.o, pattn, P2, splitk, p, st, ly.mlp_norm, pxn)) != cudaSuccess)
+            return err;
         p = tc_params(ly.gu, n_rows, e->gemm_err);
-        p.out_h = e->ph;
+        p.out_h = ph;
         p.ldh = FF;
-        if ((err = batch_gemm<TC_SWIGLU>(e, ly.gu, e->pxn, p, st)) != cudaSuccess) return err;
+        if ((err = batch_gemm<TC_SWIGLU>(e, ly.gu, pxn, P2, splitk, p, st)) != cudaSuccess) return err;
         p = tc_params(ly.d, n_rows, e->gemm_err);
-        p.out = e->px;
+        p.out = px;
         p.ldo = H;
         const float* next_norm = l + 1 < L ? e->layers[l + 1].attn_norm : e->final_norm;
-        if ((err = batch_gemm<TC_RESID>(e, ly.d, e->ph, p, st, next_norm, e->pxn)) != cudaSuccess) return err;
+        if ((err = batch_gemm<TC_RESID>(e, ly.d, ph, P2, splitk, p, st, next_norm, pxn)) != cudaSuccess) return err;
     }
+    const int n_vt = e->cfg.vocab / TC_BM;  // lm_head row tiles: argmax partials [n_vt][n_rows] per group
     TcGemmParams p = tc_params(e->embed, n_rows, e->gemm_err);
-    p.best_v = e->batch_best_v;
-    p.best_i = e->batch_best_i;
+    p.best_v = e->batch_best_v + (size_t)n_vt * r0;
+    p.best_i = e->batch_best_i + (size_t)n_vt * r0;
     // logits when requested; a one-row step of an f16 engine (its batch-1 decode) keeps them like
     // the GEMV head does
-    p.out = e->batch_logits ? e->batch_logits : (e->embed.fmt == FMT_F16 && n_rows == 1 ? e->logits : nullptr);
+    p.out = e->batch_logits ? e->batch_logits + (size_t)r0 * e->cfg.vocab
+                            : (e->embed.fmt == FMT_F16 && n_rows == 1 ? e->logits : nullptr);
     p.ldo = e->cfg.vocab;
     p.hilo = 1;  // the final norm's hi / lo rows
-    const int rows = 2 * e->cfg.max_pass;
-    err = e->embed.fmt == FMT_Q4A ? launch_tc_gemm<TC_ARGMAX, FMT_Q4A>(e->pxn, rows, p, st, nullptr, 1, true)
-        : e->embed.fmt == FMT_F16 ? launch_tc_gemm<TC_ARGMAX, FMT_F16>(e->pxn, rows, p, st,
+    err = e->embed.fmt == FMT_Q4A ? launch_tc_gemm<TC_ARGMAX, FMT_Q4A>(pxn, P2, p, st, nullptr, 1, true)
+        : e->embed.fmt == FMT_F16 ? launch_tc_gemm<TC_ARGMAX, FMT_F16>(pxn, P2, p, st,
                                                                        reinterpret_cast<const __half*>(e->embed.dev), 1,
                                                                        true)
-                                  : launch_tc_gemm<TC_ARGMAX, FMT_Q8>(e->pxn, rows, p, st, nullptr, 1, true);
+                                  : launch_tc_gemm<TC_ARGMAX, FMT_Q8>(pxn, P2, p, st, nullptr, 1, true);
     if (err != cudaSuccess) return err;
-    return launch(batch_commit_kernel, n_rows, 256, 0, st, true, (const float*)e->batch_best_v,
-                  (const int*)e->batch_best_i, e->cfg.vocab / TC_BM, n_rows, (const int*)e->batch_rows, e->st_all,
-                  e->out_all, e->out_stride, e->cfg.vocab);
+    return launch(batch_commit_kernel, n_rows, 256, 0, st, true, (const float*)p.best_v, (const int*)p.best_i, n_vt,
+                  n_rows, rows, e->st_all, e->out_all, e->out_stride, e->cfg.vocab);
+}
+
+// Row groups of a batched step.  With ICUA_BATCH_GROUPS=2, two groups (halves of the batch) are
+// recorded as two independent chains of the same graph, so that one group's GEMMs (tensor-bound,
+// a few dozen CTAs each) can run while the other group's attention streams its caches from HBM;
+// each group then reads the layer weights once.  Measured at config 4 (64 sessions, 2K context):
+// 4.24 ms per step against 4.28-4.29 ms for one group, inside the run-to-run spread, because the
+// attention needs every SM to reach its HBM rate.  One group below 32 rows (the weight reads
+// dominate) and above SPLITK_MAX_ROWS (each half must fit its half of the split-K scratch).
+int batch_groups(const icua_engine* e, int n_rows) {
+    if (e->batch_groups < 2 || n_rows < 32 || n_rows > SPLITK_MAX_ROWS) return 1;
+    return 2;
+}
+
+template <typename KVT>
+cudaError_t record_batch_steps(icua_engine* e, int n_rows, int steps) {
+    cudaError_t err = cudaSuccess;
+    if (batch_groups(e, n_rows) == 1) {
+        for (int i = 0; i < steps && err == cudaSuccess; ++i)
+            err = record_batch_rows<KVT>(e, e->stream, 0, n_rows, e->splitk_part);
+        return err;
+    }
+    // group 0 = rows [0, na) on the engine stream, group 1 = rows [na, n_rows) on the side stream,
+    // forked from and joined back into the capture; the second half of the split-K scratch
+    // (SPLITK_MAX x SPLITK_MAX_ROWS / 2 rows x GU_ROWS) belongs to group 1
+    const int na = (n_rows + 1) / 2;
+    float* split1 = e->splitk_part + (size_t)SPLITK_MAX * (SPLITK_MAX_ROWS / 2) * GU_ROWS;
+    if ((err = cudaEventRecord(e->ev_fork, e->stream)) != cudaSuccess) return err;
+    if ((err = cudaStreamWaitEvent(e->side, e->ev_fork, 0)) != cudaSuccess) return err;
+    for (int i = 0; i < steps && err == cudaSuccess; ++i) {
+        err = record_batch_rows<KVT>(e, e->stream, 0, na, e->splitk_part);
+        if (err == cudaSuccess) err = record_batch_rows<KVT>(e, e->side, na, n_rows - na, split1);
+    }
+    // join on every path, so that ending the capture also ends the side stream's part of it
+    const cudaError_t j1 = cudaEventRecord(e->ev_join, e->side);
+    const cudaError_t j2 = j1 == cudaSuccess ? cudaStreamWaitEvent(e->stream, e->ev_join, 0) : j1;
+    return err != cudaSuccess ? err : j2;
 }
 
 void drop_batch_graphs(icua_engine* e) {
@@ -1453,10 +1510,8 @@ void drop_batch_graphs(icua_engine* e) {
 icua_status build_batch_graph(icua_engine* eng, int n_rows, int steps, cudaGraphExec_t* out) {
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(eng->stream, cudaStreamCaptureModeThreadLocal));
-    cudaError_t err = cudaSuccess;
-    for (int i = 0; i < steps && err == cudaSuccess; ++i)
-        err = eng->cfg.kv_dtype == ICUA_KV_BF16 ? record_batch_step<__nv_bfloat16>(eng, n_rows)
-                                                : record_batch_step<__half>(eng, n_rows);
+    const cudaError_t err = eng->cfg.kv_dtype == ICUA_KV_BF16 ? record_batch_steps<__nv_bfloat16>(eng, n_rows, steps)
+                                                              : record_batch_steps<__half>(eng, n_rows, steps);
     cudaError_t e2 = cudaStreamEndCapture(eng->stream, &g);
     if (err != cudaSuccess) {
         if (g) cudaGraphDestroy(g);
@@ -1604,6 +1659,9 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
             cudaEventCreateWithFlags(&eng->ev_done[i], cudaEventDisableTiming);
         }
         cudaStreamCreateWithFlags(&eng->side, cudaStreamNonBlocking);
+        cudaEventCreateWithFlags(&eng->ev_fork, cudaEventDisableTiming);
+        cudaEventCreateWithFlags(&eng->ev_join, cudaEventDisableTiming);
+        if (const char* g = getenv("ICUA_BATCH_GROUPS")) eng->batch_groups = atoi(g) >= 2 ? 2 : 1;
         cudaMemsetAsync(eng->ph, 0, 2 * P * FF * sizeof(__half), eng->stream);
         cudaMemsetAsync(eng->pxn, 0, 2 * P * H * sizeof(__half), eng->stream);
         cudaMemsetAsync(eng->pattn, 0, 2 * P * H * sizeof(__half), eng->stream);
@@ -1664,6 +1722,8 @@ void icua_engine_destroy(icua_engine* eng) {
         if (eng->ev_ready[i]) cudaEventDestroy(eng->ev_ready[i]);
         if (eng->ev_done[i]) cudaEventDestroy(eng->ev_done[i]);
     }
+    if (eng->ev_fork) cudaEventDestroy(eng->ev_fork);
+    if (eng->ev_join) cudaEventDestroy(eng->ev_join);
     if (eng->side) {
         cudaStreamSynchronize(eng->side);
         cudaStreamDestroy(eng->side);

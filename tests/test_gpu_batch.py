@@ -150,3 +150,30 @@ def test_tile_order_copy_made_on_first_batched_decode(tensors):
     e.decode_batch([0], 2)  # a second call adds nothing
     assert e.device_bytes == before + added
     e.close()
+
+
+def test_two_row_groups_match_one(tensors, monkeypatch):
+    """With ICUA_BATCH_GROUPS=2 a batched step of 32 to 128 rows is recorded as two row groups,
+    parallel chains of its graph (one group's GEMMs can overlap the other's attention).  Each row's
+    arithmetic does not depend on the grouping: 40 sessions in a shuffled order, graphs of 4 steps
+    and single steps, give the same tokens and logits as one group (the default)."""
+    n, steps = 40, 9
+    rng = np.random.default_rng(8)
+    order = [int(v) for v in rng.permutation(n)]
+    toks = [int(t) for t in rng.integers(0, 1024, n)]
+    res = []
+    for groups in ("1", "2"):
+        monkeypatch.setenv("ICUA_BATCH_GROUPS", groups)
+        e = make_engine(tensors, "bf16", sessions=n)
+        for s in range(n):
+            e.inject_kv_random(int(20 + 3 * s), seed=50 + s, session=s)
+        cap = e.capture_batch_logits(n)
+        out = e.decode_batch(order, steps, in_tokens=toks)  # 2 graphs of 4 steps + 1 single step
+        res.append((out.copy(), cap.copy()))
+        assert [e.position(s) for s in range(n)] == [20 + 3 * s + steps for s in range(n)]
+        e.close()
+    (o1, c1), (o2, c2) = res
+    err = float(np.abs(c1 - c2).max())
+    print(f"two row groups vs one: max|d| {err:.3e}, tokens equal {np.array_equal(o1, o2)}")
+    assert np.array_equal(o1, o2)
+    assert err <= ATOL and min(cos_sim(a, b) for a, b in zip(c1, c2)) >= COS
