@@ -192,6 +192,7 @@ def run_ours(args):
     ctx_p = eng.position()
     lay_ms, head_ms = eng.profile_decode(PROFILE_STEPS)
     kps = eng.kernels_per_step
+    attn_o = eng.attn_o_cluster
     dev_bytes = eng.device_bytes
     roof = None
     if rank == 0:
@@ -218,7 +219,9 @@ def run_ours(args):
                        "seq_len": CTX, "context_range": [ctx0, ctx0 + K], "parallelism": f"replicas x{world}",
                        "l2": "inputs larger than L2 (1.59 GB streamed per step)"},
             "roofline": {"kernel": ("decode_mk_kernel: all 28 decoder layers of a token in one cooperative launch"
-                                    if kps == 3 else "decoder layers: 5 x 28 PDL-chained launches"),
+                                    if kps == 3 else
+                                    f"decoder layers: {(kps - 2) // NL} x {NL} PDL-chained launches"
+                                    + (f" (o-proj folded into the attention, clusters of {attn_o})" if attn_o else "")),
                          "bound": "hbm", "achieved": round(lay_ach, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(lay_ach / peak, 4),
                          "traffic": profile_traffic("decode_mk_layers_config2.md") if kps == 3 else None,

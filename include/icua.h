@@ -146,6 +146,13 @@ icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token
  * on the first icua_decode_batch.  0 for NULL. */
 uint64_t icua_device_bytes(const icua_engine* eng);
 
+/* CTAs per cluster of the decode attention kernel with the o-projection folded in (q4s engines:
+ * one cluster per kv head, 16 when eight clusters of 16 fit on the device at once, else 8), or 0
+ * when the engine launches the o-proj GEMV on its own (other formats, grammar-commit passes,
+ * ICUA_ATTN_O=0).  No counterpart in the reference (a query of this build's launch shape).  0 for
+ * NULL. */
+int32_t icua_attn_o_cluster(const icua_engine* eng);
+
 /* Kernels one decode step launches on this engine: 3 for q4s engines on the persistent layers
  * kernel (all layers in one cooperative launch, then the lm_head GEMV and the commit), else
  * 5 x n_layers + 2 (one launch per projection / attention, lm_head, commit).  0 for NULL. */

@@ -93,6 +93,7 @@ PROTOTYPES = {
     "icua_set_wait_limit": (_I, [C.c_uint32]),
     "icua_decode_kernels_per_step": (_I, [_P]),
     "icua_device_bytes": (C.c_uint64, [_P]),
+    "icua_attn_o_cluster": (_I, [_P]),
     "icua_profile_decode": (_I, [_P, _I, _I, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "icua_quantize_q8": (_I, [_FP, _I, _I, _P, _P]),
     "icua_quantize_q4s": (_I, [_FP, _I, _I, _P, _P]),

@@ -56,10 +56,15 @@ struct AttnParams {
     int qkv_parts;
     long long qkv_part_stride;
     int out16_hilo;  // out16 as fp16 hi / lo row pairs (the batched GEMMs' input)
+    // o-projection folded in (attn_decode_kernel<KVT, false, true>): the q4s o-proj matrix and the
+    // per-kv-head partial products [NKV][2048] the next kernels add to the residual
+    const uint8_t* wo;
+    float* o_part;
 };
 
-// NT: query tokens per pass the layout holds (2 in the grammar-commit kernels).
-template <typename KVT, int NT = 1>
+// NT: query tokens per pass the layout holds (2 in the grammar-commit kernels).  CLM: largest
+// cluster (16 for the kernel with the o-projection folded in, one cluster per kv head).
+template <typename KVT, int NT = 1, int CLM = 8>
 struct AttnSmem {
     static constexpr int row_bytes = HD * (int)sizeof(KVT);
     static constexpr int slot_bytes = 2 * ATT_SLOT * row_bytes;   // K rows then V rows
@@ -68,10 +73,17 @@ struct AttnSmem {
     static constexpr int new_off = 8 * ring_warp;                 // K rows, then V rows, of the new positions
     static constexpr int q_off = new_off + 2 * NT * row_bytes;    // float q[NT][2][128] (scaled)
     static constexpr int wpart_off = q_off + NT * 2 * HD * 4;     // float [8 warps][NT][ATT_PART]
-    static constexpr int cpart_off = wpart_off + 8 * NT * ATT_PART * 4;  // float [8 cluster ranks][NT][ATT_PART]
-    static constexpr int bars_off = cpart_off + 8 * NT * ATT_PART * 4;
-    static constexpr int total = bars_off + 8 * ATT_NS * 8;
+    static constexpr int cpart_off = wpart_off + 8 * NT * ATT_PART * 4;  // float [CLM cluster ranks][NT][ATT_PART]
+    static constexpr int bars_off = cpart_off + CLM * NT * ATT_PART * 4;
+    static constexpr int total = bars_off + 8 * ATT_NS * 8 + 8;  // + the o-proj tile barrier
 };
+
+// o-projection folded into the attention (one cluster of n_split = 8 or 16 CTAs per kv head):
+// CTA j of kv head h multiplies the head pair's output (256 columns of the o-proj input) by output
+// rows [R j, R j + R), R = 2048 / n_split: R / 16 tiles of 16 rows x 4 q4s units of 64 columns.
+// In the GEMV layout (16 K slices of 2 units) those units are slices 2h and 2h+1, and a slice's
+// R / 16 tiles are one contiguous run of R / 8 units.
+__host__ __device__ constexpr int att_o_run_bytes(int rows) { return (rows / 16) * 2 * icua_layout::Q4_UNIT_BYTES; }
 
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -229,10 +241,17 @@ __device__ __forceinline__ void attn_block(uint32_t kslot, uint32_t vslot, int r
 // (DevState::n_tok) at positions pos and pos + 1: both are normalised, rotated and appended, the
 // second token's queries take MMA columns 4..7 next to the first's, so every K/V byte is still read
 // once, and each token writes its own parts (token 1 after token 0's).
-template <typename KVT, bool DUAL = false>
+// FO: the o-projection is folded in (one token, q4s o-proj, one cluster of n_split = 8 or 16 CTAs
+// per kv head): the cluster leader's combined output of the head pair is read by every CTA of the
+// cluster through distributed shared memory, and each CTA writes the products of its 2048 / n_split
+// o-proj rows with it to o_part[h] (replaces the o-proj GEMV launch and its fold of the attention
+// parts; the next kernels add the eight partial vectors to the residual).
+template <typename KVT, bool DUAL = false, bool FO = false>
 __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KVT> p) {
+    static_assert(!(DUAL && FO), "the folded o-projection is a one-token kernel");
     extern __shared__ __align__(128) uint8_t smem[];
-    using S = AttnSmem<KVT, DUAL ? 2 : 1>;
+    using S = AttnSmem<KVT, DUAL ? 2 : 1, FO ? 16 : 8>;
+    constexpr int CLM = FO ? 16 : 8;
     constexpr int NTK = DUAL ? 2 : 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int NSP = p.n_split;
@@ -275,8 +294,10 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
         bulk_g2s(dst, kbase + (long long)r0 * HD, bytes, bar);
         bulk_g2s(dst + ATT_SLOT * S::row_bytes, vbase + (long long)r0 * HD, bytes, bar);
     };
+    uint64_t* wbar = reinterpret_cast<uint64_t*>(smem + S::bars_off) + 8 * ATT_NS;  // o-proj tiles (FO)
     if (lane == 0) {
         for (int s = 0; s < ATT_NS; ++s) mbar_init(&bars[s], 1);
+        if (FO && warp == 0) mbar_init(wbar, 1);
         fence_mbar_init();
         for (int c = 0; c < min(ATT_NS, n_chunks); ++c) issue(c);
     }
@@ -430,6 +451,18 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
         }
     }
     __syncthreads();
+    const int o_rows = H / NSP;                  // FO: o-proj rows of this CTA (128 or 256)
+    const int o_run = att_o_run_bytes(o_rows);   // FO: bytes of one slice's run of them
+    if (FO && tid == 0) {
+        // every warp is done with its ring (all chunk copies waited for): the CTA's o-proj tiles go
+        // to the start of the ring while the splits are combined
+        fence_proxy_async_smem();
+        mbar_expect_tx(wbar, 2 * o_run);
+        const long long run0 = ((long long)(2 * h) * (H / 16) + (o_rows / 16) * j) * 2 * icua_layout::Q4_UNIT_BYTES;
+        const long long run1 = ((long long)(2 * h + 1) * (H / 16) + (o_rows / 16) * j) * 2 * icua_layout::Q4_UNIT_BYTES;
+        bulk_g2s(smem + S::ring_off, p.wo + run0, o_run, wbar);
+        bulk_g2s(smem + S::ring_off + o_run, p.wo + run1, o_run, wbar);
+    }
     // CTA combine of the 8 warps: thread (hh, d), per token
     const int hh = tid >> 7, d = tid & 127;
     float Mt[NTK], Lt[NTK], Ot[NTK];
@@ -467,18 +500,19 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
     // one cluster barrier: the pushes (release) are visible to the leader (acquire); the other
     // CTAs are done, since nobody reads their shared memory
     cluster_sync_all();
-    if (cluster_ctarank() != 0) return;
+    const bool leader = cluster_ctarank() == 0;
+    if (!FO && !leader) return;
     const int CL = p.cluster;
 #pragma unroll
     for (int tq = 0; tq < NTK; ++tq) {
-        if (tq >= ntok) continue;
+        if (tq >= ntok || !leader) continue;
         float M = -INFINITY;
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
+        for (int q = 0; q < CLM; ++q)
             if (q < CL) M = fmaxf(M, cpart[(q * NTK + tq) * ATT_PART + hh]);
         float Lsum = 0.f, O = 0.f;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < CLM; ++q) {
             if (q < CL) {
                 const float* cq = cpart + (q * NTK + tq) * ATT_PART;
                 const float mq = cq[hh];
@@ -487,7 +521,9 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
                 O = fmaf(cq[4 + hh * HD + d], f, O);
             }
         }
-        if (p.out16 != nullptr) {
+        if (FO) {
+            qs[tid] = O / Lsum;  // the head pair's output, element hh * 128 + d (q is in registers now)
+        } else if (p.out16 != nullptr) {
             const float y = O / Lsum;
             const size_t col = (size_t)(2 * h + hh) * HD + d;
             if (p.out16_hilo) {  // fp16 hi / lo rows 2 row, 2 row + 1
@@ -506,6 +542,65 @@ __global__ void __launch_bounds__(256, 2) attn_decode_kernel(const AttnParams<KV
                 out[2 + hh] = Lsum;
             }
         }
+    }
+    if constexpr (FO) {
+        // every CTA reads the leader's output of the head pair, multiplies it by its 128 o-proj rows
+        cluster_sync_all();  // the leader's qs is written (release / acquire)
+        const float y = ld_dsmem(&qs[tid], 0);
+        float* xv = wpart;  // the warp parts are consumed: [256] inputs, then fragments and group sums
+        uint2* xfrag = reinterpret_cast<uint2*>(wpart + 256);
+        float* xsum = wpart + 256 + 64 * 4;
+        xv[tid] = y;
+        cluster_arrive_relaxed();  // the leader may leave once every CTA has read its output
+        __syncthreads();
+        if (tid < 64) {  // pair q = tid: elements k0, k0 + 1, k0 + 8, k0 + 9 (the GEMV fragment order)
+            const int q = tid, k0 = (q >> 2) * 16 + 2 * (q & 3);
+            const int kk[4] = {k0, k0 + 1, k0 + 8, k0 + 9};
+            __half hi[4], lo[4];
+            float gsum = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float x = xv[kk[i]];
+                hi[i] = __float2half_rn(x);
+                lo[i] = __float2half_rn(x - __half2float(hi[i]));
+                gsum += __half2float(hi[i]) + __half2float(lo[i]);
+            }
+            uint2 h2, l2;
+            h2.x = (uint32_t)__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[1]) << 16);
+            h2.y = (uint32_t)__half_as_ushort(hi[2]) | ((uint32_t)__half_as_ushort(hi[3]) << 16);
+            l2.x = (uint32_t)__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[1]) << 16);
+            l2.y = (uint32_t)__half_as_ushort(lo[2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16);
+            xfrag[q * 2 + 0] = h2;
+            xfrag[q * 2 + 1] = l2;
+            gsum += __shfl_xor_sync(0xffffffffu, gsum, 1);
+            gsum += __shfl_xor_sync(0xffffffffu, gsum, 2);
+            gsum += __shfl_xor_sync(0xffffffffu, gsum, 4);
+            if ((q & 7) == 0) xsum[q >> 3] = gsum;
+        }
+        __syncthreads();
+        if (!mbar_wait_bounded(wbar, 0)) {
+            if (lane == 0) atomicOr(&st->error, ERR_WAIT_ATTN);
+            mbar_wait_bounded(wbar, 0);  // the copy lands before this CTA reads or leaves
+        }
+        // warp w: tiles w, w + 8 of the CTA's o_rows / 16 (rows o_rows j + 16 tile ..), the 4 units
+        // of the head pair
+        UnitConst<FMT_Q4S> uc[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) load_unit_const<FMT_Q4S>(uc[u], u, xfrag, xsum, lane);
+        for (int tile = warp; tile < o_rows / 16; tile += 8) {
+            float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint8_t* ub = smem + S::ring_off + (u >> 1) * o_run + (tile * 2 + (u & 1)) * icua_layout::Q4_UNIT_BYTES;
+                gemv_unit<FMT_Q4S>(ub, uc[u], lane, acc0, acc1);
+            }
+            if ((lane & 3) == 0) {
+                const int g = lane >> 2, r = o_rows * j + 16 * tile + g;
+                p.o_part[h * H + r] = acc0 * 16777216.0f;  // rows g in units of 2^-24, rows g + 8 of 2^-20
+                p.o_part[h * H + r + 8] = acc1 * 1048576.0f;
+            }
+        }
+        cluster_wait();
     }
 }
 

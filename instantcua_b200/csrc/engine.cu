@@ -97,6 +97,11 @@ struct icua_engine {
     int n_sm = 0;
     int att_split = 16;   // CTAs per kv head in the decode attention
     int att_cluster = 8;  // CTAs per cluster (att_split / att_cluster parts per kv head)
+    // batch-1 decode with the o-projection folded into the attention: one cluster of attn_o CTAs per
+    // kv head (16 when eight non-portable clusters of 16 fit at once, else 8; 0 = off, the o-proj
+    // GEMV launch); ICUA_ATTN_O=0 turns it off
+    int attn_o = 0;
+    float* o_part = nullptr;  // [NKV][2048] o-proj partial products of the head pairs
     cudaStream_t stream = nullptr;
     std::string err;
     bool failed = false;
@@ -588,6 +593,8 @@ cudaError_t set_smem_attrs() {
     SETA((gemv_kernel<FMT_Q4A, EPI_LOGITS, 2048, false, IN_F32, true>));
     SETA((attn_decode_kernel<__half, true>));
     SETA((attn_decode_kernel<__nv_bfloat16, true>));
+    SETA((attn_decode_kernel<__half, false, true>));
+    SETA((attn_decode_kernel<__nv_bfloat16, false, true>));
     SETA(commit_kernel);
     SETA(advance_kernel);
     SETA(decode_mk_kernel<__half>);
@@ -714,6 +721,29 @@ cudaError_t launch_mk(icua_engine* e, Session& S) {
     return cudaLaunchKernelEx(&cfg, decode_mk_kernel<KVT>, p);
 }
 
+// One layer's attention with the o-projection folded in (attn_decode_kernel<KVT, false, true>):
+// NKV clusters of e->attn_o CTAs, the head pairs' o-proj partial products into e->o_part.
+template <typename KVT>
+cudaError_t launch_attn_o(icua_engine* e, Session& S, const Layer& ly, int l, const L2Plan& l2) {
+    const size_t kv_layer = (size_t)NKV * e->cfg.max_context * HD;
+    AttnParams<KVT> a{};
+    a.qkv = e->qkv;
+    a.q_norm = ly.q_norm;
+    a.k_norm = ly.k_norm;
+    a.rope = S.rope;
+    a.kc = reinterpret_cast<KVT*>(S.kc) + kv_layer * l;
+    a.vc = reinterpret_cast<KVT*>(S.vc) + kv_layer * l;
+    a.max_ctx = e->cfg.max_context;
+    a.n_split = e->attn_o;
+    a.cluster = e->attn_o;
+    a.st = S.st;
+    a.l2 = l2;
+    a.wo = ly.o.dev;
+    a.o_part = e->o_part;
+    return launch_cluster(attn_decode_kernel<KVT, false, true>, NKV * e->attn_o, e->attn_o, 256,
+                          AttnSmem<KVT, 1, 16>::total, e->stream, a);
+}
+
 template <bool DUAL>
 cudaError_t record_layers_t(icua_engine* e, Session& S) {
     cudaError_t err;
@@ -722,6 +752,48 @@ cudaError_t record_layers_t(icua_engine* e, Session& S) {
         return e->cfg.kv_dtype == ICUA_KV_BF16 ? launch_mk<__nv_bfloat16>(e, S) : launch_mk<__half>(e, S);
     for (int l = 0; l < L; ++l) {
         Layer& ly = e->layers[l];
+        if (!DUAL && e->attn_o && ly.o.fmt == FMT_Q4S) {
+            // QKV -> attention + o-proj -> gate/up -> down; L2 prefetch: QKV(l) the o-proj and gate/up
+            // matrices, attention(l) the down matrix, gate/up(l) QKV(l+1), down(l) the next cache rows
+            GemvParams p = base_params(e, ly.qkv);
+            p.in_mode = (l == 0) ? IN_EMBED : IN_F32;
+            p.x = e->x;
+            p.norm_w = ly.attn_norm;
+            p.prompt = S.prompt;
+            p.pooler = e->pooler;
+            p.x_resid = e->x;
+            p.out = e->qkv;
+            p.st = S.st;
+            p.l2 = plan_weights(ly.o);
+            p.l2.ptr[1] = ly.gu.dev;
+            p.l2.bytes[1] = icua_packed_bytes(ly.gu.fmt, ly.gu.n_rows, ly.gu.k);
+            p.l2.n = 2;
+            err = (l == 0) ? launch_layer_gemv<EPI_STORE, 2048, IN_EMBED>(e, ly.qkv, p, e->stream)
+                           : launch_layer_gemv<EPI_STORE, 2048, IN_F32>(e, ly.qkv, p, e->stream);
+            if (err != cudaSuccess) return err;
+            err = e->cfg.kv_dtype == ICUA_KV_BF16 ? launch_attn_o<__nv_bfloat16>(e, S, ly, l, plan_weights(ly.d))
+                                                  : launch_attn_o<__half>(e, S, ly, l, plan_weights(ly.d));
+            if (err != cudaSuccess) return err;
+            p = base_params(e, ly.gu);
+            p.in_mode = IN_F32;
+            p.x = e->x;
+            p.in_add = e->o_part;
+            p.norm_w = ly.mlp_norm;
+            p.out = e->h;
+            p.st = S.st;
+            if (l + 1 < L) p.l2 = plan_weights(e->layers[l + 1].qkv);
+            if ((err = launch_layer_gemv<EPI_SWIGLU, 2048, IN_F32>(e, ly.gu, p, e->stream)) != cudaSuccess) return err;
+            p = base_params(e, ly.d);
+            p.in_mode = IN_F32;
+            p.x = e->h;
+            p.x_resid = e->x;
+            p.resid_add = e->o_part;
+            p.deepstack = (l < 3) ? e->deepstack[l] : nullptr;
+            p.st = S.st;
+            p.l2 = (l + 1 < L) ? plan_kv(e, S, l + 1) : plan_weights(e->embed);
+            if ((err = launch_layer_gemv<EPI_RESID, 6144, IN_F32>(e, ly.d, p, e->stream)) != cudaSuccess) return err;
+            continue;
+        }
         // 1. RMSNorm + QKV projection (layer 0 embeds the input row first)
         GemvParams p = base_params(e, ly.qkv);
         p.in_mode = (l == 0) ? IN_EMBED : IN_F32;
@@ -1507,6 +1579,40 @@ void drop_batch_graphs(icua_engine* e) {
     e->batch_key.clear();
 }
 
+// The folded o-projection's launch shape (NKV clusters of cl CTAs) is usable when clusters of cl
+// are allowed for the kernel and all NKV of them can be resident at once.
+template <typename KVT>
+bool attn_o_fits_t(int cl) {
+    auto k = attn_decode_kernel<KVT, false, true>;
+    if ((cl > 8 && cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) ||
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem<KVT, 1, 16>::total) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(NKV * cl);
+    lc.blockDim = dim3(256);
+    lc.dynamicSmemBytes = AttnSmem<KVT, 1, 16>::total;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cl;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    int n_clusters = 0;
+    const bool ok = cudaOccupancyMaxActiveClusters(&n_clusters, k, &lc) == cudaSuccess && n_clusters >= NKV;
+    cudaGetLastError();
+    return ok;
+}
+
+// Cluster size of the folded o-projection: 16, else 8, else 0 (not usable).
+int attn_o_cluster() {
+    for (int cl : {16, 8})
+        if (attn_o_fits_t<__half>(cl) && attn_o_fits_t<__nv_bfloat16>(cl)) return cl;
+    return 0;
+}
+
 icua_status build_batch_graph(icua_engine* eng, int n_rows, int steps, cudaGraphExec_t* out) {
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(eng->stream, cudaStreamCaptureModeThreadLocal));
@@ -1597,6 +1703,10 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
     }
     // the o-proj GEMV folds at most ATT_MAX_PARTS parts per kv head
     if (eng->att_split / eng->att_cluster > ATT_MAX_PARTS) eng->att_split = eng->att_cluster * ATT_MAX_PARTS;
+    {
+        const char* env = getenv("ICUA_ATTN_O");
+        if (cfg->format == ICUA_FMT_Q4S && !(env && atoi(env) == 0)) eng->attn_o = attn_o_cluster();
+    }
     for (int i = 0; i < 64; ++i) {
         const float a = (float)(2 * i) / 128.0f;
         eng->inv_freq[i] = 1.0f / powf(5000000.0f, a);
@@ -1632,6 +1742,7 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
     TRY(dalloc_t(eng, &eng->pooler, (size_t)cfg->max_pass * H));
     for (int i = 0; i < 3; ++i) TRY(dalloc_t(eng, &eng->deepstack[i], (size_t)cfg->max_pass * H));
     TRY(dalloc_t(eng, &eng->att_part, (size_t)2 * NKV * eng->att_split * ATT_PART));
+    TRY(dalloc_t(eng, &eng->o_part, (size_t)NKV * H));
     TRY(dalloc_t(eng, &eng->cta_best_v, (size_t)eng->n_sm));
     TRY(dalloc_t(eng, &eng->cta_best_i, (size_t)eng->n_sm));
     {
@@ -2272,9 +2383,12 @@ icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token
 
 uint64_t icua_device_bytes(const icua_engine* eng) { return eng ? eng->device_bytes : 0; }
 
+int32_t icua_attn_o_cluster(const icua_engine* eng) { return eng ? eng->attn_o : 0; }
+
 int32_t icua_decode_kernels_per_step(const icua_engine* eng) {
     if (!eng) return 0;
     if (eng->mk && !eng->grammar) return 3;  // persistent layers kernel, lm_head GEMV, commit
+    if (eng->attn_o && !eng->grammar) return 4 * eng->cfg.n_layers + 2;  // o-proj folded into the attention
     return 5 * eng->cfg.n_layers + 2;
 }
 

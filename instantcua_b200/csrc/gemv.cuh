@@ -62,6 +62,11 @@ struct GemvParams {
     const float* att_part;   // IN_ATTN: [NKV][att_parts][ATT_PART]
     int att_parts;
     float* x_resid;          // residual stream; written by CTA 0 in IN_EMBED, updated by EPI_RESID
+    // o-projection partial products [NKV][2048] of an attention kernel with the o-proj folded in, or
+    // nullptr, added in head order: in_add to the IN_F32 input (k = 2048), resid_add to the
+    // residual rows EPI_RESID updates
+    const float* in_add;
+    const float* resid_add;
     // epilogue
     float* out;              // EPI_STORE: y [n_rows]; EPI_SWIGLU: h [n_rows / 2]
     const float* deepstack;  // EPI_RESID: [n_vis, 2048] for this layer, or nullptr
@@ -184,6 +189,21 @@ __device__ __forceinline__ void load_input(InputRegs<KMAX, NT>& r, const GemvPar
             r.v[j][1] = a.y;
             r.v[j][2] = b.x;
             r.v[j][3] = b.y;
+            if (p.in_add != nullptr) {  // x + o_part[0] + ... + o_part[7]: every load first, then the sums
+                float2 pa[NKV], pb[NKV];
+#pragma unroll
+                for (int hq = 0; hq < NKV; ++hq) {
+                    pa[hq] = *reinterpret_cast<const float2*>(p.in_add + hq * H + k0);
+                    pb[hq] = *reinterpret_cast<const float2*>(p.in_add + hq * H + k0 + 8);
+                }
+#pragma unroll
+                for (int hq = 0; hq < NKV; ++hq) {
+                    r.v[j][0] += pa[hq].x;
+                    r.v[j][1] += pa[hq].y;
+                    r.v[j][2] += pb[hq].x;
+                    r.v[j][3] += pb[hq].y;
+                }
+            }
         } else if (IN == IN_BF16) {
             const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(p.x);
             r.v[j][0] = __bfloat162float(x[k0]);
@@ -468,7 +488,19 @@ __global__ void __maxnreg__(64) gemv_kernel(const GemvParams p) {
     InputRegs<KMAX, NT> in;
     // the residual rows this thread finalises (non-streaming path: thread i -> row i of the CTA)
     float xold = 0.f;
-    if (!STREAM && EPI == EPI_RESID && (int)threadIdx.x < nt * 16) xold = p.x_resid[t_begin * 16 + threadIdx.x];
+    if (!STREAM && EPI == EPI_RESID && (int)threadIdx.x < nt * 16) {
+        const int r = t_begin * 16 + threadIdx.x;
+        xold = p.x_resid[r];
+        // the o-proj partial products were written two launches ago (the attention kernel), so they
+        // are complete and visible once this kernel runs; summed in the order the IN_F32 load uses
+        if (p.resid_add != nullptr) {
+            float pr[NKV];
+#pragma unroll
+            for (int hq = 0; hq < NKV; ++hq) pr[hq] = p.resid_add[hq * H + r];
+#pragma unroll
+            for (int hq = 0; hq < NKV; ++hq) xold += pr[hq];
+        }
+    }
     __syncwarp();
 
     // the lm_head of a 2-token pass reads its last row; n_tok was set by the previous step's commit

@@ -275,6 +275,12 @@ class Engine:
         return int(self._lib.icua_decode_kernels_per_step(self._h))
 
     @property
+    def attn_o_cluster(self) -> int:
+        """CTAs per cluster of the decode attention with the o-projection folded in (0: separate
+        o-proj GEMV launch)."""
+        return int(self._lib.icua_attn_o_cluster(self._h))
+
+    @property
     def device_bytes(self) -> int:
         """Bytes of device memory the engine holds (its own allocations)."""
         return int(self._lib.icua_device_bytes(self._h))

@@ -179,3 +179,30 @@ def test_prefix_cache_reuses_system_prompt(require_gpu, golden, tensors):
     e.generate_vision(other, max_new_tokens=2, **args)
     assert e.last_timing.prefill_tokens == len(toks)
     e.close()
+
+
+@pytest.mark.parametrize("kv", ["f16", "bf16"])
+def test_folded_oproj_matches_launch_chain(require_gpu, golden, tensors, kv, monkeypatch):
+    """q4s engines fold the o-projection into the decode attention (one cluster of 8 or 16 CTAs per
+    kv head, 4 launches per layer instead of 5).  On the B200 it must be active; its tokens and
+    logits match the five-launch chain (ICUA_ATTN_O=0) and the oracle."""
+    steps = len(golden[f"text_{kv}_gen"])
+    runs = {}
+    for fold in ("1", "0"):
+        monkeypatch.setenv("ICUA_ATTN_O", fold)
+        e = make_engine(tensors, kv=kv)
+        want_k = 4 * 2 + 2 if fold == "1" else 5 * 2 + 2
+        assert e.kernels_per_step == want_k, (fold, e.kernels_per_step, e.attn_o_cluster)
+        assert (e.attn_o_cluster in (8, 16)) if fold == "1" else e.attn_o_cluster == 0
+        print(f"{kv}: ICUA_ATTN_O={fold}, cluster {e.attn_o_cluster}")
+        cap = e.capture_step_logits(steps)
+        first = e.prefill(golden["text_tokens"], write_logits=True)
+        first_logits = cap[0].copy()
+        toks = [first] + e.decode(steps - 1)
+        runs[fold] = (toks, np.concatenate([first_logits[None], cap[: steps - 1]]))
+        e.close()
+    assert runs["1"][0] == runs["0"][0] == golden[f"text_{kv}_gen"].tolist()
+    check_logits(runs["1"][1], golden[f"text_{kv}_logits"], kv + " folded o-proj")
+    err = float(np.abs(runs["1"][1] - runs["0"][1]).max())
+    print(f"{kv}: folded o-proj vs launch chain max|d| {err:.2e}")
+    assert err <= 1e-3
