@@ -102,6 +102,7 @@ struct icua_engine {
     // GEMV launch); ICUA_ATTN_O=0 turns it off
     int attn_o = 0;
     float* o_part = nullptr;  // [NKV][2048] o-proj partial products of the head pairs
+    int* host_tok = nullptr;  // pinned host word: the token icua_decode_step returns
     cudaStream_t stream = nullptr;
     std::string err;
     bool failed = false;
@@ -1743,6 +1744,8 @@ icua_status icua_engine_create(const icua_config* cfg, icua_engine** out) {
     for (int i = 0; i < 3; ++i) TRY(dalloc_t(eng, &eng->deepstack[i], (size_t)cfg->max_pass * H));
     TRY(dalloc_t(eng, &eng->att_part, (size_t)2 * NKV * eng->att_split * ATT_PART));
     TRY(dalloc_t(eng, &eng->o_part, (size_t)NKV * H));
+    if (cudaMallocHost(reinterpret_cast<void**>(&eng->host_tok), sizeof(int)) != cudaSuccess)
+        TRY(fail(eng, ICUA_ERR_CUDA, "cudaMallocHost failed"));
     TRY(dalloc_t(eng, &eng->cta_best_v, (size_t)eng->n_sm));
     TRY(dalloc_t(eng, &eng->cta_best_i, (size_t)eng->n_sm));
     {
@@ -1833,6 +1836,7 @@ void icua_engine_destroy(icua_engine* eng) {
         if (eng->ev_ready[i]) cudaEventDestroy(eng->ev_ready[i]);
         if (eng->ev_done[i]) cudaEventDestroy(eng->ev_done[i]);
     }
+    if (eng->host_tok) cudaFreeHost(eng->host_tok);
     if (eng->ev_fork) cudaEventDestroy(eng->ev_fork);
     if (eng->ev_join) cudaEventDestroy(eng->ev_join);
     if (eng->side) {
@@ -2359,23 +2363,13 @@ icua_status icua_decode_step(icua_engine* eng, int32_t session, int32_t in_token
     CK(cudaSetDevice(eng->cfg.device));
     if ((s = ensure_graphs(eng, *S)) != ICUA_OK) return s;
     if (S->step >= eng->cfg.max_steps) S->step = 0;  // wrap the output slot for long host-driven loops
-    // one small state write (H2D) per step: input token, step budget, no prompt rows left
-    struct {
-        int step, done, max_steps;
-    } head = {S->step, 0, S->step + 1};
-    CK(cudaMemcpyAsync(&S->st->step, &head, sizeof head, cudaMemcpyHostToDevice, eng->stream));
-    CK(cudaMemcpyAsync(&S->st->cur_token, &in_token, 4, cudaMemcpyHostToDevice, eng->stream));
-    const int big = 1 << 30, one = 1;
-    CK(cudaMemcpyAsync(&S->st->prompt_idx, &big, 4, cudaMemcpyHostToDevice, eng->stream));
-    CK(cudaMemcpyAsync(&S->st->write_logits, &one, 4, cudaMemcpyHostToDevice, eng->stream));
-    if (eng->grammar) {
-        // caller-driven steps carry one token and never force one
-        static const int one_tok[3] = {1, 0, 0};  // n_tok, cur_token2, grammar
-        CK(cudaMemcpyAsync(&S->st->n_tok, one_tok, sizeof one_tok, cudaMemcpyHostToDevice, eng->stream));
-    }
+    // the step's loop state (input token, step budget, no prompt rows left) in one small launch,
+    // the generated token back through the engine's pinned word
+    CK(launch(step_head_kernel, 1, 32, 0, eng->stream, false, S->st, S->step, in_token, eng->grammar ? 1 : 0));
     CK(cudaGraphLaunch(S->g_step1, eng->stream));
-    CK(cudaMemcpyAsync(out_token, S->out_tokens + S->step, 4, cudaMemcpyDeviceToHost, eng->stream));
+    CK(cudaMemcpyAsync(eng->host_tok, S->out_tokens + S->step, 4, cudaMemcpyDeviceToHost, eng->stream));
     CK(cudaStreamSynchronize(eng->stream));
+    *out_token = *eng->host_tok;
     S->step += 1;
     S->pos += 1;
     return ICUA_OK;

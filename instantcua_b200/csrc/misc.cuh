@@ -17,6 +17,25 @@ __global__ void advance_kernel(DevState* st) {
     }
 }
 
+// Loop state of one host-driven decode step (icua_decode_step), written by one launch whose
+// arguments carry the host values instead of one host-to-device copy per field: the input token,
+// the step's output slot and a budget of one token, no prompt rows left, logits kept; passes of
+// grammar-commit engines carry one token and force none.
+__global__ void step_head_kernel(DevState* st, int step, int cur_token, int grammar) {
+    if (threadIdx.x != 0) return;
+    st->step = step;
+    st->done = 0;
+    st->max_steps = step + 1;
+    st->cur_token = cur_token;
+    st->prompt_idx = 1 << 30;
+    st->write_logits = 1;
+    if (grammar) {
+        st->n_tok = 1;
+        st->cur_token2 = 0;
+        st->grammar = 0;
+    }
+}
+
 template <int FMT>
 __global__ void dequant_kernel(const uint8_t* tiles, int n_rows, int K, float* out) {
     const long long total = (long long)n_rows * K;

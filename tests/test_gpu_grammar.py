@@ -96,11 +96,14 @@ def forced_indices(rule, toks):
 @pytest.mark.parametrize("kv", ["f16", "bf16"])
 def test_grammar_rule_never_firing_is_bit_identical(tiny, kv, monkeypatch):
     """Two-token kernels with one-token passes == the single-token launch-chain kernels they are
-    built from, bit for bit (grammar engines always decode by the launch chain)."""
+    built from, bit for bit (grammar engines always decode by the five-launch chain, so the
+    single-token engine runs it too: no persistent kernel, no o-projection folded into the
+    attention)."""
     tensors, _ = tiny
     prompt = np.random.default_rng(11).integers(0, 1024, 40).astype(np.int32)
     n = 16
     monkeypatch.delenv("ICUA_DECODE", raising=False)
+    monkeypatch.setenv("ICUA_ATTN_O", "0")
     base, lb = engine_run(tensors, kv, prompt, n, None)
     unused = [t for t in range(1024) if t not in base][:4]
     rule = {"actions": (unused[0],), "comma": unused[1], "space": 220, "open": 7, "close": unused[2]}
